@@ -1,0 +1,415 @@
+#!/usr/bin/env python
+"""Benchmark of the unoq-dsp INT8 CNN execution path on B200.
+
+Headline (BASELINE.json metric, config 4): MobileNetV4-Conv-Small-224 INT8 images/sec over a
+global batch (default 4096) batch-sharded across N GPUs, one process per GPU, each GPU
+replaying one CUDA graph of the whole network; YOLO26n-320 (global batch 1024) is reported in
+the same line under "yolo26n_320". Weights are the bundled .uqmodel plans (staged into models/
+by __graft_entry__.build()); inputs are seeded uniform int8 images (synthetic, no dataset).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+value  -- images/sec with inputs already in HBM: W untimed steps, then exactly K steps between
+          a barrier + device sync on both sides, CUDA-event timed, max over ranks.
+e2e    -- the same images/sec through the public batch call ug_infer_batch with pinned host
+          buffers: per step the input H2D copy, the graph and the output D2H copy.
+--impl reference -- the reference's own C runtime (oracle/_ref/libug_ref.so, built from the
+          reference sources) on all host cores; rank 0 only.
+"""
+import argparse
+import ctypes as C
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT / "unoq-dsp_b200"), str(ROOT)]
+
+METRIC = "INT8 images/sec (MobileNetV4-S 224, YOLO26n 320) at 1/2/4/8 B200; % INT8/HBM roofline"
+MODELS = {
+    "mobilenetv4-small": {"shape": (1, 224, 224, 3), "batch": 4096, "key": "mobilenetv4_small_224"},
+    "yolo26n-320": {"shape": (1, 320, 320, 3), "batch": 1024, "key": "yolo26n_320"},
+}
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+# --------------------------------------------------------------------------- reference CPU
+def _ref_worker(args):
+    plan_path, shape, images, seed = args
+    sys.path[:0] = [str(ROOT), str(ROOT / "unoq-dsp_b200")]
+    from oracle.oracle import Reference
+    from unoq_dsp.bundle import load
+    plan = load(plan_path).plan
+    ref = Reference()
+    if ref.load(plan):
+        raise RuntimeError("reference ug_load failed")
+    x = np.random.default_rng(seed).integers(-128, 128, size=shape, dtype=np.int64).astype(np.int8)
+    t0 = time.perf_counter()
+    for _ in range(images):
+        ref.run(plan, x)
+    return time.perf_counter() - t0
+
+
+def reference_throughput(plan_path, shape, images_per_proc, procs, pool=None):
+    """Images/sec of the reference runtime: `procs` independent processes, each running
+    `images_per_proc` whole images (the reference runtime is single-threaded off Hexagon)."""
+    jobs = [(str(plan_path), shape, images_per_proc, 1000 + i) for i in range(procs)]
+    t0 = time.perf_counter()
+    times = pool.map(_ref_worker, jobs)
+    wall = time.perf_counter() - t0
+    return procs * images_per_proc / wall, wall, max(times)
+
+
+def make_pool(procs):
+    import multiprocessing as mp
+    return mp.get_context("spawn").Pool(procs)
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.device)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        reasons = set()
+        for r in self.rows:
+            for name, val in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), r[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.rows)}
+
+
+# --------------------------------------------------------------------------- distributed
+class Dist:
+    def __init__(self, gpus):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+            self.dist = dist
+            self.pg = True
+
+    def barrier(self):
+        if self.pg:
+            self.dist.barrier()
+
+    def max(self, value):
+        if not self.pg:
+            return value
+        import torch
+        t = torch.tensor([float(value)], dtype=torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, value):
+        if not self.pg:
+            return value
+        import torch
+        t = torch.tensor([float(value)], dtype=torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.dist.destroy_process_group()
+
+
+# --------------------------------------------------------------------------- roofline
+def op_traffic(plan, images):
+    """Algorithmic bytes and int8 ops per plan op for `images` images: every activation input
+    read once, the output written once, constants (weights, tables) read once per launch."""
+    import struct
+    magic, version, nt, no, arena, inp, out, flags = struct.unpack_from("<8I", plan)
+    ts = [struct.unpack_from("<12I", plan, 32 + 48 * i) for i in range(nt)]
+    ops = [struct.unpack_from("<8I", plan, 32 + 48 * nt + 32 * i) for i in range(no)]
+    meta = 32 + 48 * nt + 32 * no
+    rows = []
+    for o in ops:
+        code, a, b, z = o[:4]
+        abytes, bbytes, zbytes = ts[a][1], ts[b][1], ts[z][1]
+        const_b = ts[b][8]
+        byt = (abytes + zbytes) * images
+        mac = 0
+        if code in (14, 15):
+            q = np.frombuffer(plan, dtype="<i4", count=20, offset=meta + ts[o[4]][0])
+            kh, kw, oh, ow, ic, oc = q[0], q[1], q[10], q[11], q[16], q[17]
+            k = kh * kw * (1 if code == 15 else ic)
+            mac = int(ts[z][4] * oh * ow) * oc * k * images
+            byt += bbytes + (20 + 3 * oc) * 4
+        elif code in (18, 20, 25, 27):
+            byt += bbytes * (1 if const_b else images)
+        rows.append({"code": code, "bytes": int(byt), "ops": 2 * int(mac)})
+    return rows
+
+
+def roofline(lib, handle, plan, images, iters, peaks, kernel_names):
+    n_ops = len(op_traffic(plan, 1))
+    ns = (C.c_uint64 * 512)()
+    total = C.c_float()
+    rc = lib.ug_profile_batch(handle, images, iters, ns, 512, C.byref(total))
+    if rc:
+        return None, None
+    traffic = op_traffic(plan, images)
+    per_kind = {}
+    for i in range(n_ops):
+        kind = kernel_names.get(traffic[i]["code"], f"op{traffic[i]['code']}")
+        d = per_kind.setdefault(kind, {"ns": 0, "bytes": 0, "ops": 0, "launches": 0})
+        d["ns"] += ns[i] / iters
+        d["bytes"] += traffic[i]["bytes"]
+        d["ops"] += traffic[i]["ops"]
+        d["launches"] += 1 if traffic[i]["code"] != 5 else 0
+    top = max(per_kind, key=lambda k: per_kind[k]["ns"])
+    d = per_kind[top]
+    t = d["ns"] * 1e-9
+    gbs = d["bytes"] / t / 1e9
+    tops = d["ops"] / t / 1e12
+    int8_peak = 2 * peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
+    hbm = peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])
+    ai = d["ops"] / max(d["bytes"], 1)
+    bound = "hbm" if ai < int8_peak * 1e12 / (hbm * 1e9) else "tensor"
+    if bound == "hbm":
+        roof = {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s", "frac": round(gbs / hbm, 4)}
+    else:
+        roof = {"bound": "tensor", "achieved": round(tops, 1), "peak": int8_peak, "unit": "TOPS",
+                "frac": round(tops / int8_peak, 4)}
+    roof.update({"kernel": top, "traffic": None, "launches_per_step": d["launches"],
+                 "ms_per_step": round(d["ns"] / 1e6, 4), "int8_tops": round(tops, 1),
+                 "algorithmic_bytes_per_step": d["bytes"], "share_of_eager_step": round(d["ns"] / 1e6 / total.value * iters, 3)})
+    breakdown = {k: {"ms": round(v["ns"] / 1e6, 4), "GB/s": round(v["bytes"] / (v["ns"] * 1e-9) / 1e9, 1) if v["ns"] else None,
+                     "TOPS": round(v["ops"] / (v["ns"] * 1e-9) / 1e12, 1) if v["ns"] else None}
+                 for k, v in sorted(per_kind.items(), key=lambda kv: -kv[1]["ns"])}
+    return roof, breakdown
+
+
+KERNEL_NAMES = {14: "conv", 15: "depthwise", 16: "pool", 17: "softmax_table", 18: "add", 19: "pack", 20: "concat",
+                21: "resize", 22: "lut", 23: "pad", 24: "mean", 25: "mul", 26: "slice", 27: "bmm", 28: "softmax_exact",
+                10: "permute", 5: "alias"}
+
+
+# --------------------------------------------------------------------------- one model
+def bench_model(lib, dist, name, global_batch, steps, warmup, peaks, want_roofline):
+    from unoq_dsp.bundle import load
+    spec = MODELS[name]
+    model = load(ROOT / "models" / f"{name}.uqmodel")
+    plan = model.plan
+    per_gpu = global_batch // dist.world
+    err = C.c_int()
+    buf = C.create_string_buffer(plan, len(plan))
+    handle = lib.ug_open_mode(buf, len(plan), 0, C.byref(err))
+    if not handle:
+        raise RuntimeError(f"ug_open_mode failed {err.value}: {lib.ug_last_error()}")
+    try:
+        d_in, d_out = C.c_void_p(), C.c_void_p()
+        rc = lib.ug_batch_buffers(handle, per_gpu, C.byref(d_in), C.byref(d_out))
+        if rc:
+            raise RuntimeError(f"batch setup rc={rc}: {lib.ug_last_error()}")
+        ni = int(np.prod(spec["shape"]))
+        no = int(model.metadata["output"]["bytes"])
+        # seeded synthetic images, pinned host staging for the e2e leg
+        h_in = lib.ug_host_alloc(ni * per_gpu)
+        h_out = lib.ug_host_alloc(no * per_gpu)
+        x_host = np.ctypeslib.as_array(C.cast(h_in, C.POINTER(C.c_int8)), shape=(ni * per_gpu,))
+        x_host[:] = np.random.default_rng(1234 + dist.rank).integers(-128, 128, size=ni * per_gpu,
+                                                                        dtype=np.int64).astype(np.int8)
+        # device-resident inputs: one e2e call fills the arena input from the pinned buffer
+        rc = lib.ug_infer_batch(handle, h_in, per_gpu, h_out)
+        if rc:
+            raise RuntimeError(f"ug_infer_batch rc={rc}: {lib.ug_last_error()}")
+        kernels = lib.ug_batch_kernel_count(handle, per_gpu)
+        for _ in range(warmup):
+            lib.ug_launch_batch(handle, per_gpu)
+        lib.ug_synchronize(handle)
+        dist.barrier()
+        ms = C.c_float()
+        with ClockSampler(dist.local) as clocks:
+            rc = lib.ug_time_batch(handle, per_gpu, steps, C.byref(ms))
+        if rc:
+            raise RuntimeError(f"timed run rc={rc}: {lib.ug_last_error()}")
+        dist.barrier()
+        t_dev = dist.max(ms.value / 1e3)
+        value = global_batch * steps / t_dev
+        # e2e through the public batch API (pinned host buffers, copies inside the timed region)
+        for _ in range(1):
+            lib.ug_infer_batch(handle, h_in, per_gpu, h_out)
+        dist.barrier()
+        e2e_ms = 0.0
+        for _ in range(steps):
+            rc = lib.ug_infer_batch(handle, h_in, per_gpu, h_out)
+            if rc:
+                raise RuntimeError(f"e2e rc={rc}")
+            e2e_ms += lib.ug_last_infer_ms(handle)
+        dist.barrier()
+        t_e2e = dist.max(e2e_ms / 1e3)
+        roof = breakdown = None
+        if want_roofline:
+            roof, breakdown = roofline(lib, handle, plan, per_gpu, max(1, min(steps, 3)), peaks, KERNEL_NAMES)
+        lib.ug_host_free(h_in)
+        lib.ug_host_free(h_out)
+        return {
+            "value": value, "ms_per_step": t_dev / steps * 1e3, "per_gpu_batch": per_gpu, "kernels_per_step": kernels,
+            "e2e": {"value": global_batch * steps / t_e2e, "unit": "images/s", "h2d_bytes_per_step": ni * per_gpu,
+                    "d2h_bytes_per_step": no * per_gpu, "ms_per_step": t_e2e / steps * 1e3},
+            "clocks": clocks.summary(), "roofline": roof, "breakdown": breakdown,
+        }
+    finally:
+        lib.ug_close(handle)
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.is_file():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return dict(PEAKS_FALLBACK, source="fallback")
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--global-batch", type=int, default=MODELS["mobilenetv4-small"]["batch"])
+    ap.add_argument("--yolo-batch", type=int, default=MODELS["yolo26n-320"]["batch"])
+    ap.add_argument("--no-yolo", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    mpath = ROOT / "models" / "mobilenetv4-small.uqmodel"
+    cores = os.cpu_count() or 1
+    config = {"workload": f"MobileNetV4-Conv-Small-224 INT8, global batch {args.global_batch} batch-sharded over "
+                          f"{world} GPU(s) (BASELINE config 4); YOLO26n-320 INT8 global batch {args.yolo_batch} "
+                          "alongside", "model": "mobilenetv4-small.uqmodel (bundled weights)",
+              "global_batch": args.global_batch, "image": "224x224x3 int8 NHWC", "parallelism": f"dp{world}",
+              "l2": "inputs larger than L2 (616 MB per 4096 images); no flush needed"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        from oracle.oracle import REF_LIB
+        if not REF_LIB.is_file():
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libug_ref.so not built"}))
+            return
+        pool = make_pool(cores)
+        per_proc = 1
+        for _ in range(args.warmup):
+            reference_throughput(mpath, MODELS["mobilenetv4-small"]["shape"], per_proc, cores, pool)
+        t0 = time.perf_counter()
+        n = 0
+        for _ in range(args.steps):
+            reference_throughput(mpath, MODELS["mobilenetv4-small"]["shape"], per_proc, cores, pool)
+            n += per_proc * cores
+        wall = time.perf_counter() - t0
+        pool.close()
+        value = n / wall
+        sample = f"{per_proc} image(s) per process per step x {cores} processes, seeded int8 input"
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "images/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": wall / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8 (u8 x s8 -> s32)",
+            "data": "synthetic seeded images", "config": config,
+            "cpu_baseline": {"value": round(value, 3), "unit": "images/s", "cores": cores, "kind": "reference",
+                             "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        return
+
+    # CPU baseline pool is spawned before the first CUDA call in this process.
+    pool = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle.oracle import REF_LIB
+        if REF_LIB.is_file():
+            pool = make_pool(cores)
+
+    from unoq_dsp.native import load_library
+    lib = load_library()
+    dist = Dist(args.gpus)
+    if lib.ug_set_device(dist.local) != 0:
+        raise SystemExit(f"cannot select CUDA device {dist.local}")
+    peaks = load_peaks()
+    res = bench_model(lib, dist, "mobilenetv4-small", args.global_batch, args.steps, args.warmup, peaks, True)
+    yolo = None
+    if not args.no_yolo:
+        yolo = bench_model(lib, dist, "yolo26n-320", args.yolo_batch, args.steps, args.warmup, peaks, True)
+    cpu = None
+    if pool is not None:
+        per_proc = 4
+        value, wall, _ = reference_throughput(mpath, MODELS["mobilenetv4-small"]["shape"], per_proc, cores, pool)
+        pool.close()
+        cpu = {"value": round(value, 3), "unit": "images/s", "cores": cores, "kind": "reference",
+               "sample": f"{per_proc * cores} MobileNetV4 images ({per_proc} per process on {cores} processes), "
+                         f"{wall:.1f} s wall"}
+    launches = res["kernels_per_step"] * args.steps
+    dist.close()
+    if rank != 0:
+        return
+    roof = res["roofline"]
+    if roof is not None:
+        roof["peak_source"] = peaks["source"]
+    line = {
+        "metric": METRIC, "value": round(res["value"], 2), "unit": "images/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(res["ms_per_step"], 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8 (s8 x s8 -> s32, int64 requant)",
+        "data": "synthetic seeded int8 images; bundled model weights", "config": config,
+        "e2e": {k: (round(v, 2) if isinstance(v, float) else v) for k, v in res["e2e"].items()},
+        "roofline": roof, "cpu_baseline": cpu, "clocks": res["clocks"], "gpu_launches": launches,
+        "per_gpu_batch": res["per_gpu_batch"], "kernel_breakdown": res["breakdown"],
+    }
+    if yolo is not None:
+        line[MODELS["yolo26n-320"]["key"]] = {
+            "value": round(yolo["value"], 2), "unit": "images/s", "global_batch": args.yolo_batch,
+            "ms_per_step": round(yolo["ms_per_step"], 4), "e2e": yolo["e2e"], "roofline": yolo["roofline"],
+            "kernels_per_step": yolo["kernels_per_step"], "kernel_breakdown": yolo["breakdown"], "clocks": yolo["clocks"]}
+    print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,101 @@
+/*
+ * unoq_cuda.h -- C ABI of libunoq_cuda.so, the B200 (sm_100a) backend for unoq-dsp plans.
+ *
+ * The library is a drop-in for the reference's FastRPC/Hexagon backend. It exports the same
+ * symbols with the same argument meaning and error codes, so existing ctypes/FFI callers
+ * (unoq_dsp.transport via UNOQ_DSP_LIBRARY, the reference tests via UNOQ_NATIVE_LIBRARY)
+ * can load it unchanged. Plans are the reference's UGN1 format (runtime/graph.h:15-38).
+ *
+ * All buffers named by a plain pointer are HOST memory unless the name says "device".
+ * Every call is synchronous unless stated. Error codes:
+ *   10-16 header/tensor/matmul validation, 17-19 op validation, 20 work limit,
+ *   21 output undefined, 22 bad call, 24 unavailable/poisoned, 25 lifetime overlap
+ *   (runtime/graph.c:50-216); 1001 session busy, 1002 allocation, 1003 bad arguments,
+ *   1004 transfer, 1005 thread, 1006 timeout (runtime/bridge.c); 2001 CUDA runtime error,
+ *   2002 no CUDA device, 2003 device-side wait timed out.
+ */
+#ifndef UNOQ_CUDA_H
+#define UNOQ_CUDA_H
+#include <stddef.h>
+#include <stdint.h>
+#if defined(__GNUC__)
+#define UG_API __attribute__((visibility("default")))
+#else
+#define UG_API
+#endif
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- Graph ABI: replaces runtime/graph.h:39-45 (process-global single graph). ---------- */
+
+/* Replaces ug_load (runtime/graph.c:50-262): validate the plan, upload constants, prepare
+ * kernels. Any earlier graph is released first. Returns 0 or a 10-25 code. */
+UG_API int ug_load(const void *plan, uint32_t bytes);
+/* Replaces ug_run (runtime/graph.c:438-448): one image, host buffers, synchronous.
+ * A failing run clears the loaded state (reload required), as in the reference. */
+UG_API int ug_run(const void *input, uint32_t input_bytes, void *output, uint32_t output_bytes);
+/* Replace ug_input_bytes / ug_output_bytes (runtime/graph.c:263-264); 0 when nothing loaded. */
+UG_API uint32_t ug_input_bytes(void);
+UG_API uint32_t ug_output_bytes(void);
+/* Replaces ug_snapshot (runtime/graph.c:265-268): copy tensor `tensor` of the last image run. */
+UG_API int ug_snapshot(uint32_t tensor, void *out, uint32_t bytes);
+/* Replaces ug_profile (runtime/graph.c:269-284): command 0 off, 1 reset+on, 2 read.
+ * `out` receives (UG_MAX_OP+2) or 130 uint64 counters: [0] runs, [1] total ns,
+ * [2+i] nanoseconds spent in op i (CUDA-event timed, profiling runs are not graph-captured). */
+UG_API int ug_profile(uint32_t command, void *out, uint32_t bytes);
+
+/* ---- Session ABI: replaces runtime/bridge.c (libuno_backend.so exports). -------------- */
+
+/* Replaces ug_open_mode (runtime/bridge.c:99-125). One active session per process (1001).
+ * pipeline 0 = blocking, 1 = "mailbox" (accepted for compatibility; both are stream-ordered). */
+UG_API void *ug_open_mode(const void *plan, uint32_t bytes, int pipeline, int *error);
+/* Replaces ug_open (runtime/bridge.c:126). */
+UG_API void *ug_open(const void *plan, uint32_t bytes, int *error);
+/* Replaces ug_infer (runtime/bridge.c:148-185): one image, host buffers. */
+UG_API int ug_infer(void *session, const void *input, uint32_t input_bytes, void *output, uint32_t output_bytes);
+/* Replaces ug_close (runtime/bridge.c:70-80); idempotent on NULL. */
+UG_API void ug_close(void *session);
+/* Replaces ug_snapshot_tensor (runtime/bridge.c:127-130). */
+UG_API int ug_snapshot_tensor(void *session, uint32_t tensor, void *out, uint32_t bytes);
+/* Replaces ug_profile_control (runtime/bridge.c:134-147). */
+UG_API int ug_profile_control(void *session, uint32_t command, void *out, uint32_t bytes);
+
+/* ---- Extensions (no reference counterpart): batching, device selection, timing. ------- */
+
+/* Select the CUDA device used by the next ug_open/ug_load in this process (default 0). */
+UG_API int ug_set_device(int device);
+/* Run `images` independent images (inputs back to back, outputs back to back), host
+ * buffers. Pinned buffers from ug_host_alloc give full-bandwidth copies. The first call
+ * for a batch size prepares and captures a CUDA graph for it. */
+UG_API int ug_infer_batch(void *session, const void *input, uint32_t images, void *output);
+/* Device-resident variant: `device_input`/`device_output` are this session's device
+ * buffers from ug_batch_buffers; nothing crosses PCIe. Asynchronous on the session stream. */
+UG_API int ug_batch_buffers(void *session, uint32_t images, void **device_input, void **device_output);
+UG_API int ug_launch_batch(void *session, uint32_t images);
+UG_API int ug_synchronize(void *session);
+/* Time `iterations` back-to-back ug_launch_batch(images) on the session stream with CUDA
+ * events; writes the elapsed milliseconds. */
+UG_API int ug_time_batch(void *session, uint32_t images, uint32_t iterations, float *milliseconds);
+/* Milliseconds of the last ug_infer_batch measured by events on the session stream,
+ * host-to-device copy, graph and device-to-host copy included. */
+UG_API float ug_last_infer_ms(void *session);
+/* Pinned host memory for ug_infer_batch buffers. */
+UG_API void *ug_host_alloc(size_t bytes);
+UG_API void ug_host_free(void *ptr);
+/* Host-only loader check with the exact ug_load codes; touches no GPU. */
+UG_API int ug_validate_plan(const void *plan, uint32_t bytes);
+/* Number of kernel launches one ug_launch_batch issues (graph nodes of this library). */
+UG_API int ug_batch_kernel_count(void *session, uint32_t images);
+/* Eager profiling of a batch: `iterations` passes with a CUDA event after every plan op;
+ * op_ns[i] (count >= number of plan ops) receives the summed nanoseconds of op i and
+ * *total_ms the summed pass time. Not graph-captured, so launch gaps are included. */
+UG_API int ug_profile_batch(void *session, uint32_t images, uint32_t iterations, uint64_t *op_ns, uint32_t count,
+                            float *total_ms);
+/* Last CUDA error string seen by the library (empty if none). */
+UG_API const char *ug_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

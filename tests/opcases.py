@@ -1,0 +1,306 @@
+"""Seeded one-op and few-op plans covering every INT8 opcode of the plan ABI.
+
+Each builder returns (plan_bytes, input_array). Shapes are parameterised by `scale` so the same
+case runs small (CPU oracle, golden fixtures) and large (GPU parity). Edge cases the reference
+tests pin are included: ragged channel counts, stride/dilation/padding mixes, requantisation
+with left shifts and negative ties, post-LUT fusion, saturating clamps, adj flags for BMM.
+"""
+import math
+
+import numpy as np
+
+from unoq_dsp import synth
+from unoq_dsp.synth import PlanWriter, conv2d, multiplier
+
+
+def _rand_input(rng, shape):
+    return rng.integers(-128, 128, size=shape, dtype=np.int64).astype(np.int8)
+
+
+def conv_case(rng, x_shape, oc, kernel, stride, **kw):
+    plan, xs, _ = synth.single_conv_plan(rng, x_shape, oc, kernel, stride, **kw)
+    return plan, _rand_input(rng, xs)
+
+
+def conv_post_case(rng, x_shape, oc, kernel, stride, depthwise=False):
+    """Conv/depthwise with a fused 256-entry post table (YOLO's SiLU-style fusion)."""
+    spec = synth.random_quant_conv(rng, x_shape, oc, kernel, stride, depthwise=depthwise, act="none")
+    pw = PlanWriter()
+    x = pw.tensor(x_shape)
+    table = rng.integers(0, 256, size=256).astype(np.uint8)
+    z, _ = conv2d(pw, x, x_shape, spec["xq"], spec["weights"], spec["bias"], spec["wscales"], spec["yq"],
+                  stride=stride, act="none", depthwise=depthwise, post=table)
+    return pw.build(x, z), _rand_input(rng, x_shape)
+
+
+def conv_shift_case(rng, x_shape, oc, kernel):
+    """Output scale small enough that multipliers exceed one: positive exponents (pre-shift)."""
+    spec = synth.random_quant_conv(rng, x_shape, oc, kernel, (1, 1), xq=(0.02, 1), yq=(2e-6, 0), act="none",
+                                   bias_bits=4, wscale_range=(1e-3, 2e-3))
+    w = spec["weights"]
+    w[:] = np.clip(w // 32, -4, 4)
+    pw = PlanWriter()
+    x = pw.tensor(x_shape)
+    z, _ = conv2d(pw, x, x_shape, spec["xq"], w, spec["bias"], spec["wscales"], spec["yq"], act="none")
+    xin = rng.integers(-3, 4, size=x_shape).astype(np.int8)
+    return pw.build(x, z), xin
+
+
+def conv_ties_case(rng):
+    """1x1 identity-like conv with exponents 1..15 below zero and small biases: exercises the
+    ties-away-from-zero rounding on negative values (the reference pins this in
+    tests/test_modern_ops.py:66-73)."""
+    c = 16
+    x_shape = (1, 4, 8, c)
+    w = np.zeros((c, 1, 1, c), dtype=np.int8)
+    for j in range(c):
+        w[j, 0, 0, j] = 1 if j % 2 else -1
+    pw = PlanWriter()
+    x = pw.tensor(x_shape)
+    ws = np.array([2.0 ** -(1 + j % 15) for j in range(c)])
+    z, _ = conv2d(pw, x, x_shape, (1.0, 0), w, np.arange(-8, 8), ws, (1.0, 0), padding="valid", act="none")
+    xin = np.resize(np.arange(-128, 128, dtype=np.int64), int(np.prod(x_shape))).astype(np.int8).reshape(x_shape)
+    return pw.build(x, z), xin
+
+
+def pool_case(rng, x_shape, kernel, stride, is_max, padding="same"):
+    pw = PlanWriter()
+    x = pw.tensor(x_shape)
+    z, _ = synth.pool2d(pw, x, x_shape, (-100, 120), kernel, stride, padding=padding, is_max=is_max, zero=-3)
+    return pw.build(x, z), _rand_input(rng, x_shape)
+
+
+def add_case(rng, shape):
+    pw = PlanWriter()
+    x = pw.tensor(shape)
+    b = pw.tensor(shape)
+    # b must be an activation defined before the add: produce it from x by a LUT op.
+    table = rng.integers(0, 256, size=256).astype(np.uint8)
+    t = pw.tensor((256,), "u1", table)
+    pw.op(22, x, t, b)
+    q = synth.add_parameters(0.05, -3, 0.08, 7, 0.1, -1, -120, 127)
+    qi = pw.tensor((520,), "i4", q)
+    z = pw.tensor(shape)
+    pw.op(18, x, b, z, (qi, 0, 0, 0))
+    return pw.build(x, z), _rand_input(rng, shape)
+
+
+def mul_case(rng, shape):
+    pw = PlanWriter()
+    x = pw.tensor(shape)
+    t = pw.tensor((256,), "u1", rng.integers(0, 256, size=256).astype(np.uint8))
+    b = pw.tensor(shape)
+    pw.op(22, x, t, b)
+    qm, qs = multiplier(0.05 * 0.04 / 0.03)
+    qi = pw.tensor((7,), "i4", [-3, 5, 2, qm, qs, -128, 127])
+    z = pw.tensor(shape)
+    pw.op(25, x, b, z, (qi, 0, 0, 0))
+    return pw.build(x, z), _rand_input(rng, shape)
+
+
+def lut_case(rng, shape, out_dtype="i1"):
+    pw = PlanWriter()
+    x = pw.tensor(shape)
+    t = pw.tensor((256,), "u1", rng.integers(0, 256, size=256).astype(np.uint8))
+    z = pw.tensor(shape, out_dtype)
+    pw.op(22, x, t, z)
+    return pw.build(x, z), _rand_input(rng, shape)
+
+
+def mean_parameters(count, xs, xz, ys, yz):
+    """MEAN block as the reference compiler forms it (tflite.py:267-272)."""
+    qm, qs = multiplier(xs / ys)
+    adjust = min(count.bit_length() - 1, 32, 31 + qs)
+    qm = (qm << adjust) // count
+    qs -= adjust
+    return [count, xz, yz, qm, qs]
+
+
+def mean_case(rng, shape):
+    n, h, w, c = shape
+    pw = PlanWriter()
+    x = pw.tensor(shape)
+    qi = pw.tensor((5,), "i4", mean_parameters(h * w, 0.05, -7, 0.03, 4))
+    z = pw.tensor((n, 1, 1, c))
+    pw.op(24, x, qi, z)
+    return pw.build(x, z), _rand_input(rng, shape)
+
+
+def concat_case(rng, shape_a, shape_b, axis):
+    pw = PlanWriter()
+    x = pw.tensor(shape_a)
+    # b: a slice of a LUT of x keeps it an activation of the right shape
+    t = pw.tensor((256,), "u1", rng.integers(0, 256, size=256).astype(np.uint8))
+    xa = pw.tensor(shape_a)
+    pw.op(22, x, t, xa)
+    b = pw.tensor(shape_b)
+    pw.op(26, xa, xa, b, (0, 0, 0, 0))
+    zshape = list(shape_a)
+    zshape[axis] += shape_b[axis]
+    z = pw.tensor(tuple(zshape))
+    pw.op(20, x, b, z, (axis, 0, 0, 0))
+    return pw.build(x, z), _rand_input(rng, shape_a)
+
+
+def slice_case(rng, shape, begin, size):
+    pw = PlanWriter()
+    x = pw.tensor(shape)
+    z = pw.tensor(size)
+    pw.op(26, x, x, z, tuple(begin) + (0,) * (4 - len(begin)))
+    return pw.build(x, z), _rand_input(rng, shape)
+
+
+def transpose_case(rng, shape, perm):
+    pw = PlanWriter()
+    x = pw.tensor(shape)
+    z = pw.tensor(tuple(shape[p] for p in perm))
+    pw.op(10, x, x, z, tuple(perm) + (0,) * (4 - len(perm)))
+    return pw.build(x, z), _rand_input(rng, shape)
+
+
+def resize_case(rng, shape, out_hw):
+    n, ih, iw, c = shape
+    oh, ow = out_hw
+    rows = (np.floor(np.arange(oh) * (ih / oh)).astype(np.int64) * iw * c)
+    cols = (np.floor(np.arange(ow) * (iw / ow)).astype(np.int64) * c)
+    pw = PlanWriter()
+    x = pw.tensor(shape)
+    b = pw.tensor((oh + ow,), "i4", np.concatenate((rows, cols)))
+    z = pw.tensor((n, oh, ow, c))
+    pw.op(21, x, b, z)
+    return pw.build(x, z), _rand_input(rng, shape)
+
+
+def pad_case(rng, shape, pads, value=-5):
+    pads = np.asarray(pads, dtype=np.int64).reshape(4, 2)
+    pw = PlanWriter()
+    x = pw.tensor(shape)
+    b = pw.tensor((8,), "i4", pads.reshape(-1))
+    z = pw.tensor(tuple(np.asarray(shape) + pads.sum(axis=1)))
+    pw.op(23, x, b, z, (value, 0, 0, 0))
+    return pw.build(x, z), _rand_input(rng, shape)
+
+
+def pack_case(rng, shape):
+    """Three outputs packed: x itself, a LUT of x, a slice of x (op 19 list semantics)."""
+    pw = PlanWriter()
+    x = pw.tensor(shape)
+    t = pw.tensor((256,), "u1", rng.integers(0, 256, size=256).astype(np.uint8))
+    y1 = pw.tensor(shape)
+    pw.op(22, x, t, y1)
+    half = (shape[0], shape[1], shape[2], max(1, shape[3] // 2))
+    y2 = pw.tensor(half)
+    pw.op(26, x, x, y2, (0, 0, 0, 0))
+    lst = pw.tensor((3,), "i4", [y1, x, y2])
+    total = 2 * int(np.prod(shape)) + int(np.prod(half))
+    z = pw.tensor((total,))
+    pw.op(19, y1, lst, z)
+    return pw.build(x, z), _rand_input(rng, shape)
+
+
+def bmm_case(rng, batch, m, k, n, adj_x=0, adj_y=0):
+    a_shape = (batch, k, m) if adj_x else (batch, m, k)
+    b_shape = (batch, n, k) if adj_y else (batch, k, n)
+    pw = PlanWriter()
+    x = pw.tensor((int(np.prod(a_shape)) + int(np.prod(b_shape)),))
+    a = pw.tensor(a_shape)
+    pw.op(26, x, x, pw.tensor((int(np.prod(a_shape)),)), (0, 0, 0, 0))
+    flat_a = len(pw.tensors) - 1
+    pw.op(5, flat_a, flat_a, a)
+    b = pw.tensor(b_shape)
+    flat_b = pw.tensor((int(np.prod(b_shape)),))
+    pw.op(26, x, x, flat_b, (int(np.prod(a_shape)), 0, 0, 0))
+    pw.op(5, flat_b, flat_b, b)
+    qm, qs = multiplier(0.02 * 0.03 / 0.5)
+    qi = pw.tensor((7,), "i4", [-5, 3, 1, qm, qs, adj_x, adj_y])
+    z = pw.tensor((batch, m, n))
+    pw.op(27, a, b, z, (qi, 0, 0, 0))
+    return pw.build(x, z), _rand_input(rng, (int(np.prod(a_shape)) + int(np.prod(b_shape)),))
+
+
+def softmax_exact_case(rng, rows, width, scale=0.1):
+    lut = [2147483647] + [int(round(2147483647 * math.exp(-i * scale))) for i in range(1, 256)]
+    lut = np.minimum.accumulate(np.asarray(lut, dtype=np.int64))
+    pw = PlanWriter()
+    x = pw.tensor((1, rows, width))
+    b = pw.tensor((257,), "i4", np.concatenate(([width], lut)))
+    z = pw.tensor((1, rows, width))
+    pw.op(28, x, b, z)
+    return pw.build(x, z), _rand_input(rng, (1, rows, width))
+
+
+def softmax_table_case(rng, rows, width, scale=0.05):
+    table = [1 << 24] + [int(round((1 << 24) * math.exp(-i * scale))) for i in range(1, 256)]
+    q = [1, 1, 1, 1, 1, 1, 0, 0, 0, 0, 1, 1, -128, -128, -128, 127, width, width, 8, 0] + table
+    pw = PlanWriter()
+    x = pw.tensor((1, rows, width))
+    qi = pw.tensor((len(q),), "i4", q)
+    z = pw.tensor((1, rows, width))
+    pw.op(17, x, x, z, (qi, 0, 0, 0))
+    return pw.build(x, z), _rand_input(rng, (1, rows, width))
+
+
+def block_case(rng, hw=14, c=32, expand=96):
+    """Inverted-residual block: pw expand -> dw 3x3 -> pw project -> residual add."""
+    x_shape = (1, hw, hw, c)
+    pw = PlanWriter()
+    x = pw.tensor(x_shape)
+    s1 = synth.random_quant_conv(rng, x_shape, expand, (1, 1), (1, 1), xq=(0.05, -3), yq=(0.04, -128))
+    h, hs = conv2d(pw, x, x_shape, s1["xq"], s1["weights"], s1["bias"], s1["wscales"], s1["yq"], act="relu")
+    s2 = synth.random_quant_conv(rng, hs, expand, (3, 3), (1, 1), xq=(0.04, -128), yq=(0.03, -128), depthwise=True)
+    d, ds = conv2d(pw, h, hs, s2["xq"], s2["weights"], s2["bias"], s2["wscales"], s2["yq"], act="relu",
+                   depthwise=True)
+    s3 = synth.random_quant_conv(rng, ds, c, (1, 1), (1, 1), xq=(0.03, -128), yq=(0.06, 2), act="none")
+    p, _ = conv2d(pw, d, ds, s3["xq"], s3["weights"], s3["bias"], s3["wscales"], s3["yq"], act="none")
+    q = synth.add_parameters(0.06, 2, 0.05, -3, 0.07, 0, -128, 127)
+    qi = pw.tensor((520,), "i4", q)
+    z = pw.tensor(x_shape)
+    pw.op(18, p, x, z, (qi, 0, 0, 0))
+    return pw.build(x, z, version=2), _rand_input(rng, x_shape)
+
+
+def all_cases(scale=1):
+    """(name, builder) pairs; scale multiplies spatial sizes for the GPU runs."""
+    s = scale
+    return [
+        ("conv_pw_c0", lambda r: conv_case(r, (1, 8 * s, 8 * s, 64), 128, (1, 1), (1, 1))),
+        ("conv_pw_ragged", lambda r: conv_case(r, (1, 5 * s, 7, 48), 40, (1, 1), (1, 1), act="none")),
+        ("conv_3x3_s1", lambda r: conv_case(r, (1, 9 * s, 7, 16), 24, (3, 3), (1, 1))),
+        ("conv_3x3_s2", lambda r: conv_case(r, (1, 10 * s, 10, 32), 16, (3, 3), (2, 2), xq=(0.03, 17))),
+        ("conv_stem_rgb", lambda r: conv_case(r, (1, 16 * s, 12, 3), 16, (3, 3), (2, 2), xq=(0.02, -13))),
+        ("conv_5x5_dil2_valid", lambda r: conv_case(r, (1, 12 * s, 11, 8), 4, (5, 5), (1, 1), dilation=(2, 2),
+                                                    padding=(1, 0, 2, 3), act="relu6")),
+        ("conv_fc", lambda r: conv_case(r, (1, 1, 1, 96), 40, (1, 1), (1, 1), act="none")),
+        ("conv_wide_k", lambda r: conv_case(r, (1, 4 * s, 5, 256), 64, (3, 3), (1, 1))),
+        ("conv_post_lut", lambda r: conv_post_case(r, (1, 6 * s, 6, 32), 32, (3, 3), (1, 1))),
+        ("conv_shift_pos", lambda r: conv_shift_case(r, (1, 4 * s, 4, 16), 8, (1, 1))),
+        ("conv_ties", lambda r: conv_ties_case(r)),
+        ("dw3_s1", lambda r: conv_case(r, (1, 9 * s, 8, 32), 32, (3, 3), (1, 1), depthwise=True)),
+        ("dw3_s2", lambda r: conv_case(r, (1, 11 * s, 9, 48), 48, (3, 3), (2, 2), depthwise=True)),
+        ("dw5_s1", lambda r: conv_case(r, (1, 7 * s, 7, 64), 64, (5, 5), (1, 1), depthwise=True, act="none")),
+        ("dw5_s2", lambda r: conv_case(r, (1, 14 * s, 14, 16), 16, (5, 5), (2, 2), depthwise=True)),
+        ("dw3_c6", lambda r: conv_case(r, (1, 5 * s, 5, 6), 6, (3, 3), (1, 1), depthwise=True)),
+        ("dw3_post_lut", lambda r: conv_post_case(r, (1, 6 * s, 6, 24), 24, (3, 3), (1, 1), depthwise=True)),
+        ("pool_max5", lambda r: pool_case(r, (1, 10 * s, 10, 16), (5, 5), (1, 1), True)),
+        ("pool_avg3_s2", lambda r: pool_case(r, (1, 9 * s, 7, 8), (3, 3), (2, 2), False)),
+        ("pool_avg2_valid", lambda r: pool_case(r, (1, 8 * s, 8, 4), (2, 2), (2, 2), False, padding="valid")),
+        ("add", lambda r: add_case(r, (1, 7 * s, 5, 16))),
+        ("mul", lambda r: mul_case(r, (1, 6 * s, 5, 8))),
+        ("lut_i8", lambda r: lut_case(r, (1, 5 * s, 7, 9))),
+        ("lut_u8", lambda r: lut_case(r, (1, 3 * s, 3, 16), out_dtype="u1")),
+        ("mean", lambda r: mean_case(r, (1, 7, 7, 40 * s))),
+        ("concat_c", lambda r: concat_case(r, (1, 4 * s, 5, 16), (1, 4 * s, 5, 8), 3)),
+        ("concat_h", lambda r: concat_case(r, (1, 4 * s, 5, 16), (1, 2, 5, 16), 1)),
+        ("slice", lambda r: slice_case(r, (1, 6 * s, 7, 16), (0, 1, 2, 4), (1, 3, 4, 8))),
+        ("transpose_nchw", lambda r: transpose_case(r, (1, 5 * s, 6, 12), (0, 3, 1, 2))),
+        ("transpose_3d", lambda r: transpose_case(r, (2, 7 * s, 9), (0, 2, 1))),
+        ("resize2x", lambda r: resize_case(r, (1, 5 * s, 6, 8), (10 * s, 12))),
+        ("pad", lambda r: pad_case(r, (1, 4 * s, 5, 6), [0, 0, 1, 2, 2, 1, 0, 0])),
+        ("pad_channels", lambda r: pad_case(r, (1, 3, 4 * s, 5), [0, 1, 0, 0, 1, 0, 2, 3])),
+        ("pack", lambda r: pack_case(r, (1, 4 * s, 3, 6))),
+        ("bmm", lambda r: bmm_case(r, 2, 10 * s, 16, 12)),
+        ("bmm_adj", lambda r: bmm_case(r, 2, 9, 20, 7 * s, adj_x=1, adj_y=1)),
+        ("softmax_exact", lambda r: softmax_exact_case(r, 10 * s, 100)),
+        ("softmax_table", lambda r: softmax_table_case(r, 6 * s, 33)),
+        ("block", lambda r: block_case(r, hw=7 * s)),
+    ]

@@ -1,0 +1,83 @@
+"""GPU parity, per opcode: libunoq_cuda.so through its C ABI against the reference's outputs
+(golden fixtures) and against the oracle at larger sizes and batches. Bit-exact throughout:
+every op is integer arithmetic."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import opcases
+from gpuhelp import NativeSession
+
+pytestmark = pytest.mark.gpu
+NAMES = [n for n, _ in opcases.all_cases(1)]
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_graph_abi_matches_reference_golden(name, native, golden_ops):
+    """ug_load + ug_run (runtime/graph.h ABI), one image, against the reference runtime's output."""
+    plan = golden_ops[f"{name}/plan"].tobytes()
+    x = golden_ops[f"{name}/x"]
+    buf = C.create_string_buffer(plan, len(plan))
+    assert native.ug_load(buf, len(plan)) == 0, native.ug_last_error()
+    no = native.ug_output_bytes()
+    y = np.empty(no, dtype=np.int8)
+    assert native.ug_run(x.ctypes.data, x.nbytes, y.ctypes.data, no) == 0, native.ug_last_error()
+    np.testing.assert_array_equal(y, golden_ops[f"{name}/y"])
+
+
+@pytest.mark.parametrize("name", NAMES)
+@pytest.mark.parametrize("images", [3])
+def test_batched_session_matches_oracle_at_scale(name, images, native, oracle):
+    builder = dict(opcases.all_cases(4))[name]
+    rng = np.random.default_rng(101)
+    plan, x0 = builder(rng)
+    xs = np.stack([x0] + [rng.integers(-128, 128, size=x0.shape, dtype=np.int64).astype(np.int8)
+                          for _ in range(images - 1)])
+    expect = oracle.run(plan, xs, images)
+    with NativeSession(native, plan) as s:
+        got = s.run(xs, images)
+        np.testing.assert_array_equal(got, expect)
+        # the same images one at a time give the same bytes (no cross-image coupling)
+        single = s.run(xs[1])
+        np.testing.assert_array_equal(single, expect[single.size:2 * single.size])
+
+
+def test_reload_replaces_graph(native, golden_ops):
+    for name in ("conv_pw_c0", "dw3_s2", "softmax_exact"):
+        plan = golden_ops[f"{name}/plan"].tobytes()
+        assert native.ug_load(C.create_string_buffer(plan, len(plan)), len(plan)) == 0
+    assert native.ug_output_bytes() == golden_ops["softmax_exact/y"].size
+
+
+def test_bad_calls_return_reference_codes(native, golden_ops):
+    plan = golden_ops["add/plan"].tobytes()
+    assert native.ug_load(C.create_string_buffer(plan, len(plan)), len(plan)) == 0
+    x = golden_ops["add/x"]
+    y = np.empty(golden_ops["add/y"].size, dtype=np.int8)
+    assert native.ug_run(x.ctypes.data, x.nbytes - 1, y.ctypes.data, y.nbytes) == 22
+    assert native.ug_snapshot(0, y.ctypes.data, 3) == 22
+    err = C.c_int()
+    h = native.ug_open_mode(C.create_string_buffer(plan, len(plan)), len(plan), 0, C.byref(err))
+    assert h and err.value == 0
+    h2 = native.ug_open_mode(C.create_string_buffer(plan, len(plan)), len(plan), 0, C.byref(err))
+    assert not h2 and err.value == 1001  # one session per process (bridge.c:101)
+    assert native.ug_infer(h, x.ctypes.data, x.nbytes + 1, y.ctypes.data, y.nbytes) == 1003
+    native.ug_close(h)
+    native.ug_close(None)
+
+
+def test_snapshot_and_profile(native, golden_ops):
+    plan = golden_ops["block/plan"].tobytes()
+    assert native.ug_load(C.create_string_buffer(plan, len(plan)), len(plan)) == 0
+    counters = np.zeros(514, dtype=np.uint64)
+    assert native.ug_profile(1, counters.ctypes.data, counters.nbytes) == 0
+    x = golden_ops["block/x"]
+    y = np.empty(golden_ops["block/y"].size, dtype=np.int8)
+    assert native.ug_run(x.ctypes.data, x.nbytes, y.ctypes.data, y.nbytes) == 0
+    np.testing.assert_array_equal(y, golden_ops["block/y"])
+    assert native.ug_profile(2, counters.ctypes.data, counters.nbytes) == 0
+    assert counters[0] == 1 and counters[1] > 0
+    inp = np.empty(x.size, dtype=np.int8)
+    assert native.ug_snapshot(0, inp.ctypes.data, inp.nbytes) == 0
+    np.testing.assert_array_equal(inp, x)

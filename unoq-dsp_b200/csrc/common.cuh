@@ -1,0 +1,56 @@
+// common.cuh -- device helpers shared by every kernel of libunoq_cuda.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace uq {
+
+// TFLite double-rounding requantisation, bit-exact with the reference (runtime/qnn.c:61-83):
+// optional pre-multiply left shift; rounding-doubling high multiply (v*m + 2^30) >> 31 on the
+// full 64-bit product; ties-away-from-zero rounding right shift for negative exponents.
+__device__ __forceinline__ int32_t dev_scale(int32_t v, int32_t m, int shift) {
+    if (shift > 0) v = (int32_t)((uint32_t)v << shift);
+    int64_t p = (int64_t)v * (int64_t)m;
+    int32_t h = (int32_t)((p + (1ll << 30)) >> 31);
+    if (shift >= 0) return h;
+    unsigned s = (unsigned)(-shift);
+    uint32_t mask = (1u << s) - 1u;
+    int32_t base = h >> s;
+    uint32_t rem = (uint32_t)h & mask;
+    return base + (int32_t)(rem > ((mask >> 1) + (h < 0 ? 1u : 0u)));
+}
+
+__device__ __forceinline__ int32_t dev_clamp(int32_t v, int32_t lo, int32_t hi) {
+    return v < lo ? lo : (v > hi ? hi : v);
+}
+
+// Per-output-channel requantisation block prepared at load time from a plan's q tensor
+// (qnn.c:12-16): y = post[clamp(scale(acc + bias[c], mult[c], shift[c]) + yzp, lo, hi)].
+struct Requant {
+    const int32_t *bias;   // corrected bias (plus any load-time folded terms), wraps mod 2^32
+    const int32_t *mult;   // Q31 multiplier
+    const int32_t *shift;  // exponent in [-31, 15]
+    const uint8_t *post;   // optional 256-entry table indexed by y + 128, or nullptr
+    int32_t yzp, lo, hi;
+};
+
+__device__ __forceinline__ int8_t requant_one(int32_t acc, int c, const Requant &r) {
+    int32_t v = (int32_t)((uint32_t)acc + (uint32_t)__ldg(r.bias + c));
+    v = dev_scale(v, __ldg(r.mult + c), __ldg(r.shift + c)) + r.yzp;
+    v = dev_clamp(v, r.lo, r.hi);
+    if (r.post) v = (int8_t)__ldg(r.post + v + 128);
+    return (int8_t)v;
+}
+
+inline unsigned ceil_div(uint64_t a, uint64_t b) { return (unsigned)((a + b - 1) / b); }
+
+// Grid size for a grid-stride loop over `n` items of `per_block` each, capped to keep
+// every SM of a B200 (148) busy without an excessive tail.
+inline unsigned grid_for(uint64_t n, unsigned per_block, unsigned cap = 148u * 32u) {
+    uint64_t g = (n + per_block - 1) / per_block;
+    if (g < 1) g = 1;
+    if (g > cap) g = cap;
+    return (unsigned)g;
+}
+
+}  // namespace uq

@@ -1,0 +1,664 @@
+// engine.cu -- plan preparation, batched arena planning, op lowering and CUDA-graph replay.
+#include "engine.hpp"
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <numeric>
+
+#include "conv_tc.cuh"
+#include "kernels.cuh"
+
+namespace uq {
+
+namespace {
+std::mutex g_err_mu;
+std::string g_err;
+
+constexpr size_t kAlign = 256;
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+}  // namespace
+
+void set_error(const std::string &msg) {
+    std::lock_guard<std::mutex> lk(g_err_mu);
+    g_err = msg;
+}
+const char *last_error() { return g_err.c_str(); }
+
+#define UQ_CUDA(call)                                                                      \
+    do {                                                                                   \
+        cudaError_t e_ = (call);                                                           \
+        if (e_ != cudaSuccess) {                                                           \
+            set_error(std::string(#call) + ": " + cudaGetErrorString(e_));                 \
+            return 2001;                                                                   \
+        }                                                                                  \
+    } while (0)
+
+Engine::~Engine() { release(); }
+
+void Engine::release() {
+    if (device_ >= 0 && (d_const_ || stream_)) cudaSetDevice(device_);
+    if (stream_) cudaStreamSynchronize(stream_);
+    for (auto &kv : batches_) {
+        BatchCtx &b = *kv.second;
+        if (b.exec) cudaGraphExecDestroy(b.exec);
+        if (b.graph) cudaGraphDestroy(b.graph);
+        if (b.arena) cudaFree(b.arena);
+        if (b.host_in) cudaFreeHost(b.host_in);
+        if (b.host_out) cudaFreeHost(b.host_out);
+    }
+    batches_.clear();
+    for (void *p : prep_) cudaFree(p);
+    prep_.clear();
+    if (d_const_) cudaFree(d_const_);
+    d_const_ = nullptr;
+    if (ev0_) cudaEventDestroy(ev0_);
+    if (ev1_) cudaEventDestroy(ev1_);
+    ev0_ = ev1_ = nullptr;
+    if (stream_) cudaStreamDestroy(stream_);
+    stream_ = nullptr;
+    steps_.clear();
+    ready_ = false;
+}
+
+void *Engine::prep_alloc(size_t bytes) {
+    void *p = nullptr;
+    if (cudaMalloc(&p, bytes ? bytes : 1) != cudaSuccess) return nullptr;
+    prep_.push_back(p);
+    return p;
+}
+
+int Engine::load(const void *plan, uint32_t bytes, int device) {
+    release();
+    Plan P;
+    int rc = parse_plan(plan, bytes, P);
+    if (rc) return rc;
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count <= 0) {
+        set_error("no CUDA device");
+        return 2002;
+    }
+    if (device < 0 || device >= count) {
+        set_error("device index out of range");
+        return 2002;
+    }
+    device_ = device;
+    P_ = std::move(P);
+    UQ_CUDA(cudaSetDevice(device_));
+    UQ_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    UQ_CUDA(cudaEventCreate(&ev0_));
+    UQ_CUDA(cudaEventCreate(&ev1_));
+    UQ_CUDA(cudaMalloc(&d_const_, P_.h.arena_bytes));
+    UQ_CUDA(cudaMemcpy(d_const_, P_.arena.data(), P_.h.arena_bytes, cudaMemcpyHostToDevice));
+    rc = prepare();
+    if (rc) {
+        release();
+        return rc;
+    }
+    ticks_.assign(kMaxOps + 2, 0);
+    profiling_ = false;
+    ready_ = true;
+    return 0;
+}
+
+// ----------------------------------------------------------------------------------------
+// Lowering: one Step per plan op. Host-side parameter words are read from the plan arena;
+// device-side tables (weights, q blocks, LUTs) are used in place in the uploaded constants.
+int Engine::prepare() {
+    const Plan &P = P_;
+    const uint32_t nt = P.h.nt;
+    alias_.resize(nt);
+    std::iota(alias_.begin(), alias_.end(), 0);
+    steps_.clear();
+    for (uint32_t i = 0; i < P.h.no; i++) {
+        const Op o = P.ops[i];
+        const Tensor a = P.ts[o.a], b = P.ts[o.b], z = P.ts[o.out];
+        Step st;
+        st.op = i;
+        switch (o.code) {
+            case 5: {  // graph.c:408 -- a copy of identical bytes becomes a storage alias
+                int root = o.a;
+                while (alias_[root] != root) root = alias_[root];
+                alias_[o.out] = root;
+                st.run = nullptr;
+                break;
+            }
+            case 14: {
+                const int32_t *q = P.q(o.p[0]);
+                ConvGeom g{};
+                g.n = (int)a.d[0];
+                g.ih = (int)a.d[1], g.iw = (int)a.d[2], g.ic = q[16];
+                g.oh = q[10], g.ow = q[11], g.oc = q[17];
+                g.kh = q[0], g.kw = q[1], g.sh = q[2], g.sw = q[3], g.dh = q[4], g.dw = q[5], g.pt = q[6], g.pl = q[7];
+                g.xzp = q[12];
+                g.kp = q[18];
+                const int32_t *dq = reinterpret_cast<const int32_t *>(dconst(o.p[0]));
+                Requant r{dq + kHead, dq + kHead + g.oc, dq + kHead + 2 * g.oc,
+                          o.p[1] ? dconst(o.p[1] - 1) : nullptr, q[13], q[14], q[15]};
+                ConvTc *tc = nullptr;
+                int rc = conv_tc_prepare(P.s8(o.b), q, r.post, g, [this](size_t n) { return prep_alloc(n); }, &tc);
+                if (rc) return rc;
+                const int8_t *w = reinterpret_cast<const int8_t *>(dconst(o.b));
+                const uint32_t ta = o.a, tz = o.out;
+                if (tc) {
+                    std::shared_ptr<ConvTc> keep(tc, conv_tc_free);
+                    st.run = [keep, g, ta, tz](const BatchCtx &B, cudaStream_t s) {
+                        ConvGeom gb = g;
+                        gb.n = g.n * (int)B.images;
+                        conv_tc_launch(*keep, reinterpret_cast<const int8_t *>(B.ptr[ta]),
+                                       reinterpret_cast<int8_t *>(B.ptr[tz]), gb, s);
+                    };
+                } else {
+                    st.run = [g, r, w, ta, tz](const BatchCtx &B, cudaStream_t s) {
+                        ConvGeom gb = g;
+                        gb.n = g.n * (int)B.images;
+                        launch_conv_simt(reinterpret_cast<const int8_t *>(B.ptr[ta]), w,
+                                         reinterpret_cast<int8_t *>(B.ptr[tz]), gb, r, s);
+                    };
+                }
+                break;
+            }
+            case 15:
+            case 16: {
+                const int32_t *q = P.q(o.p[0]);
+                ConvGeom g{};
+                g.n = (int)a.d[0];
+                g.ih = (int)a.d[1], g.iw = (int)a.d[2], g.ic = q[16];
+                g.oh = q[10], g.ow = q[11], g.oc = q[17];
+                g.kh = q[0], g.kw = q[1], g.sh = q[2], g.sw = q[3], g.dh = q[4], g.dw = q[5], g.pt = q[6], g.pl = q[7];
+                g.xzp = q[12];
+                g.kp = q[18];
+                const uint32_t ta = o.a, tz = o.out;
+                if (o.code == 15) {
+                    const int32_t *dq = reinterpret_cast<const int32_t *>(dconst(o.p[0]));
+                    Requant r{dq + kHead, dq + kHead + g.oc, dq + kHead + 2 * g.oc,
+                              o.p[1] ? dconst(o.p[1] - 1) : nullptr, q[13], q[14], q[15]};
+                    const int8_t *w = reinterpret_cast<const int8_t *>(dconst(o.b));
+                    st.run = [g, r, w, ta, tz](const BatchCtx &B, cudaStream_t s) {
+                        ConvGeom gb = g;
+                        gb.n = g.n * (int)B.images;
+                        launch_depthwise(reinterpret_cast<const int8_t *>(B.ptr[ta]), w,
+                                         reinterpret_cast<int8_t *>(B.ptr[tz]), gb, r, s);
+                    };
+                } else {
+                    const int is_max = q[19], lo = q[14], hi = q[15];
+                    st.run = [g, is_max, lo, hi, ta, tz](const BatchCtx &B, cudaStream_t s) {
+                        ConvGeom gb = g;
+                        gb.n = g.n * (int)B.images;
+                        launch_pool(reinterpret_cast<const int8_t *>(B.ptr[ta]), reinterpret_cast<int8_t *>(B.ptr[tz]), gb,
+                                    is_max, lo, hi, s);
+                    };
+                }
+                break;
+            }
+            case 17: {
+                const int32_t *q = P.q(o.p[0]);
+                const int width = q[16], lo = q[14], hi = q[15];
+                const int32_t *table = reinterpret_cast<const int32_t *>(dconst(o.p[0])) + kHead;
+                const uint32_t ta = o.a, tz = o.out, abytes = a.bytes;
+                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                    launch_softmax_table(reinterpret_cast<const int8_t *>(B.ptr[ta]), reinterpret_cast<int8_t *>(B.ptr[tz]),
+                                         (size_t)abytes / width * B.images, width, table, lo, hi, s);
+                };
+                break;
+            }
+            case 28: {
+                const int width = P.q(o.b)[0];
+                const int32_t *dq = reinterpret_cast<const int32_t *>(dconst(o.b));
+                const uint32_t ta = o.a, tz = o.out, abytes = a.bytes;
+                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                    launch_softmax_exact(reinterpret_cast<const int8_t *>(B.ptr[ta]), reinterpret_cast<int8_t *>(B.ptr[tz]),
+                                         (size_t)abytes / width * B.images, width, dq, s);
+                };
+                break;
+            }
+            case 27: {
+                const int32_t *q = P.q(o.p[0]);
+                int32_t q7[7];
+                std::memcpy(q7, q, sizeof(q7));
+                const int m = (int)z.d[1], n = (int)z.d[2], k = (int)a.d[q[5] ? 1 : 2];
+                const uint32_t ta = o.a, tb = o.b, tz = o.out, d0 = z.d[0];
+                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                    int32_t qq[7];
+                    std::memcpy(qq, q7, sizeof(qq));
+                    launch_bmm(reinterpret_cast<const int8_t *>(B.ptr[ta]), reinterpret_cast<const int8_t *>(B.ptr[tb]),
+                               reinterpret_cast<int8_t *>(B.ptr[tz]), (size_t)d0 * B.images, m, n, k, qq, s);
+                };
+                break;
+            }
+            case 26: {
+                Shape5 in{}, out{};
+                in.rank = out.rank = (int)a.rank + 1;
+                in.d[0] = out.d[0] = 1;
+                uint32_t begin[5] = {0, 0, 0, 0, 0};
+                for (uint32_t d = 0; d < a.rank; d++) {
+                    in.d[d + 1] = a.d[d];
+                    out.d[d + 1] = z.d[d];
+                    begin[d + 1] = o.p[d];
+                }
+                const uint32_t ta = o.a, tz = o.out;
+                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                    Shape5 ib = in, ob = out;
+                    ib.d[0] = ob.d[0] = B.images;
+                    launch_slice(B.ptr[ta], B.ptr[tz], ib, ob, begin, s);
+                };
+                break;
+            }
+            case 25: {
+                int32_t q7[7];
+                std::memcpy(q7, P.q(o.p[0]), sizeof(q7));
+                const uint32_t ta = o.a, tb = o.b, tz = o.out, zb = z.bytes;
+                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                    int32_t qq[7];
+                    std::memcpy(qq, q7, sizeof(qq));
+                    launch_mul(reinterpret_cast<const int8_t *>(B.ptr[ta]), reinterpret_cast<const int8_t *>(B.ptr[tb]),
+                               reinterpret_cast<int8_t *>(B.ptr[tz]), (size_t)zb * B.images, qq, s);
+                };
+                break;
+            }
+            case 24: {
+                int32_t q5[5];
+                std::memcpy(q5, P.q(o.b), sizeof(q5));
+                const uint32_t ta = o.a, tz = o.out, d0 = a.d[0], ch = a.d[3];
+                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                    int32_t qq[5];
+                    std::memcpy(qq, q5, sizeof(qq));
+                    launch_mean(reinterpret_cast<const int8_t *>(B.ptr[ta]), reinterpret_cast<int8_t *>(B.ptr[tz]),
+                                (size_t)d0 * B.images, (int)ch, qq, s);
+                };
+                break;
+            }
+            case 23: {
+                int32_t pads[8];
+                std::memcpy(pads, P.q(o.b), sizeof(pads));
+                uint32_t ad[4], zd[4];
+                for (int d = 0; d < 4; d++) ad[d] = a.d[d], zd[d] = z.d[d];
+                const int8_t value = (int8_t)(int32_t)o.p[0];
+                const uint32_t ta = o.a, tz = o.out;
+                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                    launch_pad(B.ptr[ta], B.ptr[tz], (int)B.images, ad, zd, pads, value, s);
+                };
+                break;
+            }
+            case 22: {
+                const uint8_t *table = dconst(o.b);
+                const unsigned flip = a.type == 3 ? 128u : 0u;
+                const uint32_t ta = o.a, tz = o.out, ab = a.bytes;
+                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                    launch_lut(B.ptr[ta], B.ptr[tz], (size_t)ab * B.images, table, flip, s);
+                };
+                break;
+            }
+            case 21: {
+                const uint32_t *offsets = reinterpret_cast<const uint32_t *>(dconst(o.b));
+                const uint32_t ta = o.a, tz = o.out;
+                const int n = (int)a.d[0], ih = (int)a.d[1], iw = (int)a.d[2], c = (int)a.d[3], oh = (int)z.d[1],
+                          ow = (int)z.d[2];
+                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                    launch_resize(B.ptr[ta], B.ptr[tz], n * (int)B.images, ih, iw, c, oh, ow, offsets, s);
+                };
+                break;
+            }
+            case 20: {
+                const unsigned axis = o.p[0];
+                size_t outer = 1, inner = 1;
+                for (unsigned d = 0; d < axis; d++) outer *= a.d[d];
+                for (unsigned d = axis + 1; d < a.rank; d++) inner *= a.d[d];
+                const size_t ac = a.d[axis] * inner, bc = b.d[axis] * inner;
+                const uint32_t ta = o.a, tb = o.b, tz = o.out;
+                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                    launch_concat(B.ptr[ta], B.ptr[tb], B.ptr[tz], outer * B.images, ac, bc, s);
+                };
+                break;
+            }
+            case 19: {
+                const uint32_t *list = reinterpret_cast<const uint32_t *>(P.bytes(o.b));
+                std::vector<uint32_t> ids(list, list + b.bytes / 4);
+                const uint32_t tz = o.out, zb = z.bytes;
+                std::vector<uint32_t> sizes, offs;
+                uint32_t off = 0;
+                for (uint32_t id : ids) {
+                    sizes.push_back(P.ts[id].bytes);
+                    offs.push_back(off);
+                    off += P.ts[id].bytes;
+                }
+                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                    Segments sg{};
+                    sg.count = (int)ids.size();
+                    for (size_t j = 0; j < ids.size(); j++) {
+                        sg.src[j] = B.ptr[ids[j]];
+                        sg.bytes[j] = sizes[j];
+                        sg.dst_offset[j] = offs[j];
+                    }
+                    launch_pack(sg, B.ptr[tz], zb, (int)B.images, s);
+                };
+                break;
+            }
+            case 18: {
+                const int32_t *dq = reinterpret_cast<const int32_t *>(dconst(o.p[0]));
+                const uint32_t ta = o.a, tb = o.b, tz = o.out, zb = z.bytes;
+                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                    launch_add(reinterpret_cast<const int8_t *>(B.ptr[ta]), reinterpret_cast<const int8_t *>(B.ptr[tb]),
+                               reinterpret_cast<int8_t *>(B.ptr[tz]), (size_t)zb * B.images, dq, s);
+                };
+                break;
+            }
+            case 10: {
+                Shape5 in{};
+                in.rank = (int)a.rank + 1;
+                in.d[0] = 1;
+                int perm[5] = {0, 0, 0, 0, 0};
+                for (uint32_t d = 0; d < a.rank; d++) {
+                    in.d[d + 1] = a.d[d];
+                    perm[d + 1] = (int)o.p[d] + 1;
+                }
+                const int elem = (int)type_width(a.type);
+                const uint32_t ta = o.a, tz = o.out;
+                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                    Shape5 ib = in;
+                    ib.d[0] = B.images;
+                    launch_permute(B.ptr[ta], B.ptr[tz], ib, perm, elem, s);
+                };
+                break;
+            }
+            default:
+                // Legacy fp32 / MatMulInteger opcodes (1-4, 6-9, 11-13) are outside the INT8
+                // vision path this backend implements.
+                set_error("opcode " + std::to_string(o.code) + " is not implemented by the CUDA backend");
+                return 19;
+        }
+        steps_.push_back(std::move(st));
+    }
+    return 0;
+}
+
+// ----------------------------------------------------------------------------------------
+// Batched arena: storage groups (copy aliases share one group) placed by lifetime. A group
+// lives from its first producer to its last reader; groups whose lifetimes intersect never
+// share bytes. Constants read as activations are replicated per image once, up front.
+int Engine::plan_arena(BatchCtx &B) {
+    const Plan &P = P_;
+    const uint32_t nt = P.h.nt;
+    std::vector<int> root(nt);
+    for (uint32_t t = 0; t < nt; t++) {
+        int r = (int)t;
+        while (alias_[r] != r) r = alias_[r];
+        root[t] = r;
+    }
+    // Constants used as activation operands need per-image copies.
+    std::vector<uint8_t> replicate(nt, 0);
+    auto mark = [&](uint32_t t) {
+        if (P.ts[t].flags) replicate[root[t]] = 1;
+    };
+    for (const Op &o : P.ops) {
+        mark(o.a);
+        if (o.code == 18 || o.code == 20 || o.code == 25 || o.code == 27) mark(o.b);
+        if (o.code == 19) {
+            const uint32_t *list = reinterpret_cast<const uint32_t *>(P.bytes(o.b));
+            for (uint32_t j = 0; j < P.ts[o.b].bytes / 4; j++) mark(list[j]);
+        }
+    }
+    mark(P.h.output);
+    struct Group {
+        int root;
+        size_t size;
+        int birth, death;
+        size_t offset;
+    };
+    std::vector<int> gid(nt, -1);
+    std::vector<Group> groups;
+    for (uint32_t t = 0; t < nt; t++) {
+        const int r = root[t];
+        const bool is_const = P.ts[r].flags != 0;
+        if (is_const && !replicate[r]) continue;
+        if (gid[r] < 0) {
+            gid[r] = (int)groups.size();
+            groups.push_back({r, align_up((size_t)P.ts[r].bytes * B.images, kAlign), is_const ? -1 : P.birth[r],
+                              is_const ? (int)P.h.no : P.death[r], 0});
+        }
+        Group &g = groups[gid[r]];
+        if (!is_const) {
+            g.birth = std::min(g.birth, P.birth[t]);
+            g.death = std::max(g.death, P.death[t]);
+        }
+        gid[t] = gid[r];
+    }
+    std::vector<int> order(groups.size());
+    std::iota(order.begin(), order.end(), 0);
+    std::sort(order.begin(), order.end(), [&](int x, int y) { return groups[x].size > groups[y].size; });
+    std::vector<int> placed;
+    size_t total = 0;
+    for (int gi : order) {
+        Group &g = groups[gi];
+        std::vector<std::pair<size_t, size_t>> busy;
+        for (int pj : placed) {
+            const Group &h = groups[pj];
+            if (g.birth <= h.death && h.birth <= g.death) busy.push_back({h.offset, h.offset + h.size});
+        }
+        std::sort(busy.begin(), busy.end());
+        size_t off = 0;
+        for (auto &iv : busy) {
+            if (off + g.size <= iv.first) break;
+            off = std::max(off, iv.second);
+        }
+        g.offset = off;
+        total = std::max(total, off + g.size);
+        placed.push_back(gi);
+    }
+    B.arena_bytes = std::max<size_t>(total, kAlign);
+    UQ_CUDA(cudaMalloc(&B.arena, B.arena_bytes));
+    B.ptr.assign(nt, nullptr);
+    for (uint32_t t = 0; t < nt; t++) {
+        if (gid[t] >= 0) B.ptr[t] = B.arena + groups[gid[t]].offset;
+        else B.ptr[t] = d_const_ + P.ts[t].offset;
+    }
+    for (const Group &g : groups) {
+        if (!P.ts[g.root].flags) continue;
+        const size_t bytes = P.ts[g.root].bytes;
+        for (uint32_t i = 0; i < B.images; i++)
+            UQ_CUDA(cudaMemcpyAsync(B.arena + g.offset + i * bytes, d_const_ + P.ts[g.root].offset, bytes,
+                                    cudaMemcpyDeviceToDevice, stream_));
+    }
+    UQ_CUDA(cudaStreamSynchronize(stream_));
+    return 0;
+}
+
+int Engine::run_steps(const BatchCtx &B, cudaStream_t s, bool profile) {
+    std::vector<cudaEvent_t> evs;
+    if (profile) {
+        evs.resize(steps_.size() + 1);
+        for (auto &e : evs) UQ_CUDA(cudaEventCreate(&e));
+        UQ_CUDA(cudaEventRecord(evs[0], s));
+    }
+    for (size_t i = 0; i < steps_.size(); i++) {
+        if (steps_[i].run) steps_[i].run(B, s);
+        if (profile) UQ_CUDA(cudaEventRecord(evs[i + 1], s));
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        set_error(std::string("kernel launch: ") + cudaGetErrorString(e));
+        return 2001;
+    }
+    if (profile) {
+        UQ_CUDA(cudaEventSynchronize(evs.back()));
+        for (size_t i = 0; i < steps_.size(); i++) {
+            float ms = 0.f;
+            UQ_CUDA(cudaEventElapsedTime(&ms, evs[i], evs[i + 1]));
+            ticks_[2 + steps_[i].op] += (uint64_t)(ms * 1e6);
+        }
+        float total = 0.f;
+        UQ_CUDA(cudaEventElapsedTime(&total, evs[0], evs.back()));
+        ticks_[0] += 1;
+        ticks_[1] += (uint64_t)(total * 1e6);
+        for (auto &ev : evs) cudaEventDestroy(ev);
+    }
+    return 0;
+}
+
+int Engine::capture(BatchCtx &B) {
+    UQ_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+    int rc = run_steps(B, stream_, false);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(stream_, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) {
+        set_error(std::string("graph capture: ") + cudaGetErrorString(e));
+        return 2001;
+    }
+    B.graph = g;
+    UQ_CUDA(cudaGraphInstantiate(&B.exec, g, 0));
+    size_t n = 0;
+    UQ_CUDA(cudaGraphGetNodes(g, nullptr, &n));
+    std::vector<cudaGraphNode_t> nodes(n);
+    UQ_CUDA(cudaGraphGetNodes(g, nodes.data(), &n));
+    int kernels = 0;
+    for (auto nd : nodes) {
+        cudaGraphNodeType ty;
+        UQ_CUDA(cudaGraphNodeGetType(nd, &ty));
+        kernels += ty == cudaGraphNodeTypeKernel;
+    }
+    B.kernel_nodes = kernels;
+    return 0;
+}
+
+int Engine::batch(uint32_t images, BatchCtx **out) {
+    if (!ready_) return 22;
+    if (!images) return 22;
+    auto it = batches_.find(images);
+    if (it != batches_.end()) {
+        *out = it->second.get();
+        return 0;
+    }
+    UQ_CUDA(cudaSetDevice(device_));
+    auto B = std::make_unique<BatchCtx>();
+    B->images = images;
+    int rc = plan_arena(*B);
+    if (!rc) rc = capture(*B);
+    if (rc) {
+        if (B->exec) cudaGraphExecDestroy(B->exec);
+        if (B->graph) cudaGraphDestroy(B->graph);
+        if (B->arena) cudaFree(B->arena);
+        return rc;
+    }
+    *out = B.get();
+    batches_[images] = std::move(B);
+    return 0;
+}
+
+int Engine::run_host(const void *in, void *out, uint32_t images) {
+    if (!ready_ || !in || !out) return 22;
+    BatchCtx *B = nullptr;
+    int rc = batch(images, &B);
+    if (rc) return rc;
+    UQ_CUDA(cudaSetDevice(device_));
+    const size_t ni = (size_t)input_bytes() * images, no = (size_t)output_bytes() * images;
+    UQ_CUDA(cudaEventRecord(ev0_, stream_));
+    UQ_CUDA(cudaMemcpyAsync(B->ptr[P_.h.input], in, ni, cudaMemcpyHostToDevice, stream_));
+    if (profiling_) rc = run_steps(*B, stream_, true);
+    else if (cudaGraphLaunch(B->exec, stream_) != cudaSuccess) {
+        set_error("graph launch failed");
+        rc = 2001;
+    }
+    if (rc) return rc;
+    UQ_CUDA(cudaMemcpyAsync(out, B->ptr[P_.h.output], no, cudaMemcpyDeviceToHost, stream_));
+    UQ_CUDA(cudaEventRecord(ev1_, stream_));
+    cudaError_t e = cudaStreamSynchronize(stream_);
+    if (e != cudaSuccess) {
+        set_error(std::string("inference: ") + cudaGetErrorString(e));
+        return 2001;
+    }
+    UQ_CUDA(cudaEventElapsedTime(&last_ms_, ev0_, ev1_));
+    last_images_ = images;
+    return 0;
+}
+
+int Engine::buffers(uint32_t images, void **d_in, void **d_out) {
+    BatchCtx *B = nullptr;
+    int rc = batch(images, &B);
+    if (rc) return rc;
+    if (d_in) *d_in = B->ptr[P_.h.input];
+    if (d_out) *d_out = B->ptr[P_.h.output];
+    return 0;
+}
+
+int Engine::launch(uint32_t images) {
+    BatchCtx *B = nullptr;
+    int rc = batch(images, &B);
+    if (rc) return rc;
+    UQ_CUDA(cudaSetDevice(device_));
+    UQ_CUDA(cudaGraphLaunch(B->exec, stream_));
+    last_images_ = images;
+    return 0;
+}
+
+int Engine::synchronize() {
+    if (!stream_) return 22;
+    UQ_CUDA(cudaSetDevice(device_));
+    UQ_CUDA(cudaStreamSynchronize(stream_));
+    return 0;
+}
+
+int Engine::time_launches(uint32_t images, uint32_t iterations, float *ms) {
+    BatchCtx *B = nullptr;
+    int rc = batch(images, &B);
+    if (rc) return rc;
+    UQ_CUDA(cudaSetDevice(device_));
+    UQ_CUDA(cudaStreamSynchronize(stream_));
+    UQ_CUDA(cudaEventRecord(ev0_, stream_));
+    for (uint32_t i = 0; i < iterations; i++) UQ_CUDA(cudaGraphLaunch(B->exec, stream_));
+    UQ_CUDA(cudaEventRecord(ev1_, stream_));
+    UQ_CUDA(cudaEventSynchronize(ev1_));
+    UQ_CUDA(cudaEventElapsedTime(ms, ev0_, ev1_));
+    last_images_ = images;
+    return 0;
+}
+
+int Engine::kernel_count(uint32_t images) {
+    BatchCtx *B = nullptr;
+    int rc = batch(images, &B);
+    if (rc) return -rc;
+    return B->kernel_nodes;
+}
+
+int Engine::snapshot(uint32_t tensor, void *out, uint32_t bytes) {
+    if (!ready_ || tensor >= P_.h.nt || !out || bytes != P_.ts[tensor].bytes) return 22;
+    auto it = batches_.find(last_images_ ? last_images_ : 1);
+    const uint8_t *src = nullptr;
+    if (it != batches_.end()) src = it->second->ptr[tensor];
+    else src = d_const_ + P_.ts[tensor].offset;
+    UQ_CUDA(cudaSetDevice(device_));
+    UQ_CUDA(cudaMemcpy(out, src, bytes, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+int Engine::profile_batch(uint32_t images, uint32_t iterations, uint64_t *op_ns, uint32_t n, float *total_ms) {
+    BatchCtx *B = nullptr;
+    int rc = batch(images, &B);
+    if (rc) return rc;
+    if (!op_ns || n < P_.h.no) return 22;
+    UQ_CUDA(cudaSetDevice(device_));
+    std::vector<uint64_t> saved = ticks_;
+    std::fill(ticks_.begin(), ticks_.end(), 0);
+    for (uint32_t it = 0; it < iterations && !rc; it++) rc = run_steps(*B, stream_, true);
+    if (!rc) {
+        for (uint32_t i = 0; i < P_.h.no; i++) op_ns[i] = ticks_[2 + i];
+        if (total_ms) *total_ms = (float)(ticks_[1] / 1e6);
+    }
+    ticks_ = saved;
+    return rc;
+}
+
+int Engine::profile(uint32_t command, void *out, uint32_t bytes) {
+    if (!ready_ || command > 2 || !out ||
+        (bytes != (kMaxOps + 2) * sizeof(uint64_t) && !(P_.h.no <= 128 && bytes == 130 * 8)))
+        return 22;
+    if (command == 1) std::fill(ticks_.begin(), ticks_.end(), 0);
+    if (command < 2) profiling_ = command == 1;
+    std::memcpy(out, ticks_.data(), bytes);
+    return 0;
+}
+
+}  // namespace uq

@@ -1,0 +1,101 @@
+// engine.hpp -- device-side executor of one loaded plan.
+//
+// Replaces the reference's run_inner dispatch loop (runtime/graph.c:285-423) and its static
+// 16 MiB arena. Constants are uploaded once; activations live in a per-batch-size device
+// arena laid out by a lifetime planner (each activation tensor holds `images` back-to-back
+// copies of its batch-1 layout); the op sequence for a batch size is captured once into a
+// CUDA graph and replayed.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <functional>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "plan.hpp"
+
+namespace uq {
+
+struct BatchCtx;
+
+// One plan op lowered to device work. `run` enqueues its kernels on the stream.
+struct Step {
+    uint32_t op = 0;
+    std::function<void(const BatchCtx &, cudaStream_t)> run;
+};
+
+struct BatchCtx {
+    uint32_t images = 0;
+    uint8_t *arena = nullptr;            // device activation arena
+    size_t arena_bytes = 0;
+    std::vector<uint8_t *> ptr;          // device address of each tensor (image 0)
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    int kernel_nodes = 0;
+    uint8_t *host_in = nullptr, *host_out = nullptr;  // pinned staging for pageable callers
+};
+
+class Engine {
+   public:
+    Engine() = default;
+    ~Engine();
+    Engine(const Engine &) = delete;
+    Engine &operator=(const Engine &) = delete;
+
+    // Validate + prepare. Returns 0 or a reference loader code; 2001/2002 for CUDA failures.
+    int load(const void *plan, uint32_t bytes, int device);
+    bool ready() const { return ready_; }
+    uint32_t input_bytes() const { return ready_ ? P_.ts[P_.h.input].bytes : 0; }
+    uint32_t output_bytes() const { return ready_ ? P_.ts[P_.h.output].bytes : 0; }
+    const Plan &plan() const { return P_; }
+    int device() const { return device_; }
+    cudaStream_t stream() const { return stream_; }
+
+    // Host buffers; `pinned` skips the staging copy. Synchronous.
+    int run_host(const void *in, void *out, uint32_t images);
+    // Device buffers of the batch context (input tensor, output tensor of image 0).
+    int buffers(uint32_t images, void **d_in, void **d_out);
+    int launch(uint32_t images);   // async on stream_
+    int synchronize();
+    int time_launches(uint32_t images, uint32_t iterations, float *ms);
+    int kernel_count(uint32_t images);
+    float last_ms() const { return last_ms_; }
+    int snapshot(uint32_t tensor, void *out, uint32_t bytes);
+    int profile(uint32_t command, void *out, uint32_t bytes);
+    // Eager (non-graph) passes with a CUDA event after every op; accumulates per-op
+    // nanoseconds into op_ns[0..no) and returns the summed pass time in *total_ms.
+    int profile_batch(uint32_t images, uint32_t iterations, uint64_t *op_ns, uint32_t n, float *total_ms);
+
+   private:
+    int prepare();
+    int batch(uint32_t images, BatchCtx **out);
+    int plan_arena(BatchCtx &b);
+    int capture(BatchCtx &b);
+    int run_steps(const BatchCtx &b, cudaStream_t s, bool profile);
+    void release();
+    uint8_t *dconst(uint32_t tensor) const { return d_const_ + P_.ts[tensor].offset; }
+    void *prep_alloc(size_t bytes);   // device memory owned by the engine for prepared data
+
+    Plan P_;
+    bool ready_ = false;
+    int device_ = 0;
+    cudaStream_t stream_ = nullptr;
+    uint8_t *d_const_ = nullptr;
+    std::vector<void *> prep_;
+    std::vector<Step> steps_;
+    std::vector<int> alias_;             // tensor -> storage root (copy ops alias their source)
+    std::map<uint32_t, std::unique_ptr<BatchCtx>> batches_;
+    cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
+    float last_ms_ = 0.f;
+    uint32_t last_images_ = 0;
+    bool profiling_ = false;
+    std::vector<uint64_t> ticks_;        // [0] runs, [1] total ns, [2+i] op ns
+};
+
+// Records the last CUDA failure for ug_last_error().
+void set_error(const std::string &msg);
+const char *last_error();
+
+}  // namespace uq
