@@ -182,7 +182,7 @@ def op_traffic(plan, images):
             q = np.frombuffer(plan, dtype="<i4", count=20, offset=meta + ts[o[4]][0])
             kh, kw, oh, ow, ic, oc = q[0], q[1], q[10], q[11], q[16], q[17]
             k = kh * kw * (1 if code == 15 else ic)
-            mac = int(ts[z][4] * oh * ow) * oc * k * images
+            mac = int(ts[z][4]) * int(oh) * int(ow) * int(oc) * int(k) * images
             byt += bbytes + (20 + 3 * oc) * 4
         elif code in (18, 20, 25, 27):
             byt += bbytes * (1 if const_b else images)
@@ -223,6 +223,11 @@ def roofline(lib, handle, plan, images, iters, peaks, kernel_names):
     roof.update({"kernel": top, "traffic": None, "launches_per_step": d["launches"],
                  "ms_per_step": round(d["ns"] / 1e6, 4), "int8_tops": round(tops, 1),
                  "algorithmic_bytes_per_step": d["bytes"], "share_of_eager_step": round(d["ns"] / 1e6 / total.value * iters, 3)})
+    top_ops = sorted(range(n_ops), key=lambda i: -ns[i])[:12]
+    roof["top_ops"] = [{"op": i, "code": traffic[i]["code"], "ms": round(ns[i] / iters / 1e6, 4),
+                        "GB/s": round(traffic[i]["bytes"] / (ns[i] / iters * 1e-9) / 1e9, 1) if ns[i] else None,
+                        "TOPS": round(traffic[i]["ops"] / (ns[i] / iters * 1e-9) / 1e12, 1) if ns[i] else None}
+                       for i in top_ops]
     breakdown = {k: {"ms": round(v["ns"] / 1e6, 4), "GB/s": round(v["bytes"] / (v["ns"] * 1e-9) / 1e9, 1) if v["ns"] else None,
                      "TOPS": round(v["ops"] / (v["ns"] * 1e-9) / 1e12, 1) if v["ns"] else None}
                  for k, v in sorted(per_kind.items(), key=lambda kv: -kv[1]["ns"])}

@@ -8,7 +8,7 @@
 #include <cstdlib>
 #include <mutex>
 
-#include "../../include/unoq_cuda.h"
+#include "unoq_cuda.h"
 #include "engine.hpp"
 
 namespace {

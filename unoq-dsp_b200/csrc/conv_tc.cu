@@ -1,16 +1,963 @@
-// conv_tc.cu -- placeholder until the tcgen05 kernel lands: every conv takes the CUDA-core path.
+// conv_tc.cu -- INT8 implicit-GEMM convolution on the 5th-generation tensor cores (sm_100a).
+//
+// Computes plan code 14 (runtime/qnn.c:1101-1227) as Y[m, n] = requant(sum_k A[m, k] W[n, k]):
+// m = output pixel, n = output channel, k = (ky, kx, ic) reduction index (tflite.py:155 order).
+//
+// One persistent CTA per SM loops over 128-pixel M tiles of one N tile (grid.y = N tiles):
+//   * W: the N tile's weights, prepared on the host in the UMMA K-major SWIZZLE_128B layout
+//     (8-row x 128-byte atoms, 16-byte chunks XOR-swizzled by row), copied to shared memory
+//     once and kept resident.
+//   * A (warps 0-3): the im2col rows of a tile, 128 reduction bytes per pipeline stage, built
+//     straight into the swizzled layout.
+//       - 16-byte channel blocks (ic % 16 == 0): cp.async per (pixel, 16 channels); taps outside
+//         the image copy 16 bytes of the input zero point from a tiny global fill row -- the
+//         value the reference feeds its dot product there (qnn.c:1166-1168) -- so no border
+//         correction is needed. A warp signals a stage a few stages after issuing it, once its
+//         copies have landed, so several stages of copies stay in flight per thread.
+//       - other channel counts (the 3-channel RGB stem, ic = 8): the input rows a tile touches
+//         (a "band") are copied to shared memory with 16-byte cp.async, double-buffered across
+//         tiles, and each thread then assembles its pixel's K bytes from the band.
+//   * warp 12 (one thread) issues tcgen05.mma.kind::i8 (s8 x s8 -> s32, M=128, N=BN, K=32)
+//     into one of two TMEM accumulators, so the epilogue of tile i overlaps the MMAs of i+1.
+//   * warps 4-11 read the accumulator with tcgen05.ld (thread = pixel row, 16 channels per load,
+//     two warps per TMEM lane quarter on alternating chunks), requantise with the exact
+//     branch-free form of the reference's `scale` (make_epilogue), apply the optional post
+//     table, stage the int8 tile in shared memory and write it out with coalesced stores.
+//
+// Reference arithmetic: the reference multiplies u8 columns (x ^ 0x80) by s8 weights and adds a
+// corrected bias; with s8 columns the same sum is  sum x*w + 128*sum(w) + xzp*sum(w_kpad), which
+// the host folds into the epilogue constants, so results are bit-identical.
+//
+// Every wait (mbarrier phases, including the ones that stand in for sub-CTA barriers) is bounded
+// by about 2 s of SM clock; on expiry the kernel records a site code in g_conv_tc_error, drains its
+// MMAs, frees its TMEM and exits.
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <numeric>
+#include <vector>
+
+#include <cuda.h>
+
 #include "conv_tc.cuh"
+#include "plan.hpp"
 
 namespace uq {
 
-struct ConvTc {};
+__device__ int g_conv_tc_error = 0;
 
-int conv_tc_prepare(const int8_t *, const int32_t *, const uint8_t *, const ConvGeom &,
-                    const std::function<void *(size_t)> &, ConvTc **out) {
+namespace {
+
+constexpr int kBM = 128;              // pixels per tile = TMEM lanes
+constexpr int kBK = 128;              // reduction bytes per stage (one 128-byte swizzle row)
+constexpr int kStageBytes = kBM * kBK;
+constexpr int kProducerWarps = 4;
+constexpr int kEpilogueWarps = 8;     // two warps per TMEM lane quarter, alternating 16-column chunks
+constexpr int kMmaWarp = kProducerWarps + kEpilogueWarps;
+constexpr int kThreads = (kMmaWarp + 1) * 32;
+constexpr int kProducers = kProducerWarps * 32;
+constexpr int kEpilogues = kEpilogueWarps * 32;
+constexpr int kMaxSmem = 227 * 1024;
+constexpr int kWeightBudget = 96 * 1024;
+
+// Per-output-channel epilogue constants (32 bytes): one branch-free form covers every
+// channel (see make_epilogue):  a = (acc << ls) + bs;  p = a*m + k;  p -= 2^31 if acc <= cut;
+// y = (int32)(p >> sh) + zadd.
+struct __align__(32) EpiChan {
+    long long k;
+    int m, cut, ls, bs, sh, zadd;
+};
+
+enum Mode { kPointwise = 0, kGather16 = 1, kBand = 2 };
+
+struct Params {
+    CUtensorMap ymap;          // output [M rows][oc] int8, box {min(bn,128), 128}, swizzled (TMA store)
+    const int8_t *x;
+    int8_t *y;
+    const int8_t *w;           // [n_tiles][kc][BN x 128] swizzled
+    const EpiChan *epi;        // [n_tiles * BN]
+    const uint8_t *post;       // 256 bytes or null
+    const int *tab;            // band mode taps: (ky*dh) << 20 | (kx*dw) << 10 | c, per k < K
+    const int8_t *fill;        // 16 bytes of the input zero point
+    long long x_bytes;         // bytes of the whole (batched) input tensor
+    int M;                     // total output pixels
+    int ih, iw, ic, oh, ow, oc;
+    int kh, kw, sh, sw, dh, dw, pt, pl;
+    int K;                     // kh*kw*ic (unpadded)
+    int kc;                    // reduction stages per tile
+    int bn;                    // N tile width (multiple of 16, <= 256)
+    int stages;
+    int lo, hi;
+    int xzp;
+    int tmem_cols;
+    int mode;
+    int band_bytes;            // per band buffer (band mode)
+    int epi_mode;              // EpiMode
+    int n_acc;                 // TMEM accumulators in rotation (2 or 4)
+    int store_tma;             // 1: staged tile leaves by TMA tensor store; 0: cooperative stores
+    int box;                   // TMA box inner bytes = min(bn, 128)
+    int swz;                   // staging swizzle: 0 none (16 B rows), 1 = 32 B, 2 = 64 B, 3 = 128 B span
+};
+
+// One staging buffer of the output tile: 128 rows, padded rows for cooperative stores or
+// swizzled sub-tiles for the TMA store; 1024-byte aligned so swizzle atoms line up.
+__host__ __device__ inline size_t out_stride(int bn) { return ((size_t)kBM * (bn + 16) + 1023) & ~(size_t)1023; }
+
+// Shared-memory carve-up, identical on host (sizing) and device.
+struct Layout {
+    size_t a, b, out, band, epi, lut, tab, bars, total;
+    __host__ __device__ Layout(int stages, int kc, int bn, int band_bytes) {
+        size_t o = 0;
+        a = o;
+        o += (size_t)stages * kStageBytes;
+        b = o;
+        o += (size_t)kc * bn * kBK;
+        out = o;
+        o += 2 * out_stride(bn);
+        band = o;
+        o += 2 * (size_t)((band_bytes + 15) & ~15);
+        epi = (o + 31) & ~(size_t)31;
+        o = epi + (size_t)bn * sizeof(EpiChan);
+        lut = o;
+        o += 256;
+        tab = o;
+        o += 4 * kBK;
+        bars = (o + 7) & ~(size_t)7;
+        o = bars + (size_t)(2 * stages + 14) * 8 + 16;
+        total = o + 1024;  // base alignment slack
+    }
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar) : "memory");
+}
+
+// Test a phase; while it is incomplete the thread may be suspended for up to `hint_ns`, and it
+// resumes as soon as the phase completes. Without a hint the hardware's default limit is short
+// and waiting warps would spin, taking issue slots from the warps doing the work.
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity, uint32_t hint_ns = 0) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait bound: 4e9 SM cycles (about 2 s at the B200's 1.9-2 GHz boost clock).
+constexpr long long kTimeoutCycles = 4000000000ll;
+
+// Bounded wait: returns false (and records `code`) if the phase does not complete in time or
+// another role of this CTA already gave up.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort, int code) {
+    constexpr uint32_t kHintNs = 200000;  // one suspension of at most 0.2 ms per poll
+    if (mbar_try_wait(bar, parity, kHintNs)) return true;
+    const long long start = clock64();
+    while (true) {
+        if (mbar_try_wait(bar, parity, kHintNs)) return true;
+        if (*abort) return false;
+        if (clock64() - start > kTimeoutCycles) {
+            *abort = 1;
+            atomicCAS(&g_conv_tc_error, 0, code);
+            return false;
+        }
+    }
+}
+
+// A barrier among the warps of one role, built on an mbarrier so that it is bounded: each warp
+// arrives once per round (lane 0, after the warp has converged) and every lane waits for the
+// round's phase. One arrival per warp keeps the shared-memory atomics on the barrier word few.
+__device__ __forceinline__ bool role_sync(uint32_t bar, unsigned &round, volatile int *abort, int code) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+    const bool ok = mbar_wait(bar, round & 1u, abort, code);
+    round++;
+    return ok;
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// cp.async.wait_group with a run-time depth (the instruction takes an immediate).
+__device__ __forceinline__ void cp_async_wait_dyn(int n) {
+    switch (n) {
+        case 0: cp_async_wait<0>(); break;
+        case 1: cp_async_wait<1>(); break;
+        case 2: cp_async_wait<2>(); break;
+        default: cp_async_wait<3>(); break;
+    }
+}
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void st_shared16(uint32_t dst, uint4 v) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+// UMMA shared-memory descriptor: K-major, SWIZZLE_128B, 8-row atoms 1024 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+    return (uint64_t)((addr >> 4) & 0x3FFF) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor for kind::i8: s32 accumulate, signed A and B, both K-major.
+__device__ __forceinline__ uint32_t instr_desc(int bn) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
+// Wait for this thread's outstanding tcgen05.ld; the registers are tied in as read-write
+// operands so no use of them can be scheduled before the wait.
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+                 :
+                 : "memory");
+}
+
+}  // namespace
+
+__host__ __device__ __forceinline__ int32_t epilogue_one(int32_t acc, const EpiChan &e, int lo, int hi) {
+    const int32_t a = (int32_t)(((uint32_t)acc << e.ls) + (uint32_t)e.bs);
+    long long p = (long long)a * e.m + e.k;
+    p -= (long long)(acc <= e.cut) << 31;
+    const int32_t v = (int32_t)(p >> e.sh) + e.zadd;
+    return v < lo ? lo : (v > hi ? hi : v);
+}
+
+namespace {
+
+// Epilogue requantisation modes, chosen per layer on the host (all exact, see make_epilogue):
+//   kRelu    every channel has -15 <= shift <= -1 and the clamp floor lo >= yzp, so the tie
+//            correction for negative high products can never survive the clamp:
+//            y = clamp((hi32(acc*m + k)) >> (sh - 32));
+//   kTies    same shifts, lo < yzp: subtract 2^31 first when acc <= cut;
+//   kGeneral any channel with a pre-shift (shift >= 0) or shift < -15: full form.
+enum EpiMode { kRelu = 0, kTies = 1, kGeneral = 2 };
+
+// Per-channel constants in shared memory as structure-of-arrays so 16 columns load as
+// 128-bit broadcast vectors.
+struct EpiSoA {
+    const long long *k;
+    const int *m, *cut, *sh, *ls, *bs, *zadd;
+};
+
+template <int EPI>
+__device__ __forceinline__ uint4 epilogue_chunk(const uint32_t (&r)[16], const EpiSoA &E, const uint8_t *lut, int c0,
+                                                int lo, int hi) {
+    uint32_t packed[4] = {0, 0, 0, 0};
+    const longlong2 *K2 = reinterpret_cast<const longlong2 *>(E.k + c0);
+    const int4 *M4 = reinterpret_cast<const int4 *>(E.m + c0);
+    const int4 *S4 = reinterpret_cast<const int4 *>(E.sh + c0);
+    const int4 *C4 = reinterpret_cast<const int4 *>(E.cut + c0);
+    const int4 *L4 = reinterpret_cast<const int4 *>(E.ls + c0);
+    const int4 *B4 = reinterpret_cast<const int4 *>(E.bs + c0);
+    const int4 *Z4 = reinterpret_cast<const int4 *>(E.zadd + c0);
+#pragma unroll
+    for (int g = 0; g < 4; g++) {
+        const int4 mv = M4[g], sv = S4[g];
+        const longlong2 ka = K2[2 * g], kb = K2[2 * g + 1];
+        int4 cv = make_int4(0, 0, 0, 0), lv = cv, bv = cv, zv = cv;
+        if (EPI >= kTies) cv = C4[g];
+        if (EPI == kGeneral) {
+            lv = L4[g];
+            bv = B4[g];
+            zv = Z4[g];
+        }
+        const int mm[4] = {mv.x, mv.y, mv.z, mv.w}, ss[4] = {sv.x, sv.y, sv.z, sv.w};
+        const int cc[4] = {cv.x, cv.y, cv.z, cv.w}, ll[4] = {lv.x, lv.y, lv.z, lv.w};
+        const int bb[4] = {bv.x, bv.y, bv.z, bv.w}, zz[4] = {zv.x, zv.y, zv.z, zv.w};
+        const long long kk[4] = {ka.x, ka.y, kb.x, kb.y};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int32_t acc = (int32_t)r[g * 4 + i];
+            int32_t v;
+            if (EPI == kGeneral) {
+                const int32_t a = (int32_t)(((uint32_t)acc << ll[i]) + (uint32_t)bb[i]);
+                long long p = (long long)a * mm[i] + kk[i];
+                p -= (long long)(acc <= cc[i]) << 31;
+                v = (int32_t)(p >> ss[i]) + zz[i];
+            } else {
+                long long p = (long long)acc * mm[i] + kk[i];
+                if (EPI == kTies) p -= (long long)(acc <= cc[i]) << 31;
+                v = ((int32_t)(p >> 32)) >> ss[i];
+            }
+            v = v < lo ? lo : (v > hi ? hi : v);
+            if (lut) v = (int8_t)lut[v + 128];
+            packed[g] |= (uint32_t)(uint8_t)v << (i * 8);
+        }
+    }
+    return make_uint4(packed[0], packed[1], packed[2], packed[3]);
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_constant__ Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const int S = p.stages;
+    const Layout L(S, p.kc, p.bn, p.band_bytes);
+    uint8_t *sA = smem + L.a;
+    uint8_t *sB = smem + L.b;
+    uint8_t *sOut = smem + L.out;
+    uint8_t *sBand = smem + L.band;
+    // per-channel constants, structure of arrays (k: int64[bn], then six int32[bn])
+    long long *sK = reinterpret_cast<long long *>(smem + L.epi);
+    int *sI = reinterpret_cast<int *>(sK + p.bn);
+    const EpiSoA E{sK, sI, sI + p.bn, sI + 2 * p.bn, sI + 3 * p.bn, sI + 4 * p.bn, sI + 5 * p.bn};
+    uint8_t *sLut = smem + L.lut;
+    int *sTab = reinterpret_cast<int *>(smem + L.tab);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
+    uint64_t *full = bars, *empty = bars + S;
+    uint64_t *tfull = bars + 2 * S, *tempty = bars + 2 * S + 4;
+    uint64_t *bfull = bars + 2 * S + 8, *drain = bars + 2 * S + 9;
+    uint64_t *psync = bars + 2 * S + 10, *esync = bars + 2 * S + 11;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 14);
+    volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int ntile = blockIdx.y;
+    const int m_tiles = (p.M + kBM - 1) / kBM;
+    const size_t b_bytes = (size_t)p.kc * p.bn * kBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(smem_u32(full + s), kProducerWarps);
+            mbar_init(smem_u32(empty + s), 1);
+        }
+        for (int a = 0; a < 4; a++) {
+            mbar_init(smem_u32(tfull + a), 1);
+            mbar_init(smem_u32(tempty + a), kEpilogueWarps);
+        }
+        mbar_init(smem_u32(bfull), kProducerWarps);
+        mbar_init(smem_u32(drain), 1);
+        mbar_init(smem_u32(psync), kProducerWarps);
+        mbar_init(smem_u32(esync), kEpilogueWarps);
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    for (int i = threadIdx.x; i < p.bn; i += blockDim.x) {
+        const EpiChan c = p.epi[(size_t)ntile * p.bn + i];
+        sK[i] = c.k;
+        sI[i] = c.m;
+        sI[p.bn + i] = c.cut;
+        sI[2 * p.bn + i] = c.sh;
+        sI[3 * p.bn + i] = c.ls;
+        sI[4 * p.bn + i] = c.bs;
+        sI[5 * p.bn + i] = c.zadd;
+    }
+    if (p.post)
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) sLut[i] = p.post[i];
+    if (p.mode == kBand)
+        for (int i = threadIdx.x; i < p.K; i += blockDim.x) sTab[i] = p.tab[i];
+    if (warp == kMmaWarp) {  // the MMA warp owns the TMEM allocation
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(p.tmem_cols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp < kProducerWarps) {
+        // ------------------------------------------------------------------ producers
+        const int t = threadIdx.x;  // 0..127
+        const uint8_t *wsrc = reinterpret_cast<const uint8_t *>(p.w) + (size_t)ntile * b_bytes;
+        for (size_t off = (size_t)t * 16; off < b_bytes; off += kProducers * 16) cp_async16(smem_u32(sB + off), wsrc + off);
+        cp_async_commit();
+        cp_async_wait<0>();
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(bfull));
+
+        long long it = 0;
+        if (p.mode != kBand) {
+            const int j = t & 7;    // 16-byte chunk of the 128-byte stage row
+            const int r0 = t >> 3;  // rows r0 + 16 i, i = 0..7
+            // Each stage's copies are tracked per thread with cp.async groups; a warp signals
+            // stage `it - lag` once all its lanes have seen that group land (one barrier arrival
+            // per warp). The lag keeps up to lag + 1 stages of copies in flight per thread.
+            const int lag = S - 1 < 3 ? S - 1 : 3;
+            int pending = 0;
+            for (int mt = blockIdx.x; mt < m_tiles; mt += gridDim.x) {
+                const int8_t *rbase[8];
+                int ry[8], rx[8];
+                bool rvalid[8];
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const int m = mt * kBM + r0 + 16 * i;
+                    rvalid[i] = m < p.M;
+                    const int mm = rvalid[i] ? m : 0;
+                    if (p.mode == kPointwise) {
+                        rbase[i] = p.x + (size_t)mm * p.ic;
+                        ry[i] = rx[i] = 0;
+                    } else {
+                        const int ox = mm % p.ow;
+                        const int oy = (mm / p.ow) % p.oh;
+                        const int n = mm / (p.ow * p.oh);
+                        rbase[i] = p.x + (size_t)n * p.ih * p.iw * p.ic;
+                        ry[i] = oy * p.sh - p.pt;
+                        rx[i] = ox * p.sw - p.pl;
+                    }
+                }
+                bool ok = true;
+                for (int kc = 0; kc < p.kc; kc++, it++) {
+                    const int s = (int)(it % S);
+                    if (!mbar_wait(smem_u32(empty + s), (uint32_t)(((it / S) & 1) ^ 1), abort, 101)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t stage = smem_u32(sA + (size_t)s * kStageBytes);
+                    const int k = kc * kBK + j * 16;
+                    if (k < p.K) {
+                        if (p.mode == kPointwise) {
+#pragma unroll
+                            for (int i = 0; i < 8; i++) {
+                                const int r = r0 + 16 * i;
+                                const uint32_t dst = stage + (r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4);
+                                if (rvalid[i]) cp_async16(dst, rbase[i] + k);
+                            }
+                        } else {
+                            const int tap = k / p.ic, c = k - tap * p.ic;
+                            const int ky = tap / p.kw, kx = tap - ky * p.kw;
+                            const int dy = ky * p.dh, dx = kx * p.dw;
+#pragma unroll
+                            for (int i = 0; i < 8; i++) {
+                                const int r = r0 + 16 * i;
+                                const uint32_t dst = stage + (r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4);
+                                if (!rvalid[i]) continue;
+                                const int iy = ry[i] + dy, ix = rx[i] + dx;
+                                const bool in = iy >= 0 && ix >= 0 && iy < p.ih && ix < p.iw;
+                                cp_async16(dst, in ? (const void *)(rbase[i] + ((size_t)iy * p.iw + ix) * p.ic + c)
+                                                   : (const void *)p.fill);
+                            }
+                        }
+                    }
+                    cp_async_commit();
+                    if (++pending > lag) {
+                        cp_async_wait_dyn(lag);
+                        fence_proxy_async();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(smem_u32(full + (int)((it - lag) % S)));
+                        pending--;
+                    }
+                }
+                if (!ok) break;
+            }
+            cp_async_wait<0>();
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0)
+                for (long long q = it - pending; q < it; q++) mbar_arrive(smem_u32(full + (int)(q % S)));
+        } else {
+            // Band mode: one K stage per tile (K <= 128), thread t builds pixel row t.
+            const size_t row_bytes = (size_t)p.iw * p.ic;
+            unsigned round = 0;
+            // band of tile `mt`: global input rows [g_lo, g_hi] (image-major rows are contiguous)
+            auto band_of = [&](int mt, long long &g_lo, long long &lead, long long &chunks) {
+                const int m0 = mt * kBM, m1 = min(p.M, m0 + kBM) - 1;
+                const int n0 = m0 / (p.oh * p.ow), oy0 = (m0 / p.ow) % p.oh;
+                const int n1 = m1 / (p.oh * p.ow), oy1 = (m1 / p.ow) % p.oh;
+                g_lo = (long long)n0 * p.ih + max(0, oy0 * p.sh - p.pt);
+                const long long g_hi = (long long)n1 * p.ih + min(p.ih - 1, oy1 * p.sh - p.pt + (p.kh - 1) * p.dh);
+                const long long start = g_lo * (long long)row_bytes, aligned = start & ~15ll;
+                lead = start - aligned;
+                const long long end = min((g_hi + 1) * (long long)row_bytes, p.x_bytes);
+                chunks = (end - aligned + 15) >> 4;
+            };
+            auto prefetch = [&](int mt, int buf) {
+                long long g_lo, lead, chunks;
+                band_of(mt, g_lo, lead, chunks);
+                const uint8_t *src = reinterpret_cast<const uint8_t *>(p.x) + ((g_lo * (long long)row_bytes) & ~15ll);
+                const uint32_t dst = smem_u32(sBand + (size_t)buf * ((p.band_bytes + 15) & ~15));
+                for (long long q = t; q < chunks; q += kProducers) cp_async16(dst + (uint32_t)(q * 16), src + q * 16);
+                cp_async_commit();
+            };
+            int i_tile = 0;
+            if (blockIdx.x < m_tiles) prefetch(blockIdx.x, 0);
+            for (int mt = blockIdx.x; mt < m_tiles; mt += gridDim.x, i_tile++, it++) {
+                const int buf = i_tile & 1;
+                const int next = mt + gridDim.x;
+                if (next < m_tiles) {
+                    prefetch(next, buf ^ 1);
+                    cp_async_wait<1>();
+                } else {
+                    cp_async_wait<0>();
+                }
+                if (!role_sync(smem_u32(psync), round, abort, 106)) break;  // band `buf` complete for all
+                const int s = (int)(it % S);
+                if (!mbar_wait(smem_u32(empty + s), (uint32_t)(((it / S) & 1) ^ 1), abort, 101)) break;
+                long long g_lo, lead, chunks;
+                band_of(mt, g_lo, lead, chunks);
+                const uint8_t *band = sBand + (size_t)buf * ((p.band_bytes + 15) & ~15) + lead;
+                const uint32_t stage = smem_u32(sA + (size_t)s * kStageBytes);
+                const int m = mt * kBM + t;
+                if (m < p.M) {
+                    const int ox = m % p.ow, oy = (m / p.ow) % p.oh, n = m / (p.ow * p.oh);
+                    const int y0 = oy * p.sh - p.pt, x0 = ox * p.sw - p.pl;
+                    const long long grow0 = (long long)n * p.ih - g_lo;
+                    const int chunks16 = (p.K + 15) >> 4;
+                    for (int jj = 0; jj < chunks16; jj++) {
+                        uint32_t words[4];
+#pragma unroll
+                        for (int w4 = 0; w4 < 4; w4++) {
+                            uint32_t word = 0;
+#pragma unroll
+                            for (int b = 0; b < 4; b++) {
+                                const int kk = jj * 16 + w4 * 4 + b;
+                                int v = 0;
+                                if (kk < p.K) {
+                                    const int e = sTab[kk];
+                                    const int iy = y0 + (e >> 20), ix = x0 + ((e >> 10) & 1023);
+                                    v = (iy >= 0 && ix >= 0 && iy < p.ih && ix < p.iw)
+                                            ? (int)(int8_t)band[(grow0 + iy) * (long long)row_bytes + ix * p.ic + (e & 1023)]
+                                            : p.xzp;
+                                }
+                                word |= (uint32_t)(uint8_t)v << (b * 8);
+                            }
+                            words[w4] = word;
+                        }
+                        const int r = t;
+                        st_shared16(stage + (r >> 3) * 1024 + (r & 7) * 128 + ((jj ^ (r & 7)) << 4),
+                                    make_uint4(words[0], words[1], words[2], words[3]));
+                    }
+                }
+                fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(full + s));
+                if (!role_sync(smem_u32(psync), round, abort, 107)) break;  // band `buf` free for reuse
+            }
+        }
+        cp_async_wait<0>();
+    } else if (warp == kMmaWarp) {
+        // ------------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = instr_desc(p.bn);
+            const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
+            bool ok = mbar_wait(smem_u32(bfull), 0, abort, 102);
+            tc_fence_after();
+            long long it = 0;
+            int lt = 0;
+            for (int mt = blockIdx.x; mt < m_tiles && ok; mt += gridDim.x, lt++) {
+                const int acc = lt % p.n_acc;
+                if (!mbar_wait(smem_u32(tempty + acc), (uint32_t)(((lt / p.n_acc) & 1) ^ 1), abort, 103)) break;
+                tc_fence_after();
+                const uint32_t tmem_d = tmem_base + (uint32_t)(acc * p.bn);
+                for (int kc = 0; kc < p.kc; kc++, it++) {
+                    const int s = (int)(it % S);
+                    if (!mbar_wait(smem_u32(full + s), (uint32_t)((it / S) & 1), abort, 104)) {
+                        ok = false;
+                        break;
+                    }
+                    // the stage was written through the generic proxy (cp.async / st.shared)
+                    fence_proxy_async();
+                    tc_fence_after();
+                    const int kbytes = min(kBK, ((p.K + 31) & ~31) - kc * kBK);
+                    for (int kk = 0; kk < kbytes / 32; kk++) {
+                        const uint64_t ad = smem_desc(a0 + (uint32_t)(s * kStageBytes + kk * 32));
+                        const uint64_t bd = smem_desc(b0 + (uint32_t)(kc * p.bn * kBK + kk * 32));
+                        mma_i8(tmem_d, ad, bd, idesc, (kc | kk) ? 1u : 0u);
+                    }
+                    mma_commit(smem_u32(empty + s));
+                }
+                if (!ok) break;
+                mma_commit(smem_u32(tfull + acc));
+            }
+            // Drain: every MMA this thread issued has completed before TMEM can be freed,
+            // including on the abort path.
+            mma_commit(smem_u32(drain));
+            const long long start = clock64();
+            while (!mbar_try_wait(smem_u32(drain), 0, 200000) && clock64() - start < kTimeoutCycles) {
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------------ epilogue
+        const int e = warp - kProducerWarps;
+        const int et = threadIdx.x - kProducers;  // 0..255
+        const int quarter = e & 3;                // TMEM lanes 32*quarter .. +31 (warp id % 4 rule)
+        const int half = e >> 2;                  // which 16-column chunks this warp takes
+        const int row = quarter * 32 + lane;
+        const uint8_t *lut = p.post ? sLut : nullptr;
+        const int n0 = ntile * p.bn;
+        const int cols = min(p.bn, p.oc - n0);
+        const int live_chunks = (cols + 15) / 16;
+        const int vw = (p.oc & 15) == 0 ? 16 : (p.oc & 7) == 0 ? 8 : (p.oc & 3) == 0 ? 4 : 1;
+        const int box_chunks = p.box / 16;
+        const int swz_row = p.swz == 3 ? (row & 7) : p.swz == 2 ? ((row >> 1) & 3) : p.swz == 1 ? ((row >> 2) & 1) : 0;
+        unsigned round = 0;
+        int lt = 0;
+        for (int mt = blockIdx.x; mt < m_tiles; mt += gridDim.x, lt++) {
+            const int acc = lt % p.n_acc;
+            if (!mbar_wait(smem_u32(tfull + acc), (uint32_t)((lt / p.n_acc) & 1), abort, 105)) break;
+            tc_fence_after();
+            uint8_t *stage = sOut + (size_t)(lt & 1) * out_stride(p.bn);
+            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.bn);
+            uint32_t ra[16], rb[16];
+            int ci = half;
+            if (ci < live_chunks) {
+                tmem_ld16_nowait(taddr + ci * 16, ra);
+                tmem_wait_ld(ra);
+            }
+            while (ci < live_chunks) {
+                const int next = ci + 2;
+                if (next < live_chunks) tmem_ld16_nowait(taddr + next * 16, rb);
+                const uint4 v = epilogue_chunk<EPI>(ra, E, lut, ci * 16, p.lo, p.hi);
+                uint32_t dst;
+                if (p.store_tma) {
+                    const int sub = ci / box_chunks, jj = ci - sub * box_chunks;
+                    dst = smem_u32(stage + (size_t)sub * kBM * p.box + (size_t)row * p.box + ((jj ^ swz_row) << 4));
+                } else {
+                    dst = smem_u32(stage + (size_t)row * (p.bn + 16) + ci * 16);
+                }
+                st_shared16(dst, v);
+                if (next < live_chunks) tmem_wait_ld(rb);
+#pragma unroll
+                for (int q = 0; q < 16; q++) ra[q] = rb[q];
+                ci = next;
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(tempty + acc));  // accumulator free for reuse
+            const int m0 = mt * kBM;
+            if (p.store_tma) {
+                fence_proxy_async();  // staged bytes visible to the TMA (async proxy)
+                if (et == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // previous store read out
+            }
+            if (!role_sync(smem_u32(esync), round, abort, 108)) break;  // tile staged by all threads
+            if (p.store_tma) {
+                if (et == 0) {
+                    for (int sub = 0; sub * p.box < cols; sub++) {
+                        const uint32_t src = smem_u32(stage + (size_t)sub * kBM * p.box);
+                        asm volatile(
+                            "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                                reinterpret_cast<uint64_t>(&p.ymap)),
+                            "r"(src), "r"(n0 + sub * p.box), "r"(m0)
+                            : "memory");
+                    }
+                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                }
+            } else {
+                // cooperative coalesced copy-out of the staged tile: rows m0.., columns n0..n0+cols
+                const int rows = min(kBM, p.M - m0);
+                const int cpr = cols / vw;
+                const int total = rows * cpr;
+                int8_t *ybase = p.y + (size_t)m0 * p.oc + n0;
+                for (int q = et; q < total; q += kEpilogues) {
+                    const int rr = q / cpr, cc = (q - rr * cpr) * vw;
+                    const uint8_t *src = stage + (size_t)rr * (p.bn + 16) + cc;
+                    int8_t *dst = ybase + (size_t)rr * p.oc + cc;
+                    if (vw == 16) *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(src);
+                    else if (vw == 8) *reinterpret_cast<uint2 *>(dst) = *reinterpret_cast<const uint2 *>(src);
+                    else if (vw == 4) *reinterpret_cast<uint32_t *>(dst) = *reinterpret_cast<const uint32_t *>(src);
+                    else *dst = (int8_t)*src;
+                }
+            }
+        }
+        if (p.store_tma && et == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(p.tmem_cols));
+    }
+}
+
+int g_sm_count = 0;
+
+}  // namespace
+
+struct ConvTc {
+    Params p{};
+    int n_tiles = 1;
+    size_t smem = 0;
+};
+
+// Exact requantisation constants, one branch-free form for every channel. The reference
+// computes y = clamp(scale(v, m, s) + yzp) with v = acc + bias (qnn.c:61-83):
+//   s >= 0:  y = floor(((v<<s) * m + 2^30) / 2^31) + yzp       -> ls = s, bs = bias<<s, k = 2^30 + yzp*2^31
+//   s = -n:  y = floor((v*m + 2^30 + 2^(30+n) - [v*m < -2^30]*2^31) / 2^(31+n)) + yzp
+//            (nested floor divisions with integer addends collapse into one; the bracket turns
+//            the ties-up of a negative high product into the reference's ties-away). With
+//            v = acc + bias this is affine in acc plus one comparison: acc <= cut, where
+//            cut = floor((-2^30 - 1) / m) - bias. yzp*2^(31+n) folds into k while n <= 15;
+//            beyond that it is added after the shift (zadd) to keep k inside int64.
+//   m == 0:  both forms give y = yzp.
+// The accumulator of the MMA is bounded by 8192*128*127 < 2^27, so cut = INT32_MIN means never.
+EpiChan make_epilogue(long long bias, int m, int shift, int yzp) {
+    EpiChan e{};
+    e.m = m;
+    e.cut = INT32_MIN;
+    if (shift >= 0) {
+        e.ls = shift;
+        e.bs = (int)((uint32_t)(uint64_t)bias << shift);
+        e.k = (1ll << 30) + (long long)yzp * (1ll << 31);
+        e.sh = 31;
+    } else {
+        // m == 0 needs no special case: p = k and floor(k / 2^(31+n)) = yzp.
+        const int n = -shift;
+        e.k = bias * (long long)m + (1ll << 30) + (1ll << (30 + n));
+        if (n <= 15) e.k += (long long)yzp * (1ll << (31 + n));
+        else e.zadd = yzp;
+        if (m > 0) {
+            const long long num = -(1ll << 30) - 1;
+            long long fl = num / m;
+            if (fl * m > num) fl -= 1;
+            const long long cut = fl - bias;
+            e.cut = (int)(cut < INT32_MIN ? INT32_MIN : (cut > INT32_MAX ? INT32_MAX : cut));
+        }
+        e.sh = 31 + n;
+    }
+    return e;
+}
+
+// Largest band (bytes, including the 16-byte alignment lead) any 128-pixel tile of this layer
+// needs; the pattern repeats every lcm(128, oh*ow) pixels.
+static long long max_band_bytes(const ConvGeom &g) {
+    const long long img = (long long)g.oh * g.ow;
+    const long long period = img / std::gcd(img, (long long)kBM) * kBM;
+    const long long row_bytes = (long long)g.iw * g.ic;
+    long long worst = 0;
+    for (long long m0 = 0; m0 < period; m0 += kBM) {
+        const long long m1 = m0 + kBM - 1;
+        const long long n0 = m0 / img, oy0 = (m0 / g.ow) % g.oh, n1 = m1 / img, oy1 = (m1 / g.ow) % g.oh;
+        const long long lo = n0 * g.ih + std::max<long long>(0, oy0 * g.sh - g.pt);
+        const long long hi = n1 * g.ih + std::min<long long>(g.ih - 1, oy1 * g.sh - g.pt + (long long)(g.kh - 1) * g.dh);
+        worst = std::max(worst, (hi - lo + 1) * row_bytes + 15 + 16);
+    }
+    return worst;
+}
+
+int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *post_dev, const ConvGeom &g,
+                    const std::function<void *(size_t)> &alloc, ConvTc **out) {
     *out = nullptr;
+    const char *env = std::getenv("UNOQ_CONV_TC");
+    if (env && env[0] == '0') return 0;
+    const int K = g.kh * g.kw * g.ic;
+    const int K32 = (K + 31) & ~31;
+    const int kc = (K32 + kBK - 1) / kBK;
+    int mode = kGather16;
+    if (g.kh == 1 && g.kw == 1 && g.sh == 1 && g.sw == 1 && g.pt == 0 && g.pl == 0 && g.ih == g.oh && g.iw == g.ow &&
+        g.ic % 16 == 0)
+        mode = kPointwise;
+    long long band = 0;
+    if (g.ic % 16 != 0) {
+        // Band gather handles one K stage (3-channel stem: K = 27; 8-channel 3x3: K = 72).
+        if (kc != 1 || (g.kh - 1) * g.dh >= 2048 || (g.kw - 1) * g.dw >= 1024 || g.ic > 1023) return 0;
+        mode = kBand;
+        band = max_band_bytes(g);
+        if (band > 48 * 1024) return 0;
+    }
+    // N tiling: a power-of-two tile width (16..256, so staged tiles match a TMA swizzle span)
+    // no wider than the channel count needs, whose weights stay resident in shared memory.
+    int bn = 16;
+    while (bn < 256 && bn < g.oc) bn *= 2;
+    while (bn > 16 && (size_t)kc * bn * kBK > (size_t)kWeightBudget) bn /= 2;
+    if ((size_t)kc * bn * kBK > (size_t)kWeightBudget) return 0;
+    const int n_tiles = (g.oc + bn - 1) / bn;
+    int stages = 8;
+    while (stages > 2 && Layout(stages, kc, bn, (int)band).total > (size_t)kMaxSmem) stages--;
+    if (Layout(stages, kc, bn, (int)band).total > (size_t)kMaxSmem) return 0;
+
+    // Weights: reference packed layout (gemm.h:9) -> per N tile, per K stage, UMMA SW128 K-major.
+    const int kp = q[18];
+    const int oc = g.oc;
+    std::vector<uint8_t> wt((size_t)n_tiles * kc * bn * kBK, 0);
+    std::vector<EpiChan> epi((size_t)n_tiles * bn);
+    auto wref = [&](int j, int t) -> int { return w_packed[(j / 4) * kp * 4 + (t / 8) * 32 + (j % 4) * 8 + t % 8]; };
+    const int32_t *cbias = q + kHead, *mult = cbias + oc, *shift = mult + oc;
+    const int xzp = q[12], yzp = q[13];
+    for (int nt = 0; nt < n_tiles; nt++)
+        for (int r = 0; r < bn; r++) {
+            const int j = nt * bn + r;
+            if (j >= oc) {
+                epi[(size_t)nt * bn + r] = make_epilogue(0, 0, 0, 0);
+                continue;
+            }
+            long long sum_all = 0, sum_pad = 0;
+            for (int t = 0; t < kp; t++) {
+                const int v = wref(j, t);
+                sum_all += v;
+                if (t >= K) sum_pad += v;
+                if (t < K) {
+                    const int c = t / kBK, byte = t % kBK, chunk = byte / 16;
+                    const size_t off = ((size_t)(nt * kc + c) * bn + (r / 8) * 8) * kBK + (r % 8) * kBK +
+                                       ((chunk ^ (r % 8)) * 16) + byte % 16;
+                    wt[off] = (uint8_t)(int8_t)v;
+                }
+            }
+            const long long bias = (long long)cbias[j] + 128ll * sum_all + (long long)xzp * sum_pad;
+            epi[(size_t)nt * bn + r] = make_epilogue(bias, mult[j], shift[j], yzp);
+        }
+    // Epilogue mode (see EpiMode): the fast forms need every live channel's shift in [-15, -1].
+    bool fast = true;
+    for (int j = 0; j < oc; j++) fast &= shift[j] <= -1 && shift[j] >= -15;
+    const int epi_mode = !fast ? kGeneral : (q[14] >= yzp ? kRelu : kTies);
+    if (epi_mode != kGeneral)
+        for (auto &e : epi) e.sh = e.sh >= 32 ? e.sh - 32 : 0;  // shift of the high word
+    std::vector<int> tab(kBK, 0);
+    for (int t = 0; t < K && t < kBK; t++) {
+        const int tap = t / g.ic, c = t % g.ic;
+        tab[t] = ((tap / g.kw) * g.dh) << 20 | ((tap % g.kw) * g.dw) << 10 | c;
+    }
+    int8_t fill[16];
+    std::memset(fill, xzp, sizeof(fill));
+    void *dw = alloc(wt.size());
+    void *de = alloc(epi.size() * sizeof(EpiChan));
+    void *dt = alloc(tab.size() * sizeof(int));
+    void *df = alloc(sizeof(fill));
+    if (!dw || !de || !dt || !df) return 2001;
+    if (cudaMemcpy(dw, wt.data(), wt.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(de, epi.data(), epi.size() * sizeof(EpiChan), cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(dt, tab.data(), tab.size() * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(df, fill, sizeof(fill), cudaMemcpyHostToDevice) != cudaSuccess)
+        return 2001;
+    if (!g_sm_count) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev);
+        if (g_sm_count <= 0) g_sm_count = 148;
+    }
+    static bool attr_set = false;
+    if (!attr_set) {
+        if (cudaFuncSetAttribute(conv_tc_kernel<kRelu>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(conv_tc_kernel<kTies>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(conv_tc_kernel<kGeneral>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
+                cudaSuccess)
+            return 2001;
+        attr_set = true;
+    }
+    ConvTc *c = new ConvTc();
+    Params &p = c->p;
+    p.w = static_cast<const int8_t *>(dw);
+    p.epi = static_cast<const EpiChan *>(de);
+    p.post = post_dev;
+    p.tab = static_cast<const int *>(dt);
+    p.fill = static_cast<const int8_t *>(df);
+    p.ih = g.ih, p.iw = g.iw, p.ic = g.ic, p.oh = g.oh, p.ow = g.ow, p.oc = g.oc;
+    p.kh = g.kh, p.kw = g.kw, p.sh = g.sh, p.sw = g.sw, p.dh = g.dh, p.dw = g.dw, p.pt = g.pt, p.pl = g.pl;
+    p.K = K;
+    p.kc = kc;
+    p.bn = bn;
+    p.stages = stages;
+    p.lo = q[14], p.hi = q[15];
+    p.xzp = xzp;
+    p.n_acc = bn <= 128 ? 4 : 2;
+    p.tmem_cols = std::max(32, p.n_acc * bn);
+    p.store_tma = (g.oc % 16) == 0;
+    p.box = std::min(bn, 128);
+    p.swz = p.box == 128 ? 3 : p.box == 64 ? 2 : p.box == 32 ? 1 : 0;
+    p.mode = mode;
+    p.band_bytes = (int)band;
+    p.epi_mode = epi_mode;
+    c->n_tiles = n_tiles;
+    c->smem = Layout(stages, kc, bn, (int)band).total;
+    *out = c;
     return 0;
 }
-void conv_tc_launch(const ConvTc &, const int8_t *, int8_t *, const ConvGeom &, cudaStream_t) {}
+
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiled encoder() {
+    static EncodeTiled fn = nullptr;
+    if (!fn) {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(ptr);
+    }
+    return fn;
+}
+
+int conv_tc_launch(const ConvTc &c, const int8_t *x, int8_t *y, const ConvGeom &g, cudaStream_t s) {
+    Params p = c.p;
+    p.x = x;
+    p.y = y;
+    p.M = g.n * g.oh * g.ow;
+    if (p.store_tma) {
+        // Output tensor [M][oc] int8; the box is one staged sub-tile, swizzled like the staging.
+        EncodeTiled enc = encoder();
+        if (!enc) return 2001;
+        const cuuint64_t dims[2] = {(cuuint64_t)g.oc, (cuuint64_t)p.M};
+        const cuuint64_t strides[1] = {(cuuint64_t)g.oc};
+        const cuuint32_t box[2] = {(cuuint32_t)p.box, (cuuint32_t)kBM};
+        const cuuint32_t estr[2] = {1, 1};
+        const CUtensorMapSwizzle sw = p.swz == 3   ? CU_TENSOR_MAP_SWIZZLE_128B
+                                      : p.swz == 2 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                      : p.swz == 1 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                                   : CU_TENSOR_MAP_SWIZZLE_NONE;
+        if (enc(&p.ymap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return 2001;
+    }
+    p.x_bytes = (long long)g.n * g.ih * g.iw * g.ic;
+    const int m_tiles = (p.M + kBM - 1) / kBM;
+    int per_tile = (g_sm_count + c.n_tiles - 1) / c.n_tiles;
+    if (per_tile < 1) per_tile = 1;
+    if (per_tile > m_tiles) per_tile = m_tiles;
+    dim3 grid(per_tile, c.n_tiles);
+    if (p.epi_mode == kRelu) conv_tc_kernel<kRelu><<<grid, kThreads, c.smem, s>>>(p);
+    else if (p.epi_mode == kTies) conv_tc_kernel<kTies><<<grid, kThreads, c.smem, s>>>(p);
+    else conv_tc_kernel<kGeneral><<<grid, kThreads, c.smem, s>>>(p);
+    return 0;
+}
+
 void conv_tc_free(ConvTc *c) { delete c; }
+
+int conv_tc_error(bool reset) {
+    int v = 0;
+    cudaMemcpyFromSymbol(&v, g_conv_tc_error, sizeof(int));
+    if (reset && v) {
+        int z = 0;
+        cudaMemcpyToSymbol(g_conv_tc_error, &z, sizeof(int));
+    }
+    return v;
+}
 
 }  // namespace uq

@@ -17,7 +17,10 @@ struct ConvTc;  // prepared weights + epilogue tables for one conv op
 // when the CUDA-core path should run instead. Returns 0 or 2001.
 int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *post_dev, const ConvGeom &g,
                     const std::function<void *(size_t)> &alloc, ConvTc **out);
-void conv_tc_launch(const ConvTc &c, const int8_t *x, int8_t *y, const ConvGeom &g, cudaStream_t s);
+// Enqueue one conv; returns 0 or 2001 when the output tensor map cannot be encoded.
+int conv_tc_launch(const ConvTc &c, const int8_t *x, int8_t *y, const ConvGeom &g, cudaStream_t s);
 void conv_tc_free(ConvTc *c);
+// Error code recorded by a timed-out device wait (0 = none); optionally cleared.
+int conv_tc_error(bool reset);
 
 }  // namespace uq

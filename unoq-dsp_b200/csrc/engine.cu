@@ -142,18 +142,19 @@ int Engine::prepare() {
                 const uint32_t ta = o.a, tz = o.out;
                 if (tc) {
                     std::shared_ptr<ConvTc> keep(tc, conv_tc_free);
-                    st.run = [keep, g, ta, tz](const BatchCtx &B, cudaStream_t s) {
+                    st.run = [keep, g, ta, tz](const BatchCtx &B, cudaStream_t s) -> int {
                         ConvGeom gb = g;
                         gb.n = g.n * (int)B.images;
-                        conv_tc_launch(*keep, reinterpret_cast<const int8_t *>(B.ptr[ta]),
-                                       reinterpret_cast<int8_t *>(B.ptr[tz]), gb, s);
+                        return conv_tc_launch(*keep, reinterpret_cast<const int8_t *>(B.ptr[ta]),
+                                              reinterpret_cast<int8_t *>(B.ptr[tz]), gb, s);
                     };
                 } else {
-                    st.run = [g, r, w, ta, tz](const BatchCtx &B, cudaStream_t s) {
+                    st.run = [g, r, w, ta, tz](const BatchCtx &B, cudaStream_t s) -> int {
                         ConvGeom gb = g;
                         gb.n = g.n * (int)B.images;
                         launch_conv_simt(reinterpret_cast<const int8_t *>(B.ptr[ta]), w,
                                          reinterpret_cast<int8_t *>(B.ptr[tz]), gb, r, s);
+                        return 0;
                     };
                 }
                 break;
@@ -174,19 +175,21 @@ int Engine::prepare() {
                     Requant r{dq + kHead, dq + kHead + g.oc, dq + kHead + 2 * g.oc,
                               o.p[1] ? dconst(o.p[1] - 1) : nullptr, q[13], q[14], q[15]};
                     const int8_t *w = reinterpret_cast<const int8_t *>(dconst(o.b));
-                    st.run = [g, r, w, ta, tz](const BatchCtx &B, cudaStream_t s) {
+                    st.run = [g, r, w, ta, tz](const BatchCtx &B, cudaStream_t s) -> int {
                         ConvGeom gb = g;
                         gb.n = g.n * (int)B.images;
                         launch_depthwise(reinterpret_cast<const int8_t *>(B.ptr[ta]), w,
                                          reinterpret_cast<int8_t *>(B.ptr[tz]), gb, r, s);
+                        return 0;
                     };
                 } else {
                     const int is_max = q[19], lo = q[14], hi = q[15];
-                    st.run = [g, is_max, lo, hi, ta, tz](const BatchCtx &B, cudaStream_t s) {
+                    st.run = [g, is_max, lo, hi, ta, tz](const BatchCtx &B, cudaStream_t s) -> int {
                         ConvGeom gb = g;
                         gb.n = g.n * (int)B.images;
                         launch_pool(reinterpret_cast<const int8_t *>(B.ptr[ta]), reinterpret_cast<int8_t *>(B.ptr[tz]), gb,
                                     is_max, lo, hi, s);
+                        return 0;
                     };
                 }
                 break;
@@ -196,9 +199,10 @@ int Engine::prepare() {
                 const int width = q[16], lo = q[14], hi = q[15];
                 const int32_t *table = reinterpret_cast<const int32_t *>(dconst(o.p[0])) + kHead;
                 const uint32_t ta = o.a, tz = o.out, abytes = a.bytes;
-                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                st.run = [=](const BatchCtx &B, cudaStream_t s) -> int {
                     launch_softmax_table(reinterpret_cast<const int8_t *>(B.ptr[ta]), reinterpret_cast<int8_t *>(B.ptr[tz]),
                                          (size_t)abytes / width * B.images, width, table, lo, hi, s);
+                    return 0;
                 };
                 break;
             }
@@ -206,9 +210,10 @@ int Engine::prepare() {
                 const int width = P.q(o.b)[0];
                 const int32_t *dq = reinterpret_cast<const int32_t *>(dconst(o.b));
                 const uint32_t ta = o.a, tz = o.out, abytes = a.bytes;
-                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                st.run = [=](const BatchCtx &B, cudaStream_t s) -> int {
                     launch_softmax_exact(reinterpret_cast<const int8_t *>(B.ptr[ta]), reinterpret_cast<int8_t *>(B.ptr[tz]),
                                          (size_t)abytes / width * B.images, width, dq, s);
+                    return 0;
                 };
                 break;
             }
@@ -218,11 +223,12 @@ int Engine::prepare() {
                 std::memcpy(q7, q, sizeof(q7));
                 const int m = (int)z.d[1], n = (int)z.d[2], k = (int)a.d[q[5] ? 1 : 2];
                 const uint32_t ta = o.a, tb = o.b, tz = o.out, d0 = z.d[0];
-                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                st.run = [=](const BatchCtx &B, cudaStream_t s) -> int {
                     int32_t qq[7];
                     std::memcpy(qq, q7, sizeof(qq));
                     launch_bmm(reinterpret_cast<const int8_t *>(B.ptr[ta]), reinterpret_cast<const int8_t *>(B.ptr[tb]),
                                reinterpret_cast<int8_t *>(B.ptr[tz]), (size_t)d0 * B.images, m, n, k, qq, s);
+                    return 0;
                 };
                 break;
             }
@@ -237,10 +243,11 @@ int Engine::prepare() {
                     begin[d + 1] = o.p[d];
                 }
                 const uint32_t ta = o.a, tz = o.out;
-                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                st.run = [=](const BatchCtx &B, cudaStream_t s) -> int {
                     Shape5 ib = in, ob = out;
                     ib.d[0] = ob.d[0] = B.images;
                     launch_slice(B.ptr[ta], B.ptr[tz], ib, ob, begin, s);
+                    return 0;
                 };
                 break;
             }
@@ -248,11 +255,12 @@ int Engine::prepare() {
                 int32_t q7[7];
                 std::memcpy(q7, P.q(o.p[0]), sizeof(q7));
                 const uint32_t ta = o.a, tb = o.b, tz = o.out, zb = z.bytes;
-                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                st.run = [=](const BatchCtx &B, cudaStream_t s) -> int {
                     int32_t qq[7];
                     std::memcpy(qq, q7, sizeof(qq));
                     launch_mul(reinterpret_cast<const int8_t *>(B.ptr[ta]), reinterpret_cast<const int8_t *>(B.ptr[tb]),
                                reinterpret_cast<int8_t *>(B.ptr[tz]), (size_t)zb * B.images, qq, s);
+                    return 0;
                 };
                 break;
             }
@@ -260,11 +268,12 @@ int Engine::prepare() {
                 int32_t q5[5];
                 std::memcpy(q5, P.q(o.b), sizeof(q5));
                 const uint32_t ta = o.a, tz = o.out, d0 = a.d[0], ch = a.d[3];
-                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                st.run = [=](const BatchCtx &B, cudaStream_t s) -> int {
                     int32_t qq[5];
                     std::memcpy(qq, q5, sizeof(qq));
                     launch_mean(reinterpret_cast<const int8_t *>(B.ptr[ta]), reinterpret_cast<int8_t *>(B.ptr[tz]),
                                 (size_t)d0 * B.images, (int)ch, qq, s);
+                    return 0;
                 };
                 break;
             }
@@ -275,8 +284,9 @@ int Engine::prepare() {
                 for (int d = 0; d < 4; d++) ad[d] = a.d[d], zd[d] = z.d[d];
                 const int8_t value = (int8_t)(int32_t)o.p[0];
                 const uint32_t ta = o.a, tz = o.out;
-                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                st.run = [=](const BatchCtx &B, cudaStream_t s) -> int {
                     launch_pad(B.ptr[ta], B.ptr[tz], (int)B.images, ad, zd, pads, value, s);
+                    return 0;
                 };
                 break;
             }
@@ -284,8 +294,9 @@ int Engine::prepare() {
                 const uint8_t *table = dconst(o.b);
                 const unsigned flip = a.type == 3 ? 128u : 0u;
                 const uint32_t ta = o.a, tz = o.out, ab = a.bytes;
-                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                st.run = [=](const BatchCtx &B, cudaStream_t s) -> int {
                     launch_lut(B.ptr[ta], B.ptr[tz], (size_t)ab * B.images, table, flip, s);
+                    return 0;
                 };
                 break;
             }
@@ -294,8 +305,9 @@ int Engine::prepare() {
                 const uint32_t ta = o.a, tz = o.out;
                 const int n = (int)a.d[0], ih = (int)a.d[1], iw = (int)a.d[2], c = (int)a.d[3], oh = (int)z.d[1],
                           ow = (int)z.d[2];
-                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                st.run = [=](const BatchCtx &B, cudaStream_t s) -> int {
                     launch_resize(B.ptr[ta], B.ptr[tz], n * (int)B.images, ih, iw, c, oh, ow, offsets, s);
+                    return 0;
                 };
                 break;
             }
@@ -306,8 +318,9 @@ int Engine::prepare() {
                 for (unsigned d = axis + 1; d < a.rank; d++) inner *= a.d[d];
                 const size_t ac = a.d[axis] * inner, bc = b.d[axis] * inner;
                 const uint32_t ta = o.a, tb = o.b, tz = o.out;
-                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                st.run = [=](const BatchCtx &B, cudaStream_t s) -> int {
                     launch_concat(B.ptr[ta], B.ptr[tb], B.ptr[tz], outer * B.images, ac, bc, s);
+                    return 0;
                 };
                 break;
             }
@@ -322,7 +335,7 @@ int Engine::prepare() {
                     offs.push_back(off);
                     off += P.ts[id].bytes;
                 }
-                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                st.run = [=](const BatchCtx &B, cudaStream_t s) -> int {
                     Segments sg{};
                     sg.count = (int)ids.size();
                     for (size_t j = 0; j < ids.size(); j++) {
@@ -331,15 +344,17 @@ int Engine::prepare() {
                         sg.dst_offset[j] = offs[j];
                     }
                     launch_pack(sg, B.ptr[tz], zb, (int)B.images, s);
+                    return 0;
                 };
                 break;
             }
             case 18: {
                 const int32_t *dq = reinterpret_cast<const int32_t *>(dconst(o.p[0]));
                 const uint32_t ta = o.a, tb = o.b, tz = o.out, zb = z.bytes;
-                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                st.run = [=](const BatchCtx &B, cudaStream_t s) -> int {
                     launch_add(reinterpret_cast<const int8_t *>(B.ptr[ta]), reinterpret_cast<const int8_t *>(B.ptr[tb]),
                                reinterpret_cast<int8_t *>(B.ptr[tz]), (size_t)zb * B.images, dq, s);
+                    return 0;
                 };
                 break;
             }
@@ -354,10 +369,11 @@ int Engine::prepare() {
                 }
                 const int elem = (int)type_width(a.type);
                 const uint32_t ta = o.a, tz = o.out;
-                st.run = [=](const BatchCtx &B, cudaStream_t s) {
+                st.run = [=](const BatchCtx &B, cudaStream_t s) -> int {
                     Shape5 ib = in;
                     ib.d[0] = B.images;
                     launch_permute(B.ptr[ta], B.ptr[tz], ib, perm, elem, s);
+                    return 0;
                 };
                 break;
             }
@@ -471,7 +487,13 @@ int Engine::run_steps(const BatchCtx &B, cudaStream_t s, bool profile) {
         UQ_CUDA(cudaEventRecord(evs[0], s));
     }
     for (size_t i = 0; i < steps_.size(); i++) {
-        if (steps_[i].run) steps_[i].run(B, s);
+        if (steps_[i].run) {
+            const int rc = steps_[i].run(B, s);
+            if (rc) {
+                set_error("launch of op " + std::to_string(steps_[i].op) + " failed");
+                return rc;
+            }
+        }
         if (profile) UQ_CUDA(cudaEventRecord(evs[i + 1], s));
     }
     cudaError_t e = cudaGetLastError();
@@ -491,6 +513,7 @@ int Engine::run_steps(const BatchCtx &B, cudaStream_t s, bool profile) {
         ticks_[0] += 1;
         ticks_[1] += (uint64_t)(total * 1e6);
         for (auto &ev : evs) cudaEventDestroy(ev);
+        return device_status();
     }
     return 0;
 }
@@ -572,6 +595,17 @@ int Engine::run_host(const void *in, void *out, uint32_t images) {
     }
     UQ_CUDA(cudaEventElapsedTime(&last_ms_, ev0_, ev1_));
     last_images_ = images;
+    return device_status();
+}
+
+// A device-side wait that gave up (bounded mbarrier waits in the tensor-core kernels) leaves a
+// code in device memory; report it as 2003 and clear it.
+int Engine::device_status() {
+    const int code = conv_tc_error(true);
+    if (code) {
+        set_error("device wait timed out in the tensor-core conv (site " + std::to_string(code) + ")");
+        return 2003;
+    }
     return 0;
 }
 
@@ -598,7 +632,7 @@ int Engine::synchronize() {
     if (!stream_) return 22;
     UQ_CUDA(cudaSetDevice(device_));
     UQ_CUDA(cudaStreamSynchronize(stream_));
-    return 0;
+    return device_status();
 }
 
 int Engine::time_launches(uint32_t images, uint32_t iterations, float *ms) {
@@ -613,7 +647,7 @@ int Engine::time_launches(uint32_t images, uint32_t iterations, float *ms) {
     UQ_CUDA(cudaEventSynchronize(ev1_));
     UQ_CUDA(cudaEventElapsedTime(ms, ev0_, ev1_));
     last_images_ = images;
-    return 0;
+    return device_status();
 }
 
 int Engine::kernel_count(uint32_t images) {

@@ -20,10 +20,11 @@ namespace uq {
 
 struct BatchCtx;
 
-// One plan op lowered to device work. `run` enqueues its kernels on the stream.
+// One plan op lowered to device work. `run` enqueues its kernels on the stream and returns 0
+// or an error code.
 struct Step {
     uint32_t op = 0;
-    std::function<void(const BatchCtx &, cudaStream_t)> run;
+    std::function<int(const BatchCtx &, cudaStream_t)> run;
 };
 
 struct BatchCtx {
@@ -75,6 +76,7 @@ class Engine {
     int capture(BatchCtx &b);
     int run_steps(const BatchCtx &b, cudaStream_t s, bool profile);
     void release();
+    int device_status();
     uint8_t *dconst(uint32_t tensor) const { return d_const_ + P_.ts[tensor].offset; }
     void *prep_alloc(size_t bytes);   // device memory owned by the engine for prepared data
 
