@@ -281,6 +281,10 @@ def all_cases(scale=1):
         ("dw5_s2", lambda r: conv_case(r, (1, 14 * s, 14, 16), 16, (5, 5), (2, 2), depthwise=True)),
         ("dw3_c6", lambda r: conv_case(r, (1, 5 * s, 5, 6), 6, (3, 3), (1, 1), depthwise=True)),
         ("dw3_post_lut", lambda r: conv_post_case(r, (1, 6 * s, 6, 24), 24, (3, 3), (1, 1), depthwise=True)),
+        ("dw3_s2_wide", lambda r: conv_case(r, (1, 13 * s, 19, 96), 96, (3, 3), (2, 2), depthwise=True)),
+        ("dw5_s1_post", lambda r: conv_post_case(r, (1, 9 * s, 11, 32), 32, (5, 5), (1, 1), depthwise=True)),
+        ("dw3_s1_c48_none", lambda r: conv_case(r, (1, 5 * s, 21, 48), 48, (3, 3), (1, 1), depthwise=True,
+                                                act="none")),
         ("pool_max5", lambda r: pool_case(r, (1, 10 * s, 10, 16), (5, 5), (1, 1), True)),
         ("pool_avg3_s2", lambda r: pool_case(r, (1, 9 * s, 7, 8), (3, 3), (2, 2), False)),
         ("pool_avg2_valid", lambda r: pool_case(r, (1, 8 * s, 8, 4), (2, 2), (2, 2), False, padding="valid")),

@@ -41,6 +41,7 @@
 
 #include "conv_tc.cuh"
 #include "plan.hpp"
+#include "requant.cuh"
 
 namespace uq {
 
@@ -59,14 +60,6 @@ constexpr int kProducers = kProducerWarps * 32;
 constexpr int kEpilogues = kEpilogueWarps * 32;
 constexpr int kMaxSmem = 227 * 1024;
 constexpr int kWeightBudget = 96 * 1024;
-
-// Per-output-channel epilogue constants (32 bytes): one branch-free form covers every
-// channel (see make_epilogue):  a = (acc << ls) + bs;  p = a*m + k;  p -= 2^31 if acc <= cut;
-// y = (int32)(p >> sh) + zadd.
-struct __align__(32) EpiChan {
-    long long k;
-    int m, cut, ls, bs, sh, zadd;
-};
 
 enum Mode { kPointwise = 0, kGather16 = 1, kBand = 2 };
 
@@ -92,6 +85,7 @@ struct Params {
     int tmem_cols;
     int mode;
     int band_bytes;            // per band buffer (band mode)
+    int nbands;                // band buffers in rotation (band mode)
     int epi_mode;              // EpiMode
     int n_acc;                 // TMEM accumulators in rotation (2 or 4)
     int store_tma;             // 1: staged tile leaves by TMA tensor store; 0: cooperative stores
@@ -106,7 +100,7 @@ __host__ __device__ inline size_t out_stride(int bn) { return ((size_t)kBM * (bn
 // Shared-memory carve-up, identical on host (sizing) and device.
 struct Layout {
     size_t a, b, out, band, epi, lut, tab, bars, total;
-    __host__ __device__ Layout(int stages, int kc, int bn, int band_bytes) {
+    __host__ __device__ Layout(int stages, int kc, int bn, int band_bytes, int nbands) {
         size_t o = 0;
         a = o;
         o += (size_t)stages * kStageBytes;
@@ -115,7 +109,7 @@ struct Layout {
         out = o;
         o += 2 * out_stride(bn);
         band = o;
-        o += 2 * (size_t)((band_bytes + 15) & ~15);
+        o += (size_t)nbands * (size_t)((band_bytes + 15) & ~15);
         epi = (o + 31) & ~(size_t)31;
         o = epi + (size_t)bn * sizeof(EpiChan);
         lut = o;
@@ -256,14 +250,6 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[16]) {
 
 }  // namespace
 
-__host__ __device__ __forceinline__ int32_t epilogue_one(int32_t acc, const EpiChan &e, int lo, int hi) {
-    const int32_t a = (int32_t)(((uint32_t)acc << e.ls) + (uint32_t)e.bs);
-    long long p = (long long)a * e.m + e.k;
-    p -= (long long)(acc <= e.cut) << 31;
-    const int32_t v = (int32_t)(p >> e.sh) + e.zadd;
-    return v < lo ? lo : (v > hi ? hi : v);
-}
-
 namespace {
 
 // Epilogue requantisation modes, chosen per layer on the host (all exact, see make_epilogue):
@@ -334,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const int S = p.stages;
-    const Layout L(S, p.kc, p.bn, p.band_bytes);
+    const Layout L(S, p.kc, p.bn, p.band_bytes, p.nbands);
     uint8_t *sA = smem + L.a;
     uint8_t *sB = smem + L.b;
     uint8_t *sOut = smem + L.out;
@@ -512,18 +498,20 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
                 for (long long q = t; q < chunks; q += kProducers) cp_async16(dst + (uint32_t)(q * 16), src + q * 16);
                 cp_async_commit();
             };
-            int i_tile = 0;
-            if (blockIdx.x < m_tiles) prefetch(blockIdx.x, 0);
+            // Up to nb bands in flight: tiles i .. i + nb - 1 are prefetched while tile i is built.
+            const int nb = p.nbands;
+            int i_tile = 0, fetched = 0;  // tiles of this CTA whose band has been requested
+            const int my_tiles = blockIdx.x < m_tiles ? (m_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+            for (; fetched < nb - 1 && fetched < my_tiles; fetched++)
+                prefetch(blockIdx.x + fetched * gridDim.x, fetched % nb);
             for (int mt = blockIdx.x; mt < m_tiles; mt += gridDim.x, i_tile++, it++) {
-                const int buf = i_tile & 1;
-                const int next = mt + gridDim.x;
-                if (next < m_tiles) {
-                    prefetch(next, buf ^ 1);
-                    cp_async_wait<1>();
-                } else {
-                    cp_async_wait<0>();
+                const int buf = i_tile % nb;
+                if (fetched < my_tiles) {
+                    prefetch(blockIdx.x + fetched * gridDim.x, fetched % nb);
+                    fetched++;
                 }
-                if (!role_sync(smem_u32(psync), round, abort, 106)) break;  // band `buf` complete for all
+                cp_async_wait_dyn(fetched - i_tile - 1);  // band of tile i_tile has landed
+                if (!role_sync(smem_u32(psync), round, abort, 106)) break;  // ... for every thread
                 const int s = (int)(it % S);
                 if (!mbar_wait(smem_u32(empty + s), (uint32_t)(((it / S) & 1) ^ 1), abort, 101)) break;
                 long long g_lo, lead, chunks;
@@ -714,44 +702,6 @@ struct ConvTc {
     size_t smem = 0;
 };
 
-// Exact requantisation constants, one branch-free form for every channel. The reference
-// computes y = clamp(scale(v, m, s) + yzp) with v = acc + bias (qnn.c:61-83):
-//   s >= 0:  y = floor(((v<<s) * m + 2^30) / 2^31) + yzp       -> ls = s, bs = bias<<s, k = 2^30 + yzp*2^31
-//   s = -n:  y = floor((v*m + 2^30 + 2^(30+n) - [v*m < -2^30]*2^31) / 2^(31+n)) + yzp
-//            (nested floor divisions with integer addends collapse into one; the bracket turns
-//            the ties-up of a negative high product into the reference's ties-away). With
-//            v = acc + bias this is affine in acc plus one comparison: acc <= cut, where
-//            cut = floor((-2^30 - 1) / m) - bias. yzp*2^(31+n) folds into k while n <= 15;
-//            beyond that it is added after the shift (zadd) to keep k inside int64.
-//   m == 0:  both forms give y = yzp.
-// The accumulator of the MMA is bounded by 8192*128*127 < 2^27, so cut = INT32_MIN means never.
-EpiChan make_epilogue(long long bias, int m, int shift, int yzp) {
-    EpiChan e{};
-    e.m = m;
-    e.cut = INT32_MIN;
-    if (shift >= 0) {
-        e.ls = shift;
-        e.bs = (int)((uint32_t)(uint64_t)bias << shift);
-        e.k = (1ll << 30) + (long long)yzp * (1ll << 31);
-        e.sh = 31;
-    } else {
-        // m == 0 needs no special case: p = k and floor(k / 2^(31+n)) = yzp.
-        const int n = -shift;
-        e.k = bias * (long long)m + (1ll << 30) + (1ll << (30 + n));
-        if (n <= 15) e.k += (long long)yzp * (1ll << (31 + n));
-        else e.zadd = yzp;
-        if (m > 0) {
-            const long long num = -(1ll << 30) - 1;
-            long long fl = num / m;
-            if (fl * m > num) fl -= 1;
-            const long long cut = fl - bias;
-            e.cut = (int)(cut < INT32_MIN ? INT32_MIN : (cut > INT32_MAX ? INT32_MAX : cut));
-        }
-        e.sh = 31 + n;
-    }
-    return e;
-}
-
 // Largest band (bytes, including the 16-byte alignment lead) any 128-pixel tile of this layer
 // needs; the pattern repeats every lcm(128, oh*ow) pixels.
 static long long max_band_bytes(const ConvGeom &g) {
@@ -796,9 +746,10 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
     while (bn > 16 && (size_t)kc * bn * kBK > (size_t)kWeightBudget) bn /= 2;
     if ((size_t)kc * bn * kBK > (size_t)kWeightBudget) return 0;
     const int n_tiles = (g.oc + bn - 1) / bn;
-    int stages = 8;
-    while (stages > 2 && Layout(stages, kc, bn, (int)band).total > (size_t)kMaxSmem) stages--;
-    if (Layout(stages, kc, bn, (int)band).total > (size_t)kMaxSmem) return 0;
+    int stages = 8, nbands = band ? 4 : 0;
+    while (stages > 2 && Layout(stages, kc, bn, (int)band, nbands).total > (size_t)kMaxSmem) stages--;
+    while (nbands > 2 && Layout(stages, kc, bn, (int)band, nbands).total > (size_t)kMaxSmem) nbands--;
+    if (Layout(stages, kc, bn, (int)band, nbands).total > (size_t)kMaxSmem) return 0;
 
     // Weights: reference packed layout (gemm.h:9) -> per N tile, per K stage, UMMA SW128 K-major.
     const int kp = q[18];
@@ -892,9 +843,10 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
     p.swz = p.box == 128 ? 3 : p.box == 64 ? 2 : p.box == 32 ? 1 : 0;
     p.mode = mode;
     p.band_bytes = (int)band;
+    p.nbands = nbands;
     p.epi_mode = epi_mode;
     c->n_tiles = n_tiles;
-    c->smem = Layout(stages, kc, bn, (int)band).total;
+    c->smem = Layout(stages, kc, bn, (int)band, nbands).total;
     *out = c;
     return 0;
 }

@@ -7,6 +7,7 @@
 #include <numeric>
 
 #include "conv_tc.cuh"
+#include "dw.cuh"
 #include "kernels.cuh"
 
 namespace uq {
@@ -175,13 +176,26 @@ int Engine::prepare() {
                     Requant r{dq + kHead, dq + kHead + g.oc, dq + kHead + 2 * g.oc,
                               o.p[1] ? dconst(o.p[1] - 1) : nullptr, q[13], q[14], q[15]};
                     const int8_t *w = reinterpret_cast<const int8_t *>(dconst(o.b));
-                    st.run = [g, r, w, ta, tz](const BatchCtx &B, cudaStream_t s) -> int {
-                        ConvGeom gb = g;
-                        gb.n = g.n * (int)B.images;
-                        launch_depthwise(reinterpret_cast<const int8_t *>(B.ptr[ta]), w,
-                                         reinterpret_cast<int8_t *>(B.ptr[tz]), gb, r, s);
-                        return 0;
-                    };
+                    DwFast *fast = nullptr;
+                    int rc = dw_prepare(P.s8(o.b), q, r.post, g, [this](size_t n) { return prep_alloc(n); }, &fast);
+                    if (rc) return rc;
+                    if (fast) {
+                        std::shared_ptr<DwFast> keep(fast, dw_free);
+                        st.run = [keep, g, ta, tz](const BatchCtx &B, cudaStream_t s) -> int {
+                            ConvGeom gb = g;
+                            gb.n = g.n * (int)B.images;
+                            return dw_launch(*keep, reinterpret_cast<const int8_t *>(B.ptr[ta]),
+                                             reinterpret_cast<int8_t *>(B.ptr[tz]), gb, s);
+                        };
+                    } else {
+                        st.run = [g, r, w, ta, tz](const BatchCtx &B, cudaStream_t s) -> int {
+                            ConvGeom gb = g;
+                            gb.n = g.n * (int)B.images;
+                            launch_depthwise(reinterpret_cast<const int8_t *>(B.ptr[ta]), w,
+                                             reinterpret_cast<int8_t *>(B.ptr[tz]), gb, r, s);
+                            return 0;
+                        };
+                    }
                 } else {
                     const int is_max = q[19], lo = q[14], hi = q[15];
                     st.run = [g, is_max, lo, hi, ta, tz](const BatchCtx &B, cudaStream_t s) -> int {
