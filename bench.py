@@ -22,7 +22,6 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -42,8 +41,11 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
 
 # --------------------------------------------------------------------------- reference CPU
-def _ref_worker(args):
-    plan_path, shape, images, seed = args
+_REF = {}
+
+
+def _ref_init(plan_path):
+    """Pool initializer: each worker process loads the reference runtime and the plan once."""
     sys.path[:0] = [str(ROOT), str(ROOT / "unoq-dsp_b200")]
     from oracle.oracle import Reference
     from unoq_dsp.bundle import load
@@ -51,6 +53,12 @@ def _ref_worker(args):
     ref = Reference()
     if ref.load(plan):
         raise RuntimeError("reference ug_load failed")
+    _REF.update(ref=ref, plan=plan)
+
+
+def _ref_worker(args):
+    shape, images, seed = args
+    ref, plan = _REF["ref"], _REF["plan"]
     x = np.random.default_rng(seed).integers(-128, 128, size=shape, dtype=np.int64).astype(np.int8)
     t0 = time.perf_counter()
     for _ in range(images):
@@ -58,69 +66,75 @@ def _ref_worker(args):
     return time.perf_counter() - t0
 
 
-def reference_throughput(plan_path, shape, images_per_proc, procs, pool=None):
-    """Images/sec of the reference runtime: `procs` independent processes, each running
-    `images_per_proc` whole images (the reference runtime is single-threaded off Hexagon)."""
-    jobs = [(str(plan_path), shape, images_per_proc, 1000 + i) for i in range(procs)]
+def reference_throughput(shape, images_per_proc, procs, pool):
+    """Images/sec of the reference runtime (single-threaded C off Hexagon): `procs` worker
+    processes, each running `images_per_proc` whole images of the already-loaded plan."""
+    jobs = [(shape, images_per_proc, 1000 + i) for i in range(procs)]
     t0 = time.perf_counter()
-    times = pool.map(_ref_worker, jobs)
+    times = pool.map(_ref_worker, jobs, chunksize=1)
     wall = time.perf_counter() - t0
     return procs * images_per_proc / wall, wall, max(times)
 
 
-def make_pool(procs):
+def make_pool(procs, plan_path):
     import multiprocessing as mp
-    return mp.get_context("spawn").Pool(procs)
+    return mp.get_context("spawn").Pool(procs, initializer=_ref_init, initargs=(str(plan_path),))
 
 
 # --------------------------------------------------------------------------- clocks
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event reasons polled through NVML (read-only queries) every few
+    milliseconds while the timed region runs."""
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
+               ("hw_power_brake", "nvmlClocksEventReasonHwPowerBrakeSlowdown"))
 
-    def __init__(self, device):
-        self.device = device
-        self.rows = []
-        self.proc = None
+    def __init__(self, device, period=0.005):
+        self.device, self.period = device, period
+        self.rows, self.max_mhz, self.nvml = [], None, None
+        self.stop = threading.Event()
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", str(self.device)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            import pynvml as N
+            N.nvmlInit()
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            index = int(vis.split(",")[self.device]) if vis and vis.split(",")[0].isdigit() else self.device
+            self.handle = N.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = N.nvmlDeviceGetMaxClockInfo(self.handle, N.NVML_CLOCK_SM)
+            self.nvml = N
+            self.thread = threading.Thread(target=self._poll, daemon=True)
             self.thread.start()
-        except OSError:
-            self.proc = None
+        except Exception:  # no NVML: the line says "unsampled"
+            self.nvml = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                self.rows.append(parts)
+    def _poll(self):
+        N = self.nvml
+        while not self.stop.is_set():
+            try:
+                self.rows.append((N.nvmlDeviceGetClockInfo(self.handle, N.NVML_CLOCK_SM),
+                                  N.nvmlDeviceGetCurrentClocksEventReasons(self.handle)))
+            except Exception:
+                pass
+            time.sleep(self.period)
 
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self.stop.set()
+        if self.nvml:
+            self.thread.join(timeout=5)
+            self.nvml.nvmlShutdown()
 
     def summary(self):
         if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
-        reasons = set()
-        for r in self.rows:
-            for name, val in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), r[5:9]):
-                if val.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(self.rows)}
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"]}
+        N = self.nvml or __import__("pynvml")
+        reasons = {name for name, attr in self.REASONS for _, bits in self.rows
+                   if getattr(N, attr, 0) and bits & getattr(N, attr)}
+        return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(self.rows), "source": "NVML, 5 ms polling"}
 
 
 # --------------------------------------------------------------------------- distributed
@@ -179,7 +193,7 @@ def op_traffic(plan, images):
         byt = (abytes + zbytes) * images
         mac = 0
         if code in (14, 15):
-            q = np.frombuffer(plan, dtype="<i4", count=20, offset=meta + ts[o[4]][0])
+            q = [int(v) for v in np.frombuffer(plan, dtype="<i4", count=20, offset=meta + ts[o[4]][0])]
             kh, kw, oh, ow, ic, oc = q[0], q[1], q[10], q[11], q[16], q[17]
             k = kh * kw * (1 if code == 15 else ic)
             mac = int(ts[z][4]) * int(oh) * int(ow) * int(oc) * int(k) * images
@@ -344,14 +358,14 @@ def main():
         if not REF_LIB.is_file():
             print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libug_ref.so not built"}))
             return
-        pool = make_pool(cores)
+        pool = make_pool(cores, mpath)
         per_proc = 1
         for _ in range(args.warmup):
-            reference_throughput(mpath, MODELS["mobilenetv4-small"]["shape"], per_proc, cores, pool)
+            reference_throughput(MODELS["mobilenetv4-small"]["shape"], per_proc, cores, pool)
         t0 = time.perf_counter()
         n = 0
         for _ in range(args.steps):
-            reference_throughput(mpath, MODELS["mobilenetv4-small"]["shape"], per_proc, cores, pool)
+            reference_throughput(MODELS["mobilenetv4-small"]["shape"], per_proc, cores, pool)
             n += per_proc * cores
         wall = time.perf_counter() - t0
         pool.close()
@@ -372,7 +386,7 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle.oracle import REF_LIB
         if REF_LIB.is_file():
-            pool = make_pool(cores)
+            pool = make_pool(cores, mpath)
 
     from unoq_dsp.native import load_library
     lib = load_library()
@@ -386,8 +400,10 @@ def main():
         yolo = bench_model(lib, dist, "yolo26n-320", args.yolo_batch, args.steps, args.warmup, peaks, True)
     cpu = None
     if pool is not None:
-        per_proc = 4
-        value, wall, _ = reference_throughput(mpath, MODELS["mobilenetv4-small"]["shape"], per_proc, cores, pool)
+        # bounded sample: about 20 s of CPU work in total, spread over every host core
+        _, _, t1 = reference_throughput(MODELS["mobilenetv4-small"]["shape"], 1, cores, pool)
+        per_proc = max(1, min(16, int(20.0 / (cores * max(t1, 1e-3)))))
+        value, wall, _ = reference_throughput(MODELS["mobilenetv4-small"]["shape"], per_proc, cores, pool)
         pool.close()
         cpu = {"value": round(value, 3), "unit": "images/s", "cores": cores, "kind": "reference",
                "sample": f"{per_proc * cores} MobileNetV4 images ({per_proc} per process on {cores} processes), "

@@ -20,6 +20,28 @@ __device__ __forceinline__ int32_t dev_scale(int32_t v, int32_t m, int shift) {
     return base + (int32_t)(rem > ((mask >> 1) + (h < 0 ? 1u : 0u)));
 }
 
+// Exact n / d for 0 <= n < 2^31 and 1 <= d < 2^31 with one 64-bit multiply and a shift, the
+// invariant-divisor method of Granlund and Montgomery ("Division by invariant integers using
+// multiplication", PLDI 1994): with p = ceil(log2 d) and m = ceil(2^(31+p) / d), m*d lies in
+// [2^(31+p), 2^(31+p) + 2^p], hence floor(n / d) = floor(n*m / 2^(31+p)) for every n < 2^31, and
+// n*m < 2^64 because m <= 2^32 + 1. Replaces the ~20-instruction dependent sequence of a run-time
+// integer division in per-pixel index arithmetic.
+struct FastDiv {
+    unsigned long long m = 1ull << 31;
+    int s = 31;
+    int d = 1;
+    FastDiv() = default;
+    explicit FastDiv(int divisor) : d(divisor) {
+        int p = 0;
+        while ((1ll << p) < divisor) p++;
+        m = ((1ull << (31 + p)) + (unsigned long long)divisor - 1) / (unsigned long long)divisor;
+        s = 31 + p;
+    }
+    __host__ __device__ __forceinline__ int div(int n) const {
+        return (int)(((unsigned long long)(unsigned)n * m) >> s);
+    }
+};
+
 __device__ __forceinline__ int32_t dev_clamp(int32_t v, int32_t lo, int32_t hi) {
     return v < lo ? lo : (v > hi ? hi : v);
 }

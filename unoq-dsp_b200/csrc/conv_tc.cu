@@ -52,11 +52,17 @@ namespace {
 constexpr int kBM = 128;              // pixels per tile = TMEM lanes
 constexpr int kBK = 128;              // reduction bytes per stage (one 128-byte swizzle row)
 constexpr int kStageBytes = kBM * kBK;
-constexpr int kProducerWarps = 4;
+constexpr int kProducerWarps = 8;
 constexpr int kEpilogueWarps = 8;     // two warps per TMEM lane quarter, alternating 16-column chunks
 constexpr int kMmaWarp = kProducerWarps + kEpilogueWarps;
 constexpr int kThreads = (kMmaWarp + 1) * 32;
 constexpr int kProducers = kProducerWarps * 32;
+// 16-byte-chunk producers: thread t builds chunk t % 8 of rows t / 8 + kRowStep * i, i < kRowIters.
+constexpr int kRowStep = kProducers / 8;
+constexpr int kRowIters = kBM / kRowStep;
+// word-assembly producers: thread t builds chunks t / kBM + kChunkStep * k of row t % kBM.
+constexpr int kChunkStep = kProducers / kBM;
+static_assert(kBM % kRowStep == 0 && kProducers % kBM == 0, "producer mapping");
 constexpr int kEpilogues = kEpilogueWarps * 32;
 constexpr int kMaxSmem = 227 * 1024;
 constexpr int kWeightBudget = 96 * 1024;
@@ -70,10 +76,11 @@ struct Params {
     const int8_t *w;           // [n_tiles][kc][BN x 128] swizzled
     const EpiChan *epi;        // [n_tiles * BN]
     const uint8_t *post;       // 256 bytes or null
-    const int *tab;            // band mode taps: (ky*dh) << 20 | (kx*dw) << 10 | c, per k < K
+    const int *tab;            // band mode: chunk taps (ic % 16 == 0) or word sources (else), see conv_tc_prepare
     const int8_t *fill;        // 16 bytes of the input zero point
     long long x_bytes;         // bytes of the whole (batched) input tensor
     int M;                     // total output pixels
+    FastDiv f_ow, f_img;       // division by ow and by oh*ow (pixel index -> n, oy, ox)
     int ih, iw, ic, oh, ow, oc;
     int kh, kw, sh, sw, dh, dw, pt, pl;
     int K;                     // kh*kw*ic (unpadded)
@@ -84,38 +91,49 @@ struct Params {
     int xzp;
     int tmem_cols;
     int mode;
-    int band_bytes;            // per band buffer (band mode)
+    int band_bytes;            // per band buffer (band mode): band_rows x pitch
     int nbands;                // band buffers in rotation (band mode)
+    int band_rows;             // most input rows any tile's band spans
+    int pitch;                 // band row: ml margin bytes, iw*ic data bytes, right margin (multiple of 16)
+    int ml;                    // left margin bytes (multiple of 16)
+    int row16;                 // 16-byte chunks of one input row
+    int fill_bytes;            // zero-point row read for taps above / below the image
+    int K32;                   // K rounded up to 32
+    int tab_bytes;             // size of the band table
     int epi_mode;              // EpiMode
     int n_acc;                 // TMEM accumulators in rotation (2 or 4)
     int store_tma;             // 1: staged tile leaves by TMA tensor store; 0: cooperative stores
-    int box;                   // TMA box inner bytes = min(bn, 128)
+    int box;                   // TMA store box: columns of one epilogue warp (max(16, bn / 2)) x 32 rows
+    int out_bytes;             // output staging: per-warp double buffers (TMA) or two whole tiles
     int swz;                   // staging swizzle: 0 none (16 B rows), 1 = 32 B, 2 = 64 B, 3 = 128 B span
 };
 
-// One staging buffer of the output tile: 128 rows, padded rows for cooperative stores or
-// swizzled sub-tiles for the TMA store; 1024-byte aligned so swizzle atoms line up.
+// One staging buffer of the output tile for cooperative stores: 128 padded rows.
 __host__ __device__ inline size_t out_stride(int bn) { return ((size_t)kBM * (bn + 16) + 1023) & ~(size_t)1023; }
+// One epilogue warp's staging buffer for the TMA store: 32 rows x box bytes, swizzled like the
+// box, 1024-byte aligned so swizzle atoms line up.
+__host__ __device__ inline size_t warp_stage_bytes(int box) { return ((size_t)32 * box + 1023) & ~(size_t)1023; }
 
 // Shared-memory carve-up, identical on host (sizing) and device.
 struct Layout {
     size_t a, b, out, band, epi, lut, tab, bars, total;
-    __host__ __device__ Layout(int stages, int kc, int bn, int band_bytes, int nbands) {
+    __host__ __device__ Layout(int stages, int kc, int bn, int band_bytes, int nbands, int fill_bytes, int tab_bytes,
+                               int out_bytes) {
         size_t o = 0;
         a = o;
         o += (size_t)stages * kStageBytes;
         b = o;
         o += (size_t)kc * bn * kBK;
         out = o;
-        o += 2 * out_stride(bn);
+        o += (size_t)out_bytes;
         band = o;
-        o += (size_t)nbands * (size_t)((band_bytes + 15) & ~15);
+        o += (size_t)nbands * (size_t)band_bytes + (size_t)fill_bytes;
         epi = (o + 31) & ~(size_t)31;
         o = epi + (size_t)bn * sizeof(EpiChan);
         lut = o;
         o += 256;
-        tab = o;
-        o += 4 * kBK;
+        tab = (o + 15) & ~(size_t)15;
+        o = tab + (size_t)tab_bytes;
         bars = (o + 7) & ~(size_t)7;
         o = bars + (size_t)(2 * stages + 14) * 8 + 16;
         total = o + 1024;  // base alignment slack
@@ -203,6 +221,20 @@ __device__ __forceinline__ void fence_proxy_async() {
 __device__ __forceinline__ void st_shared16(uint32_t dst, uint4 v) {
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                  : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_shared16(uint32_t src) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(src));
+    return v;
+}
+// Four bytes at any shared-memory address: two aligned words joined by a funnel shift.
+__device__ __forceinline__ uint32_t ld_shared_u32_unaligned(uint32_t addr) {
+    const uint32_t base = addr & ~3u;
+    uint32_t lo, hi;
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(lo) : "r"(base));
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(hi) : "r"(base + 4));
+    return __funnelshift_r(lo, hi, (addr & 3u) * 8);
 }
 
 // UMMA shared-memory descriptor: K-major, SWIZZLE_128B, 8-row atoms 1024 bytes apart.
@@ -320,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const int S = p.stages;
-    const Layout L(S, p.kc, p.bn, p.band_bytes, p.nbands);
+    const Layout L(S, p.kc, p.bn, p.band_bytes, p.nbands, p.fill_bytes, p.tab_bytes, p.out_bytes);
     uint8_t *sA = smem + L.a;
     uint8_t *sB = smem + L.b;
     uint8_t *sOut = smem + L.out;
@@ -373,7 +405,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     if (p.post)
         for (int i = threadIdx.x; i < 256; i += blockDim.x) sLut[i] = p.post[i];
     if (p.mode == kBand)
-        for (int i = threadIdx.x; i < p.K; i += blockDim.x) sTab[i] = p.tab[i];
+        for (int i = threadIdx.x; i < (p.tab_bytes >> 2); i += blockDim.x) sTab[i] = p.tab[i];
     if (warp == kMmaWarp) {  // the MMA warp owns the TMEM allocation
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(p.tmem_cols));
@@ -398,28 +430,27 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
         long long it = 0;
         if (p.mode != kBand) {
             const int j = t & 7;    // 16-byte chunk of the 128-byte stage row
-            const int r0 = t >> 3;  // rows r0 + 16 i, i = 0..7
+            const int r0 = t >> 3;  // rows r0 + kRowStep i
             // Each stage's copies are tracked per thread with cp.async groups; a warp signals
             // stage `it - lag` once all its lanes have seen that group land (one barrier arrival
             // per warp). The lag keeps up to lag + 1 stages of copies in flight per thread.
             const int lag = S - 1 < 3 ? S - 1 : 3;
             int pending = 0;
             for (int mt = blockIdx.x; mt < m_tiles; mt += gridDim.x) {
-                const int8_t *rbase[8];
-                int ry[8], rx[8];
-                bool rvalid[8];
+                const int8_t *rbase[kRowIters];
+                int ry[kRowIters], rx[kRowIters];
+                bool rvalid[kRowIters];
 #pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    const int m = mt * kBM + r0 + 16 * i;
+                for (int i = 0; i < kRowIters; i++) {
+                    const int m = mt * kBM + r0 + kRowStep * i;
                     rvalid[i] = m < p.M;
                     const int mm = rvalid[i] ? m : 0;
                     if (p.mode == kPointwise) {
                         rbase[i] = p.x + (size_t)mm * p.ic;
                         ry[i] = rx[i] = 0;
                     } else {
-                        const int ox = mm % p.ow;
-                        const int oy = (mm / p.ow) % p.oh;
-                        const int n = mm / (p.ow * p.oh);
+                        const int n = p.f_img.div(mm), rem = mm - n * p.f_img.d;
+                        const int oy = p.f_ow.div(rem), ox = rem - oy * p.ow;
                         rbase[i] = p.x + (size_t)n * p.ih * p.iw * p.ic;
                         ry[i] = oy * p.sh - p.pt;
                         rx[i] = ox * p.sw - p.pl;
@@ -437,8 +468,8 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
                     if (k < p.K) {
                         if (p.mode == kPointwise) {
 #pragma unroll
-                            for (int i = 0; i < 8; i++) {
-                                const int r = r0 + 16 * i;
+                            for (int i = 0; i < kRowIters; i++) {
+                                const int r = r0 + kRowStep * i;
                                 const uint32_t dst = stage + (r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4);
                                 if (rvalid[i]) cp_async16(dst, rbase[i] + k);
                             }
@@ -447,8 +478,8 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
                             const int ky = tap / p.kw, kx = tap - ky * p.kw;
                             const int dy = ky * p.dh, dx = kx * p.dw;
 #pragma unroll
-                            for (int i = 0; i < 8; i++) {
-                                const int r = r0 + 16 * i;
+                            for (int i = 0; i < kRowIters; i++) {
+                                const int r = r0 + kRowStep * i;
                                 const uint32_t dst = stage + (r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4);
                                 if (!rvalid[i]) continue;
                                 const int iy = ry[i] + dy, ix = rx[i] + dx;
@@ -475,84 +506,144 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
             if (lane == 0)
                 for (long long q = it - pending; q < it; q++) mbar_arrive(smem_u32(full + (int)(q % S)));
         } else {
-            // Band mode: one K stage per tile (K <= 128), thread t builds pixel row t.
-            const size_t row_bytes = (size_t)p.iw * p.ic;
+            // Band mode: the input rows a tile touches (its "band") are copied to shared memory with
+            // contiguous 16-byte cp.async, each row framed by margins of the input zero point, with
+            // up to nb bands in flight; A rows are then assembled from the band. Rows above or below
+            // the image read a shared row of zero-point bytes instead.
+            const int pitch = p.pitch, ML = p.ml;
+            const uint32_t buf_bytes = (uint32_t)p.band_bytes;
+            const uint32_t band0 = smem_u32(sBand), fillrow = band0 + (uint32_t)p.nbands * buf_bytes + 16;
+            const uint32_t fill4 = 0x01010101u * (uint32_t)(uint8_t)p.xzp;
+            {
+                const uint4 f = make_uint4(fill4, fill4, fill4, fill4);
+                const int data16 = p.row16, margin16 = (pitch >> 4) - data16;
+                const int slots = p.nbands * p.band_rows;
+                for (int q = t; q < slots * margin16; q += kProducers) {
+                    const int row = q / margin16, c = q - row * margin16;
+                    const int col = c < (ML >> 4) ? c * 16 : ML + data16 * 16 + (c - (ML >> 4)) * 16;
+                    const int b = row / p.band_rows, r = row - b * p.band_rows;
+                    st_shared16(band0 + (uint32_t)b * buf_bytes + (uint32_t)(r * pitch + col), f);
+                }
+                for (int q = t; q < (p.fill_bytes >> 4); q += kProducers) st_shared16(fillrow - 16 + q * 16, f);
+            }
             unsigned round = 0;
-            // band of tile `mt`: global input rows [g_lo, g_hi] (image-major rows are contiguous)
-            auto band_of = [&](int mt, long long &g_lo, long long &lead, long long &chunks) {
+            const long long row_bytes = (long long)p.iw * p.ic;
+            // band of tile `mt`: global input rows [g_lo, g_lo + rows) (image-major rows are contiguous)
+            auto band_of = [&](int mt, long long &g_lo, int &rows) {
                 const int m0 = mt * kBM, m1 = min(p.M, m0 + kBM) - 1;
-                const int n0 = m0 / (p.oh * p.ow), oy0 = (m0 / p.ow) % p.oh;
-                const int n1 = m1 / (p.oh * p.ow), oy1 = (m1 / p.ow) % p.oh;
+                const int n0 = p.f_img.div(m0), oy0 = p.f_ow.div(m0 - n0 * p.f_img.d);
+                const int n1 = p.f_img.div(m1), oy1 = p.f_ow.div(m1 - n1 * p.f_img.d);
                 g_lo = (long long)n0 * p.ih + max(0, oy0 * p.sh - p.pt);
-                const long long g_hi = (long long)n1 * p.ih + min(p.ih - 1, oy1 * p.sh - p.pt + (p.kh - 1) * p.dh);
-                const long long start = g_lo * (long long)row_bytes, aligned = start & ~15ll;
-                lead = start - aligned;
-                const long long end = min((g_hi + 1) * (long long)row_bytes, p.x_bytes);
-                chunks = (end - aligned + 15) >> 4;
+                const long long g_hi =
+                    (long long)n1 * p.ih + max(-1, min(p.ih - 1, oy1 * p.sh - p.pt + (p.kh - 1) * p.dh));
+                rows = g_hi >= g_lo ? (int)(g_hi - g_lo + 1) : 0;
             };
             auto prefetch = [&](int mt, int buf) {
-                long long g_lo, lead, chunks;
-                band_of(mt, g_lo, lead, chunks);
-                const uint8_t *src = reinterpret_cast<const uint8_t *>(p.x) + ((g_lo * (long long)row_bytes) & ~15ll);
-                const uint32_t dst = smem_u32(sBand + (size_t)buf * ((p.band_bytes + 15) & ~15));
-                for (long long q = t; q < chunks; q += kProducers) cp_async16(dst + (uint32_t)(q * 16), src + q * 16);
+                long long g_lo;
+                int rows;
+                band_of(mt, g_lo, rows);
+                const uint8_t *src = reinterpret_cast<const uint8_t *>(p.x) + g_lo * row_bytes;
+                const uint32_t dst = band0 + (uint32_t)buf * buf_bytes + (uint32_t)ML;
+                for (int r = warp; r < rows; r += kProducerWarps)
+                    for (int c = lane; c < p.row16; c += 32)
+                        cp_async16(dst + (uint32_t)(r * pitch + c * 16), src + r * row_bytes + c * 16);
                 cp_async_commit();
             };
-            // Up to nb bands in flight: tiles i .. i + nb - 1 are prefetched while tile i is built.
             const int nb = p.nbands;
             int i_tile = 0, fetched = 0;  // tiles of this CTA whose band has been requested
             const int my_tiles = blockIdx.x < m_tiles ? (m_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
             for (; fetched < nb - 1 && fetched < my_tiles; fetched++)
                 prefetch(blockIdx.x + fetched * gridDim.x, fetched % nb);
-            for (int mt = blockIdx.x; mt < m_tiles; mt += gridDim.x, i_tile++, it++) {
-                const int buf = i_tile % nb;
+            bool ok = true;
+            for (int mt = blockIdx.x; mt < m_tiles && ok; mt += gridDim.x, i_tile++) {
+                const uint32_t bandb = band0 + (uint32_t)(i_tile % nb) * buf_bytes;
                 if (fetched < my_tiles) {
                     prefetch(blockIdx.x + fetched * gridDim.x, fetched % nb);
                     fetched++;
                 }
-                cp_async_wait_dyn(fetched - i_tile - 1);  // band of tile i_tile has landed
-                if (!role_sync(smem_u32(psync), round, abort, 106)) break;  // ... for every thread
-                const int s = (int)(it % S);
-                if (!mbar_wait(smem_u32(empty + s), (uint32_t)(((it / S) & 1) ^ 1), abort, 101)) break;
-                long long g_lo, lead, chunks;
-                band_of(mt, g_lo, lead, chunks);
-                const uint8_t *band = sBand + (size_t)buf * ((p.band_bytes + 15) & ~15) + lead;
-                const uint32_t stage = smem_u32(sA + (size_t)s * kStageBytes);
-                const int m = mt * kBM + t;
-                if (m < p.M) {
-                    const int ox = m % p.ow, oy = (m / p.ow) % p.oh, n = m / (p.ow * p.oh);
-                    const int y0 = oy * p.sh - p.pt, x0 = ox * p.sw - p.pl;
-                    const long long grow0 = (long long)n * p.ih - g_lo;
-                    const int chunks16 = (p.K + 15) >> 4;
-                    for (int jj = 0; jj < chunks16; jj++) {
-                        uint32_t words[4];
+                cp_async_wait_dyn(fetched - i_tile - 1);  // this thread's copies of tile i_tile's band
+                if (!role_sync(smem_u32(psync), round, abort, 106)) break;  // ... and everyone's
+                long long g_lo;
+                int rows;
+                band_of(mt, g_lo, rows);
+                if (p.ic % 16 == 0) {
+                    // 16-byte chunks: thread (j = t % 8, r0 = t / 8) builds chunk j of rows r0 + kRowStep i.
+                    const int j = t & 7, r0 = t >> 3;
+                    int y0[kRowIters], rb[kRowIters], cb[kRowIters];
 #pragma unroll
-                        for (int w4 = 0; w4 < 4; w4++) {
-                            uint32_t word = 0;
-#pragma unroll
-                            for (int b = 0; b < 4; b++) {
-                                const int kk = jj * 16 + w4 * 4 + b;
-                                int v = 0;
-                                if (kk < p.K) {
-                                    const int e = sTab[kk];
-                                    const int iy = y0 + (e >> 20), ix = x0 + ((e >> 10) & 1023);
-                                    v = (iy >= 0 && ix >= 0 && iy < p.ih && ix < p.iw)
-                                            ? (int)(int8_t)band[(grow0 + iy) * (long long)row_bytes + ix * p.ic + (e & 1023)]
-                                            : p.xzp;
-                                }
-                                word |= (uint32_t)(uint8_t)v << (b * 8);
-                            }
-                            words[w4] = word;
-                        }
-                        const int r = t;
-                        st_shared16(stage + (r >> 3) * 1024 + (r & 7) * 128 + ((jj ^ (r & 7)) << 4),
-                                    make_uint4(words[0], words[1], words[2], words[3]));
+                    for (int i = 0; i < kRowIters; i++) {
+                        const int m = mt * kBM + r0 + kRowStep * i;
+                        const int n = p.f_img.div(m), rem = m - n * p.f_img.d;
+                        const int oy = p.f_ow.div(rem), ox = rem - oy * p.ow;
+                        y0[i] = m < p.M ? oy * p.sh - p.pt : -(1 << 20);  // rows past M read the fill row
+                        rb[i] = (int)((long long)n * p.ih - g_lo);
+                        cb[i] = ML + (ox * p.sw - p.pl) * p.ic;
                     }
+                    for (int kc = 0; kc < p.kc; kc++, it++) {
+                        const int s = (int)(it % S);
+                        if (!mbar_wait(smem_u32(empty + s), (uint32_t)(((it / S) & 1) ^ 1), abort, 101)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t stage = smem_u32(sA + (size_t)s * kStageBytes);
+                        const int e = sTab[kc * 8 + j];
+                        if (e >= 0) {
+                            const int dy = e >> 20, off = e & 0xFFFFF;
+#pragma unroll
+                            for (int i = 0; i < kRowIters; i++) {
+                                const int r = r0 + kRowStep * i, iy = y0[i] + dy;
+                                const uint32_t src = (iy >= 0 && iy < p.ih)
+                                                         ? bandb + (uint32_t)((rb[i] + iy) * pitch + cb[i] + off)
+                                                         : fillrow + (uint32_t)off;
+                                st_shared16(stage + (r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4),
+                                            ld_shared16(src));
+                            }
+                        }
+                        fence_proxy_async();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(smem_u32(full + s));
+                    }
+                } else {
+                    // One K stage (K <= 128); thread t builds row t % 128 word by word, chunks
+                    // t / 128 + kChunkStep k. Word w takes its
+                    // bytes from at most two kernel rows (runs of kw*ic contiguous band bytes):
+                    // table entry {dy_a, off_a, dy_b, off_b, mask_a, mask_b}, dy = -1 for none.
+                    const int s = (int)(it % S);
+                    if (!mbar_wait(smem_u32(empty + s), (uint32_t)(((it / S) & 1) ^ 1), abort, 101)) break;
+                    const uint32_t stage = smem_u32(sA + (size_t)s * kStageBytes);
+                    const int row = t % kBM;
+                    const int m = mt * kBM + row;
+                    if (m < p.M) {
+                        const int n = p.f_img.div(m), rem = m - n * p.f_img.d;
+                        const int oy = p.f_ow.div(rem), ox = rem - oy * p.ow;
+                        const int y0 = oy * p.sh - p.pt, rb = (int)((long long)n * p.ih - g_lo);
+                        const int cb = ML + (ox * p.sw - p.pl) * p.ic;
+                        auto run = [&](int dy) -> uint32_t {
+                            const int iy = y0 + dy;
+                            return (iy >= 0 && iy < p.ih) ? bandb + (uint32_t)((rb + iy) * pitch + cb) : fillrow;
+                        };
+                        const int4 *wt = reinterpret_cast<const int4 *>(sTab);
+                        const int chunks = p.K32 >> 4;
+                        for (int c = t / kBM; c < chunks; c += kChunkStep) {
+                            uint32_t words[4];
+#pragma unroll
+                            for (int w4 = 0; w4 < 4; w4++) {
+                                const int4 ea = wt[2 * (c * 4 + w4)], eb = wt[2 * (c * 4 + w4) + 1];
+                                uint32_t v = 0;
+                                if (ea.x >= 0) v = ld_shared_u32_unaligned(run(ea.x) + ea.y) & (uint32_t)eb.x;
+                                if (ea.z >= 0) v |= ld_shared_u32_unaligned(run(ea.z) + ea.w) & (uint32_t)eb.y;
+                                words[w4] = v;
+                            }
+                            st_shared16(stage + (row >> 3) * 1024 + (row & 7) * 128 + ((c ^ (row & 7)) << 4),
+                                        make_uint4(words[0], words[1], words[2], words[3]));
+                        }
+                    }
+                    fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(smem_u32(full + s));
+                    it++;
                 }
-                fence_proxy_async();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(smem_u32(full + s));
-                if (!role_sync(smem_u32(psync), round, abort, 107)) break;  // band `buf` free for reuse
+                if (!ok || !role_sync(smem_u32(psync), round, abort, 107)) break;  // band free for reuse
             }
         }
         cp_async_wait<0>();
@@ -601,7 +692,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     } else {
         // ------------------------------------------------------------------ epilogue
         const int e = warp - kProducerWarps;
-        const int et = threadIdx.x - kProducers;  // 0..255
+        const int et = threadIdx.x - kProducers;  // 0..kEpilogues-1
         const int quarter = e & 3;                // TMEM lanes 32*quarter .. +31 (warp id % 4 rule)
         const int half = e >> 2;                  // which 16-column chunks this warp takes
         const int row = quarter * 32 + lane;
@@ -610,61 +701,84 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
         const int cols = min(p.bn, p.oc - n0);
         const int live_chunks = (cols + 15) / 16;
         const int vw = (p.oc & 15) == 0 ? 16 : (p.oc & 7) == 0 ? 8 : (p.oc & 3) == 0 ? 4 : 1;
-        const int box_chunks = p.box / 16;
-        const int swz_row = p.swz == 3 ? (row & 7) : p.swz == 2 ? ((row >> 1) & 3) : p.swz == 1 ? ((row >> 2) & 1) : 0;
         unsigned round = 0;
         int lt = 0;
-        for (int mt = blockIdx.x; mt < m_tiles; mt += gridDim.x, lt++) {
-            const int acc = lt % p.n_acc;
-            if (!mbar_wait(smem_u32(tfull + acc), (uint32_t)((lt / p.n_acc) & 1), abort, 105)) break;
-            tc_fence_after();
-            uint8_t *stage = sOut + (size_t)(lt & 1) * out_stride(p.bn);
-            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.bn);
-            uint32_t ra[16], rb[16];
-            int ci = half;
-            if (ci < live_chunks) {
-                tmem_ld16_nowait(taddr + ci * 16, ra);
-                tmem_wait_ld(ra);
-            }
-            while (ci < live_chunks) {
-                const int next = ci + 2;
-                if (next < live_chunks) tmem_ld16_nowait(taddr + next * 16, rb);
-                const uint4 v = epilogue_chunk<EPI>(ra, E, lut, ci * 16, p.lo, p.hi);
-                uint32_t dst;
-                if (p.store_tma) {
-                    const int sub = ci / box_chunks, jj = ci - sub * box_chunks;
-                    dst = smem_u32(stage + (size_t)sub * kBM * p.box + (size_t)row * p.box + ((jj ^ swz_row) << 4));
-                } else {
-                    dst = smem_u32(stage + (size_t)row * (p.bn + 16) + ci * 16);
+        if (p.store_tma) {
+            // Each warp owns rows 32*quarter.. and the column half [half*box, half*box + box) of every
+            // tile: it stages them in its own double buffer (swizzled like the box) and stores them
+            // with its own TMA store, so no epilogue warp ever waits for another.
+            const int c0 = half * p.box;
+            const int my_chunks = c0 < cols ? (min(p.box, cols - c0) + 15) / 16 : 0;
+            const int swz_row = p.swz == 3 ? (lane & 7) : p.swz == 2 ? ((lane >> 1) & 3) : p.swz == 1 ? ((lane >> 2) & 1) : 0;
+            const size_t wsb = warp_stage_bytes(p.box);
+            uint8_t *wstage0 = sOut + (size_t)e * 2 * wsb;
+            for (int mt = blockIdx.x; mt < m_tiles; mt += gridDim.x, lt++) {
+                const int acc = lt % p.n_acc;
+                if (!mbar_wait(smem_u32(tfull + acc), (uint32_t)((lt / p.n_acc) & 1), abort, 105)) break;
+                tc_fence_after();
+                uint8_t *stage = wstage0 + (size_t)(lt & 1) * wsb;
+                // this buffer's previous store (two tiles back) must have been read out
+                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                __syncwarp();
+                const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.bn + c0);
+                uint32_t ra[16], rb[16];
+                if (my_chunks > 0) {
+                    tmem_ld16_nowait(taddr, ra);
+                    tmem_wait_ld(ra);
                 }
-                st_shared16(dst, v);
-                if (next < live_chunks) tmem_wait_ld(rb);
+                for (int ci = 0; ci < my_chunks; ci++) {
+                    const bool more = ci + 1 < my_chunks;
+                    if (more) tmem_ld16_nowait(taddr + (ci + 1) * 16, rb);
+                    const uint4 v = epilogue_chunk<EPI>(ra, E, lut, c0 + ci * 16, p.lo, p.hi);
+                    st_shared16(smem_u32(stage + (size_t)lane * p.box + ((ci ^ swz_row) << 4)), v);
+                    if (more) tmem_wait_ld(rb);
 #pragma unroll
-                for (int q = 0; q < 16; q++) ra[q] = rb[q];
-                ci = next;
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(tempty + acc));  // accumulator free for reuse
-            const int m0 = mt * kBM;
-            if (p.store_tma) {
+                    for (int q = 0; q < 16; q++) ra[q] = rb[q];
+                }
+                tc_fence_before();
                 fence_proxy_async();  // staged bytes visible to the TMA (async proxy)
-                if (et == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // previous store read out
-            }
-            if (!role_sync(smem_u32(esync), round, abort, 108)) break;  // tile staged by all threads
-            if (p.store_tma) {
-                if (et == 0) {
-                    for (int sub = 0; sub * p.box < cols; sub++) {
-                        const uint32_t src = smem_u32(stage + (size_t)sub * kBM * p.box);
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(smem_u32(tempty + acc));  // accumulator free for reuse
+                    const int r0 = mt * kBM + quarter * 32;
+                    if (my_chunks > 0 && r0 < p.M)
                         asm volatile(
                             "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
                                 reinterpret_cast<uint64_t>(&p.ymap)),
-                            "r"(src), "r"(n0 + sub * p.box), "r"(m0)
+                            "r"(smem_u32(stage)), "r"(n0 + c0), "r"(r0)
                             : "memory");
-                    }
                     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
                 }
-            } else {
+            }
+            if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        } else {
+            for (int mt = blockIdx.x; mt < m_tiles; mt += gridDim.x, lt++) {
+                const int acc = lt % p.n_acc;
+                if (!mbar_wait(smem_u32(tfull + acc), (uint32_t)((lt / p.n_acc) & 1), abort, 105)) break;
+                tc_fence_after();
+                uint8_t *stage = sOut + (size_t)(lt & 1) * out_stride(p.bn);
+                const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.bn);
+                uint32_t ra[16], rb[16];
+                int ci = half;
+                if (ci < live_chunks) {
+                    tmem_ld16_nowait(taddr + ci * 16, ra);
+                    tmem_wait_ld(ra);
+                }
+                while (ci < live_chunks) {
+                    const int next = ci + 2;
+                    if (next < live_chunks) tmem_ld16_nowait(taddr + next * 16, rb);
+                    const uint4 v = epilogue_chunk<EPI>(ra, E, lut, ci * 16, p.lo, p.hi);
+                    st_shared16(smem_u32(stage + (size_t)row * (p.bn + 16) + ci * 16), v);
+                    if (next < live_chunks) tmem_wait_ld(rb);
+#pragma unroll
+                    for (int q = 0; q < 16; q++) ra[q] = rb[q];
+                    ci = next;
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(tempty + acc));  // accumulator free for reuse
+                const int m0 = mt * kBM;
+                if (!role_sync(smem_u32(esync), round, abort, 108)) break;  // tile staged by all threads
                 // cooperative coalesced copy-out of the staged tile: rows m0.., columns n0..n0+cols
                 const int rows = min(kBM, p.M - m0);
                 const int cpr = cols / vw;
@@ -681,7 +795,6 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
                 }
             }
         }
-        if (p.store_tma && et == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     }
 
     tc_fence_before();
@@ -702,21 +815,43 @@ struct ConvTc {
     size_t smem = 0;
 };
 
-// Largest band (bytes, including the 16-byte alignment lead) any 128-pixel tile of this layer
-// needs; the pattern repeats every lcm(128, oh*ow) pixels.
-static long long max_band_bytes(const ConvGeom &g) {
+// Band geometry of a layer. Each band row holds one input row (iw*ic bytes, a multiple of 16 so
+// rows copy as whole 16-byte chunks) between margins of the input zero point wide enough for every
+// tap left / right of the image plus the few bytes a word read may run over; rows = the most input
+// rows any 128-pixel tile touches (the pattern repeats every lcm(128, oh*ow) pixels).
+struct BandGeom {
+    int rows = 0, pitch = 0, ml = 0, fill_bytes = 0;
+    long long bytes() const { return (long long)rows * pitch; }
+};
+
+static long long round16(long long v) { return (v + 15) & ~15ll; }
+
+static bool band_geometry(const ConvGeom &g, BandGeom &bg) {
+    const long long row_bytes = (long long)g.iw * g.ic;
+    if (row_bytes % 16 != 0) return false;
+    if (g.ic % 16 != 0 && g.dw != 1) return false;  // word assembly needs contiguous kx runs
+    const long long x0_max = (long long)(g.ow - 1) * g.sw - g.pl;
+    const long long over = std::max<long long>(0, (x0_max + (long long)(g.kw - 1) * g.dw + 1 - g.iw) * g.ic);
+    const long long ml = round16((long long)g.pl * g.ic + 8), mr = round16(over + 16);
+    const long long pitch = ml + row_bytes + mr;
+    const long long span = ((long long)(g.kw - 1) * g.dw + 1) * g.ic;
     const long long img = (long long)g.oh * g.ow;
     const long long period = img / std::gcd(img, (long long)kBM) * kBM;
-    const long long row_bytes = (long long)g.iw * g.ic;
-    long long worst = 0;
+    long long rows = 0;
     for (long long m0 = 0; m0 < period; m0 += kBM) {
         const long long m1 = m0 + kBM - 1;
         const long long n0 = m0 / img, oy0 = (m0 / g.ow) % g.oh, n1 = m1 / img, oy1 = (m1 / g.ow) % g.oh;
         const long long lo = n0 * g.ih + std::max<long long>(0, oy0 * g.sh - g.pt);
-        const long long hi = n1 * g.ih + std::min<long long>(g.ih - 1, oy1 * g.sh - g.pt + (long long)(g.kh - 1) * g.dh);
-        worst = std::max(worst, (hi - lo + 1) * row_bytes + 15 + 16);
+        const long long hi =
+            n1 * g.ih + std::max<long long>(-1, std::min<long long>(g.ih - 1, oy1 * g.sh - g.pt + (long long)(g.kh - 1) * g.dh));
+        rows = std::max(rows, hi - lo + 1);
     }
-    return worst;
+    if (rows * pitch > 64 * 1024 || pitch > (1 << 20) || (long long)(g.kh - 1) * g.dh >= 2048) return false;
+    bg.rows = (int)std::max<long long>(rows, 1);
+    bg.pitch = (int)pitch;
+    bg.ml = (int)ml;
+    bg.fill_bytes = (int)round16(16 + span + 16);
+    return true;
 }
 
 int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *post_dev, const ConvGeom &g,
@@ -731,14 +866,9 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
     if (g.kh == 1 && g.kw == 1 && g.sh == 1 && g.sw == 1 && g.pt == 0 && g.pl == 0 && g.ih == g.oh && g.iw == g.ow &&
         g.ic % 16 == 0)
         mode = kPointwise;
-    long long band = 0;
-    if (g.ic % 16 != 0) {
-        // Band gather handles one K stage (3-channel stem: K = 27; 8-channel 3x3: K = 72).
-        if (kc != 1 || (g.kh - 1) * g.dh >= 2048 || (g.kw - 1) * g.dw >= 1024 || g.ic > 1023) return 0;
-        mode = kBand;
-        band = max_band_bytes(g);
-        if (band > 48 * 1024) return 0;
-    }
+    BandGeom bg;
+    if (mode != kPointwise && (g.ic % 16 == 0 || kc == 1) && band_geometry(g, bg)) mode = kBand;
+    if (mode == kGather16 && g.ic % 16 != 0) return 0;
     // N tiling: a power-of-two tile width (16..256, so staged tiles match a TMA swizzle span)
     // no wider than the channel count needs, whose weights stay resident in shared memory.
     int bn = 16;
@@ -746,10 +876,30 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
     while (bn > 16 && (size_t)kc * bn * kBK > (size_t)kWeightBudget) bn /= 2;
     if ((size_t)kc * bn * kBK > (size_t)kWeightBudget) return 0;
     const int n_tiles = (g.oc + bn - 1) / bn;
-    int stages = 8, nbands = band ? 4 : 0;
-    while (stages > 2 && Layout(stages, kc, bn, (int)band, nbands).total > (size_t)kMaxSmem) stages--;
-    while (nbands > 2 && Layout(stages, kc, bn, (int)band, nbands).total > (size_t)kMaxSmem) nbands--;
-    if (Layout(stages, kc, bn, (int)band, nbands).total > (size_t)kMaxSmem) return 0;
+    // Band table: per 16-byte chunk (ic % 16 == 0) one int, else per 4-byte word eight ints.
+    const int tab_bytes = mode != kBand ? 16 : g.ic % 16 == 0 ? kc * 8 * 4 : (K32 / 4) * 32;
+    int stages = 8, nbands = 0;
+    const bool store_tma = (g.oc % 16) == 0;
+    const int box = std::max(16, bn / 2);
+    const int out_bytes = store_tma ? (int)(2 * kEpilogueWarps * warp_stage_bytes(box)) : (int)(2 * out_stride(bn));
+    auto layout = [&]() {
+        return Layout(stages, kc, bn, mode == kBand ? (int)bg.bytes() : 0, nbands, mode == kBand ? bg.fill_bytes : 0,
+                      tab_bytes, out_bytes);
+    };
+    if (mode == kBand) {
+        nbands = 3;
+        while (stages > 4 && layout().total > (size_t)kMaxSmem) stages--;
+        while (nbands > 2 && layout().total > (size_t)kMaxSmem) nbands--;
+        while (stages > 2 && layout().total > (size_t)kMaxSmem) stages--;
+        if (layout().total > (size_t)kMaxSmem) {
+            if (g.ic % 16 != 0) return 0;
+            mode = kGather16;
+            nbands = 0;
+            stages = 8;
+        }
+    }
+    while (stages > 2 && layout().total > (size_t)kMaxSmem) stages--;
+    if (layout().total > (size_t)kMaxSmem) return 0;
 
     // Weights: reference packed layout (gemm.h:9) -> per N tile, per K stage, UMMA SW128 K-major.
     const int kp = q[18];
@@ -787,10 +937,39 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
     const int epi_mode = !fast ? kGeneral : (q[14] >= yzp ? kRelu : kTies);
     if (epi_mode != kGeneral)
         for (auto &e : epi) e.sh = e.sh >= 32 ? e.sh - 32 : 0;  // shift of the high word
-    std::vector<int> tab(kBK, 0);
-    for (int t = 0; t < K && t < kBK; t++) {
-        const int tap = t / g.ic, c = t % g.ic;
-        tab[t] = ((tap / g.kw) * g.dh) << 20 | ((tap % g.kw) * g.dw) << 10 | c;
+    std::vector<int> tab(tab_bytes / 4, 0);
+    if (mode == kBand && g.ic % 16 == 0) {
+        // chunk j = reduction bytes [16 j, 16 j + 16): (ky*dh) << 20 | byte offset in the kernel-row
+        // run (kx*dw*ic + c); -1 past K (its weights are zero, the A bytes are left as they are)
+        for (int j = 0; j < kc * 8; j++) {
+            const int t0 = j * 16;
+            if (t0 >= K) {
+                tab[j] = -1;
+                continue;
+            }
+            const int tap = t0 / g.ic, c = t0 % g.ic, ky = tap / g.kw, kx = tap % g.kw;
+            tab[j] = (ky * g.dh) << 20 | (kx * g.dw * g.ic + c);
+        }
+    } else if (mode == kBand) {
+        // word w = reduction bytes [4 w, 4 w + 4); kernel row ky contributes bytes [ky*L, ky*L + L) of
+        // the row, L = kw*ic, read from the run that starts at that tap row's first column.
+        const int L = g.kw * g.ic;
+        for (int w = 0; w < K32 / 4; w++) {
+            int *e = &tab[(size_t)w * 8];
+            e[0] = e[2] = -1;
+            for (int b = 0; b < 4; b++) {
+                const int q = 4 * w + b;
+                if (q >= K) continue;
+                const int ky = q / L;
+                if (e[0] < 0 || ky * g.dh == e[0]) {
+                    if (e[0] < 0) e[0] = ky * g.dh, e[1] = 4 * w - ky * L;
+                    e[4] |= (int)(0xFFu << (8 * b));
+                } else {
+                    if (e[2] < 0) e[2] = ky * g.dh, e[3] = 4 * w - ky * L;
+                    e[5] |= (int)(0xFFu << (8 * b));
+                }
+            }
+        }
     }
     int8_t fill[16];
     std::memset(fill, xzp, sizeof(fill));
@@ -829,6 +1008,8 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
     p.tab = static_cast<const int *>(dt);
     p.fill = static_cast<const int8_t *>(df);
     p.ih = g.ih, p.iw = g.iw, p.ic = g.ic, p.oh = g.oh, p.ow = g.ow, p.oc = g.oc;
+    p.f_ow = FastDiv(g.ow);
+    p.f_img = FastDiv(g.oh * g.ow);
     p.kh = g.kh, p.kw = g.kw, p.sh = g.sh, p.sw = g.sw, p.dh = g.dh, p.dw = g.dw, p.pt = g.pt, p.pl = g.pl;
     p.K = K;
     p.kc = kc;
@@ -838,15 +1019,23 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
     p.xzp = xzp;
     p.n_acc = bn <= 128 ? 4 : 2;
     p.tmem_cols = std::max(32, p.n_acc * bn);
-    p.store_tma = (g.oc % 16) == 0;
-    p.box = std::min(bn, 128);
+    p.store_tma = store_tma;
+    p.box = box;
+    p.out_bytes = out_bytes;
     p.swz = p.box == 128 ? 3 : p.box == 64 ? 2 : p.box == 32 ? 1 : 0;
     p.mode = mode;
-    p.band_bytes = (int)band;
+    p.band_bytes = mode == kBand ? (int)bg.bytes() : 0;
     p.nbands = nbands;
+    p.band_rows = bg.rows;
+    p.pitch = bg.pitch;
+    p.ml = bg.ml;
+    p.row16 = (int)((long long)g.iw * g.ic / 16);
+    p.fill_bytes = mode == kBand ? bg.fill_bytes : 0;
+    p.K32 = K32;
+    p.tab_bytes = tab_bytes;
     p.epi_mode = epi_mode;
     c->n_tiles = n_tiles;
-    c->smem = Layout(stages, kc, bn, (int)band, nbands).total;
+    c->smem = layout().total;
     *out = c;
     return 0;
 }
@@ -871,6 +1060,7 @@ int conv_tc_launch(const ConvTc &c, const int8_t *x, int8_t *y, const ConvGeom &
     Params p = c.p;
     p.x = x;
     p.y = y;
+    if ((long long)g.n * g.oh * g.ow >= (1ll << 31)) return 2001;  // pixel indices are 31-bit
     p.M = g.n * g.oh * g.ow;
     if (p.store_tma) {
         // Output tensor [M][oc] int8; the box is one staged sub-tile, swizzled like the staging.
@@ -878,7 +1068,7 @@ int conv_tc_launch(const ConvTc &c, const int8_t *x, int8_t *y, const ConvGeom &
         if (!enc) return 2001;
         const cuuint64_t dims[2] = {(cuuint64_t)g.oc, (cuuint64_t)p.M};
         const cuuint64_t strides[1] = {(cuuint64_t)g.oc};
-        const cuuint32_t box[2] = {(cuuint32_t)p.box, (cuuint32_t)kBM};
+        const cuuint32_t box[2] = {(cuuint32_t)p.box, 32};
         const cuuint32_t estr[2] = {1, 1};
         const CUtensorMapSwizzle sw = p.swz == 3   ? CU_TENSOR_MAP_SWIZZLE_128B
                                       : p.swz == 2 ? CU_TENSOR_MAP_SWIZZLE_64B
