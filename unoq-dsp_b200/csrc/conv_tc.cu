@@ -135,7 +135,7 @@ struct Layout {
         tab = (o + 15) & ~(size_t)15;
         o = tab + (size_t)tab_bytes;
         bars = (o + 7) & ~(size_t)7;
-        o = bars + (size_t)(2 * stages + 14) * 8 + 16;
+        o = bars + (size_t)(2 * stages + 22) * 8 + 16;
         total = o + 1024;  // base alignment slack
     }
 };
@@ -299,10 +299,22 @@ struct EpiSoA {
     const int *m, *cut, *sh, *ls, *bs, *zadd;
 };
 
+// Saturating pack of four int32 values into int8 lanes (byte i = v_i): two cvt.pack.sat, each
+// putting sat(a) in byte 1 and sat(b) in byte 0 above c's low half shifted up by 16.
+__device__ __forceinline__ uint32_t pack_sat_s8x4(int32_t v0, int32_t v1, int32_t v2, int32_t v3) {
+    uint32_t hi, d;
+    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(hi) : "r"(v3), "r"(v2), "r"(0));
+    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(v1), "r"(v0), "r"(hi));
+    return d;
+}
+
+// Requantise 16 accumulators (columns c0..c0+15 of one row) and pack them as int8. The clamp to
+// [lo, hi] (both within int8) is applied per byte after a saturating pack, which gives the same
+// bytes as clamping the int32 values.
 template <int EPI>
 __device__ __forceinline__ uint4 epilogue_chunk(const uint32_t (&r)[16], const EpiSoA &E, const uint8_t *lut, int c0,
-                                                int lo, int hi) {
-    uint32_t packed[4] = {0, 0, 0, 0};
+                                                uint32_t lo4, uint32_t hi4) {
+    uint32_t packed[4];
     const longlong2 *K2 = reinterpret_cast<const longlong2 *>(E.k + c0);
     const int4 *M4 = reinterpret_cast<const int4 *>(E.m + c0);
     const int4 *S4 = reinterpret_cast<const int4 *>(E.sh + c0);
@@ -325,24 +337,27 @@ __device__ __forceinline__ uint4 epilogue_chunk(const uint32_t (&r)[16], const E
         const int cc[4] = {cv.x, cv.y, cv.z, cv.w}, ll[4] = {lv.x, lv.y, lv.z, lv.w};
         const int bb[4] = {bv.x, bv.y, bv.z, bv.w}, zz[4] = {zv.x, zv.y, zv.z, zv.w};
         const long long kk[4] = {ka.x, ka.y, kb.x, kb.y};
+        int32_t v[4];
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const int32_t acc = (int32_t)r[g * 4 + i];
-            int32_t v;
             if (EPI == kGeneral) {
                 const int32_t a = (int32_t)(((uint32_t)acc << ll[i]) + (uint32_t)bb[i]);
                 long long p = (long long)a * mm[i] + kk[i];
                 p -= (long long)(acc <= cc[i]) << 31;
-                v = (int32_t)(p >> ss[i]) + zz[i];
+                v[i] = (int32_t)(p >> ss[i]) + zz[i];
             } else {
                 long long p = (long long)acc * mm[i] + kk[i];
                 if (EPI == kTies) p -= (long long)(acc <= cc[i]) << 31;
-                v = ((int32_t)(p >> 32)) >> ss[i];
+                v[i] = ((int32_t)(p >> 32)) >> ss[i];
             }
-            v = v < lo ? lo : (v > hi ? hi : v);
-            if (lut) v = (int8_t)lut[v + 128];
-            packed[g] |= (uint32_t)(uint8_t)v << (i * 8);
         }
+        uint32_t w = pack_sat_s8x4(v[0], v[1], v[2], v[3]);
+        w = __vmins4(__vmaxs4(w, lo4), hi4);
+        if (lut)
+            w = (uint32_t)lut[(w & 0xFF) ^ 0x80] | (uint32_t)lut[((w >> 8) & 0xFF) ^ 0x80] << 8 |
+                (uint32_t)lut[((w >> 16) & 0xFF) ^ 0x80] << 16 | (uint32_t)lut[(w >> 24) ^ 0x80] << 24;
+        packed[g] = w;
     }
     return make_uint4(packed[0], packed[1], packed[2], packed[3]);
 }
@@ -350,7 +365,9 @@ __device__ __forceinline__ uint4 epilogue_chunk(const uint32_t (&r)[16], const E
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_constant__ Params p) {
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    // 1024-byte aligned base, formed by pointer arithmetic on the __shared__ array so that every
+    // pointer derived from it stays in the shared address space (ld.shared, not generic loads).
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int S = p.stages;
     const Layout L(S, p.kc, p.bn, p.band_bytes, p.nbands, p.fill_bytes, p.tab_bytes, p.out_bytes);
     uint8_t *sA = smem + L.a;
@@ -368,7 +385,8 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     uint64_t *tfull = bars + 2 * S, *tempty = bars + 2 * S + 4;
     uint64_t *bfull = bars + 2 * S + 8, *drain = bars + 2 * S + 9;
     uint64_t *psync = bars + 2 * S + 10, *esync = bars + 2 * S + 11;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 14);
+    uint64_t *bandfull = bars + 2 * S + 14, *bandfree = bars + 2 * S + 18;  // band buffers (<= 4)
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 22);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -388,6 +406,10 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
         mbar_init(smem_u32(bfull), kProducerWarps);
         mbar_init(smem_u32(drain), 1);
         mbar_init(smem_u32(psync), kProducerWarps);
+        for (int b = 0; b < 4; b++) {
+            mbar_init(smem_u32(bandfull + b), kProducers);  // every producer, on completion of its copies
+            mbar_init(smem_u32(bandfree + b), kProducerWarps);
+        }
         mbar_init(smem_u32(esync), kEpilogueWarps);
         *abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -538,31 +560,35 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
                     (long long)n1 * p.ih + max(-1, min(p.ih - 1, oy1 * p.sh - p.pt + (p.kh - 1) * p.dh));
                 rows = g_hi >= g_lo ? (int)(g_hi - g_lo + 1) : 0;
             };
-            auto prefetch = [&](int mt, int buf) {
+            // The producers fetch the band of this CTA's tile f into buffer f % nb (warp w copies rows
+            // w, w + 8, ...) once every producer warp has released that buffer's previous band (tile
+            // f - nb); each thread's copies complete onto the buffer's band-full barrier.
+            const int nb = p.nbands;
+            const int my_tiles = blockIdx.x < m_tiles ? (m_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+            auto prefetch = [&](int f) -> bool {
+                const int b = f % nb;
+                if (f >= nb && !mbar_wait(smem_u32(bandfree + b), (uint32_t)((f / nb - 1) & 1), abort, 106)) return false;
                 long long g_lo;
                 int rows;
-                band_of(mt, g_lo, rows);
+                band_of(blockIdx.x + f * gridDim.x, g_lo, rows);
                 const uint8_t *src = reinterpret_cast<const uint8_t *>(p.x) + g_lo * row_bytes;
-                const uint32_t dst = band0 + (uint32_t)buf * buf_bytes + (uint32_t)ML;
+                const uint32_t dst = band0 + (uint32_t)b * buf_bytes + (uint32_t)ML;
                 for (int r = warp; r < rows; r += kProducerWarps)
                     for (int c = lane; c < p.row16; c += 32)
                         cp_async16(dst + (uint32_t)(r * pitch + c * 16), src + r * row_bytes + c * 16);
-                cp_async_commit();
+                asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bandfull + b))
+                             : "memory");
+                return true;
             };
-            const int nb = p.nbands;
-            int i_tile = 0, fetched = 0;  // tiles of this CTA whose band has been requested
-            const int my_tiles = blockIdx.x < m_tiles ? (m_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-            for (; fetched < nb - 1 && fetched < my_tiles; fetched++)
-                prefetch(blockIdx.x + fetched * gridDim.x, fetched % nb);
-            bool ok = true;
+            // the zero-point margins written above are read by every warp
+            bool ok = role_sync(smem_u32(psync), round, abort, 109);
+            for (int f = 0; f < nb - 1 && f < my_tiles && ok; f++) ok = prefetch(f);
+            int i_tile = 0;
             for (int mt = blockIdx.x; mt < m_tiles && ok; mt += gridDim.x, i_tile++) {
-                const uint32_t bandb = band0 + (uint32_t)(i_tile % nb) * buf_bytes;
-                if (fetched < my_tiles) {
-                    prefetch(blockIdx.x + fetched * gridDim.x, fetched % nb);
-                    fetched++;
-                }
-                cp_async_wait_dyn(fetched - i_tile - 1);  // this thread's copies of tile i_tile's band
-                if (!role_sync(smem_u32(psync), round, abort, 106)) break;  // ... and everyone's
+                const int bsel = i_tile % nb;
+                const uint32_t bandb = band0 + (uint32_t)bsel * buf_bytes;
+                if (i_tile + nb - 1 < my_tiles && !prefetch(i_tile + nb - 1)) break;
+                if (!mbar_wait(smem_u32(bandfull + bsel), (uint32_t)((i_tile / nb) & 1), abort, 110)) break;
                 long long g_lo;
                 int rows;
                 band_of(mt, g_lo, rows);
@@ -643,7 +669,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
                     if (lane == 0) mbar_arrive(smem_u32(full + s));
                     it++;
                 }
-                if (!ok || !role_sync(smem_u32(psync), round, abort, 107)) break;  // band free for reuse
+                __syncwarp();
+                if (!ok) break;
+                if (lane == 0) mbar_arrive(smem_u32(bandfree + bsel));  // this warp is done with the band
             }
         }
         cp_async_wait<0>();
@@ -697,6 +725,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
         const int half = e >> 2;                  // which 16-column chunks this warp takes
         const int row = quarter * 32 + lane;
         const uint8_t *lut = p.post ? sLut : nullptr;
+        const uint32_t lo4 = 0x01010101u * (uint32_t)(uint8_t)p.lo, hi4 = 0x01010101u * (uint32_t)(uint8_t)p.hi;
         const int n0 = ntile * p.bn;
         const int cols = min(p.bn, p.oc - n0);
         const int live_chunks = (cols + 15) / 16;
@@ -729,7 +758,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
                 for (int ci = 0; ci < my_chunks; ci++) {
                     const bool more = ci + 1 < my_chunks;
                     if (more) tmem_ld16_nowait(taddr + (ci + 1) * 16, rb);
-                    const uint4 v = epilogue_chunk<EPI>(ra, E, lut, c0 + ci * 16, p.lo, p.hi);
+                    const uint4 v = epilogue_chunk<EPI>(ra, E, lut, c0 + ci * 16, lo4, hi4);
                     st_shared16(smem_u32(stage + (size_t)lane * p.box + ((ci ^ swz_row) << 4)), v);
                     if (more) tmem_wait_ld(rb);
 #pragma unroll
@@ -767,7 +796,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
                 while (ci < live_chunks) {
                     const int next = ci + 2;
                     if (next < live_chunks) tmem_ld16_nowait(taddr + next * 16, rb);
-                    const uint4 v = epilogue_chunk<EPI>(ra, E, lut, ci * 16, p.lo, p.hi);
+                    const uint4 v = epilogue_chunk<EPI>(ra, E, lut, ci * 16, lo4, hi4);
                     st_shared16(smem_u32(stage + (size_t)row * (p.bn + 16) + ci * 16), v);
                     if (next < live_chunks) tmem_wait_ld(rb);
 #pragma unroll
