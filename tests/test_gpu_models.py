@@ -1,5 +1,8 @@
 """GPU parity on the two bundled models (BASELINE configs 2/3): raw int8 outputs bit-exact
 with the reference runtime, at batch 1 and in batches, through the C ABI and the Python API."""
+import sys
+from pathlib import Path
+
 import numpy as np
 import pytest
 
@@ -61,3 +64,38 @@ def test_python_session_unpacks_yolo_outputs(golden_models):
         ref = wire[lo:lo + spec["bytes"]].view(spec["dtype"]).reshape(spec["shape"])
         np.testing.assert_array_equal(outputs[spec["name"]], ref)
         np.testing.assert_array_equal(batch[1][spec["name"]], ref)
+
+
+# ---- whole pipelines through the public Python API ------------------------------------------
+
+def _decode_gold():
+    import json
+    sys.path.insert(0, str(Path(__file__).resolve().parent / "golden"))
+    import decode_cases
+    return decode_cases, json.loads((Path(__file__).resolve().parent / "golden" / "decode.json").read_text())
+
+
+def test_image_classifier_matches_reference_pipeline():
+    """ImageClassifier (bundled center-crop profile, softmax, top-5) on the GPU against the
+    reference's ImageClassifier driven by the reference runtime, on seeded images."""
+    from unoq_dsp import ImageClassifier
+    dc, gold = _decode_gold()
+    with ImageClassifier(model_path("mobilenetv4-small")) as clf:
+        got = [[[r["class_id"], r["label"], r["score"]] for r in clf.classify(im, top_k=5)]
+               for im in dc.pipeline_images(224)]
+        batch = clf.classify_batch(dc.pipeline_images(224), top_k=5)
+    assert got == gold["classify"]
+    assert [[[r["class_id"], r["label"], r["score"]] for r in res] for res in batch] == gold["classify"]
+
+
+def test_object_detector_matches_reference_pipeline():
+    """ObjectDetector (letterbox, six packed int8 heads, one-to-one decode) on the GPU: boxes and
+    scores identical to the reference pipeline's."""
+    from unoq_dsp import ObjectDetector
+    dc, gold = _decode_gold()
+    flat = lambda ds: [[d.class_id, d.label, d.score, list(d.box)] for d in ds]  # noqa: E731
+    with ObjectDetector(model_path("yolo26n-320")) as det:
+        got = [flat(det.detect(im, score_threshold=0.0, max_results=30)) for im in dc.pipeline_images(320)]
+        batch = det.detect_batch(dc.pipeline_images(320), score_threshold=0.0, max_results=30)
+    assert got == gold["detect"]
+    assert [flat(b) for b in batch] == gold["detect"]

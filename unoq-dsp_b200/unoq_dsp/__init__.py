@@ -26,3 +26,7 @@ class Session(HardwareSession):
 
 
 __all__ = ["compile_model", "load", "CompiledModel", "Session", "DSPError", "InvalidBundle", "UnsupportedModel"]
+
+from .vision import ImageClassifier, ObjectDetector  # noqa: E402  (vision imports Session from here)
+
+__all__ += ["ImageClassifier", "ObjectDetector"]
