@@ -171,9 +171,42 @@ class Dist:
         self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
         return float(t.item())
 
+    def broadcast_bytes(self, data, size):
+        """Rank 0's `data` (bytes of length `size`) on every rank, over the gloo group."""
+        if not self.pg:
+            return data
+        obj = [data if self.rank == 0 else None]
+        self.dist.broadcast_object_list(obj, src=0)
+        if len(obj[0]) != size:
+            raise RuntimeError("bad broadcast")
+        return obj[0]
+
     def close(self):
         if self.pg:
             self.dist.destroy_process_group()
+
+
+def shard(global_batch, world, rank):
+    """Contiguous slice [start, start + count) of the global batch for `rank` (equal slices;
+    the global batch must divide evenly so every rank replays the same graph)."""
+    if global_batch % world:
+        raise ValueError(f"global batch {global_batch} does not divide over {world} GPUs")
+    per = global_batch // world
+    return rank * per, per
+
+
+def join_gather(lib, handle, dist):
+    """Multi-GPU: rank 0 makes the NCCL id, every rank receives it and joins the output gather."""
+    if dist.world == 1:
+        return
+    idbuf = C.create_string_buffer(128)
+    if dist.rank == 0 and lib.ug_dist_unique_id(idbuf, 128):
+        raise RuntimeError(f"ug_dist_unique_id: {lib.ug_last_error()}")
+    data = dist.broadcast_bytes(idbuf.raw if dist.rank == 0 else None, 128)
+    idbuf = C.create_string_buffer(data, 128)
+    rc = lib.ug_dist_init(handle, dist.rank, dist.world, idbuf, 128)
+    if rc:
+        raise RuntimeError(f"ug_dist_init rc={rc}: {lib.ug_last_error()}")
 
 
 # --------------------------------------------------------------------------- roofline
@@ -259,7 +292,7 @@ def bench_model(lib, dist, name, global_batch, steps, warmup, peaks, want_roofli
     spec = MODELS[name]
     model = load(ROOT / "models" / f"{name}.uqmodel")
     plan = model.plan
-    per_gpu = global_batch // dist.world
+    _, per_gpu = shard(global_batch, dist.world, dist.rank)
     err = C.c_int()
     buf = C.create_string_buffer(plan, len(plan))
     handle = lib.ug_open_mode(buf, len(plan), 0, C.byref(err))
@@ -270,11 +303,14 @@ def bench_model(lib, dist, name, global_batch, steps, warmup, peaks, want_roofli
         rc = lib.ug_batch_buffers(handle, per_gpu, C.byref(d_in), C.byref(d_out))
         if rc:
             raise RuntimeError(f"batch setup rc={rc}: {lib.ug_last_error()}")
+        join_gather(lib, handle, dist)
         ni = int(np.prod(spec["shape"]))
         no = int(model.metadata["output"]["bytes"])
         # seeded synthetic images, pinned host staging for the e2e leg
         h_in = lib.ug_host_alloc(ni * per_gpu)
-        h_out = lib.ug_host_alloc(no * per_gpu)
+        # rank 0 receives the gathered outputs of every rank
+        out_images = per_gpu * (dist.world if dist.rank == 0 else 1)
+        h_out = lib.ug_host_alloc(no * out_images)
         x_host = np.ctypeslib.as_array(C.cast(h_in, C.POINTER(C.c_int8)), shape=(ni * per_gpu,))
         x_host[:] = np.random.default_rng(1234 + dist.rank).integers(-128, 128, size=ni * per_gpu,
                                                                         dtype=np.int64).astype(np.int8)
@@ -314,8 +350,8 @@ def bench_model(lib, dist, name, global_batch, steps, warmup, peaks, want_roofli
         lib.ug_host_free(h_out)
         return {
             "value": value, "ms_per_step": t_dev / steps * 1e3, "per_gpu_batch": per_gpu, "kernels_per_step": kernels,
-            "e2e": {"value": global_batch * steps / t_e2e, "unit": "images/s", "h2d_bytes_per_step": ni * per_gpu,
-                    "d2h_bytes_per_step": no * per_gpu, "ms_per_step": t_e2e / steps * 1e3},
+            "e2e": {"value": global_batch * steps / t_e2e, "unit": "images/s", "h2d_bytes_per_step": ni * global_batch,
+                    "d2h_bytes_per_step": no * global_batch, "ms_per_step": t_e2e / steps * 1e3},
             "clocks": clocks.summary(), "roofline": roof, "breakdown": breakdown,
         }
     finally:
@@ -349,7 +385,9 @@ def main():
                           f"{world} GPU(s) (BASELINE config 4); YOLO26n-320 INT8 global batch {args.yolo_batch} "
                           "alongside", "model": "mobilenetv4-small.uqmodel (bundled weights)",
               "global_batch": args.global_batch, "image": "224x224x3 int8 NHWC", "parallelism": f"dp{world}",
-              "l2": "inputs larger than L2 (616 MB per 4096 images); no flush needed"}
+              "l2": "inputs larger than L2 (616 MB per 4096 images); no flush needed",
+              "collective": "int8 outputs gathered into GPU 0 over NCCL inside every timed step" if world > 1
+              else "none (1 GPU)"}
 
     if args.impl == "reference":
         if rank != 0:

@@ -12,7 +12,7 @@
  *   21 output undefined, 22 bad call, 24 unavailable/poisoned, 25 lifetime overlap
  *   (runtime/graph.c:50-216); 1001 session busy, 1002 allocation, 1003 bad arguments,
  *   1004 transfer, 1005 thread, 1006 timeout (runtime/bridge.c); 2001 CUDA runtime error,
- *   2002 no CUDA device, 2003 device-side wait timed out.
+ *   2002 no CUDA device, 2003 device-side wait timed out, 2004 collective failed or timed out.
  */
 #ifndef UNOQ_CUDA_H
 #define UNOQ_CUDA_H
@@ -92,6 +92,19 @@ UG_API int ug_batch_kernel_count(void *session, uint32_t images);
  * *total_ms the summed pass time. Not graph-captured, so launch gaps are included. */
 UG_API int ug_profile_batch(void *session, uint32_t images, uint32_t iterations, uint64_t *op_ns, uint32_t count,
                             float *total_ms);
+/* ---- Multi-GPU (extension): one process per GPU, each running a contiguous slice of the
+ * global batch; the one collective is the gather of every rank's outputs into rank 0's device
+ * memory (NCCL point-to-point over NVLink/NVSwitch, non-blocking mode, every wait bounded). ---- */
+
+/* Rank 0 creates the communicator id (128 bytes) and shares it with the other ranks. */
+UG_API int ug_dist_unique_id(void *id, uint32_t bytes);
+/* Join the gather (all ranks, same id). Afterwards every ug_launch_batch / ug_time_batch /
+ * ug_infer_batch ends with the gather; ug_infer_batch on rank 0 returns the whole gathered batch
+ * (world x images outputs, rank-major) in `output`, and returns nothing on the other ranks. */
+UG_API int ug_dist_init(void *session, int rank, int world, const void *id, uint32_t bytes);
+/* Rank 0's device buffer holding the gathered outputs of `images` per rank (NULL on others). */
+UG_API int ug_gather_buffer(void *session, uint32_t images, void **root_device_output);
+
 /* Last CUDA error string seen by the library (empty if none). */
 UG_API const char *ug_last_error(void);
 

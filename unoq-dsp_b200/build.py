@@ -2,7 +2,7 @@
 
 Usage: python unoq-dsp_b200/build.py [--debug]
 The shared library is the product's native core: C ABI (include/unoq_cuda.h) over the CUDA
-engine and kernels in csrc/. It links only the CUDA runtime (static) and libnccl.
+engine and kernels in csrc/. It links only the CUDA runtime (static); NCCL is opened at run time for multi-GPU runs.
 """
 import os
 import subprocess
@@ -15,7 +15,7 @@ CSRC = HERE / "csrc"
 LIB = HERE / "lib" / "libunoq_cuda.so"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-SOURCES = ["plan.cpp", "k_simt.cu", "k_dw.cu", "conv_tc.cu", "engine.cu", "abi.cu"]
+SOURCES = ["plan.cpp", "k_simt.cu", "k_dw.cu", "conv_tc.cu", "gather.cu", "engine.cu", "abi.cu"]
 
 
 def build(debug=False, verbose=False):
@@ -36,7 +36,7 @@ def build(debug=False, verbose=False):
                 print(" ".join(cmd))
             subprocess.run(cmd, check=True)
         objs.append(str(obj))
-    cmd = [NVCC] + ARCH + ["-shared", "-o", str(LIB)] + objs + ["-cudart", "static", "-lnccl", "-lpthread", "-ldl", "-lrt"]
+    cmd = [NVCC] + ARCH + ["-shared", "-o", str(LIB)] + objs + ["-cudart", "static", "-lpthread", "-ldl", "-lrt"]
     if verbose:
         print(" ".join(cmd))
     subprocess.run(cmd, check=True)

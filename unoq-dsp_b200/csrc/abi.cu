@@ -161,6 +161,20 @@ int ug_launch_batch(void *session, uint32_t images) {
     return s->engine.launch(images);
 }
 
+int ug_dist_unique_id(void *id, uint32_t bytes) { return uq::collective_unique_id(id, bytes); }
+
+int ug_dist_init(void *session, int rank, int world, const void *id, uint32_t bytes) {
+    Session *s = static_cast<Session *>(session);
+    if (!s) return 1003;
+    return s->engine.dist_init(rank, world, id, bytes);
+}
+
+int ug_gather_buffer(void *session, uint32_t images, void **root_device_output) {
+    Session *s = static_cast<Session *>(session);
+    if (!s || !images) return 1003;
+    return s->engine.gather_buffer(images, root_device_output);
+}
+
 int ug_synchronize(void *session) {
     Session *s = static_cast<Session *>(session);
     if (!s) return 1003;

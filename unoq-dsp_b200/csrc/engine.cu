@@ -40,6 +40,7 @@ Engine::~Engine() { release(); }
 void Engine::release() {
     if (device_ >= 0 && (d_const_ || stream_)) cudaSetDevice(device_);
     if (stream_) cudaStreamSynchronize(stream_);
+    gather_.reset();
     for (auto &kv : batches_) {
         BatchCtx &b = *kv.second;
         if (b.exec) cudaGraphExecDestroy(b.exec);
@@ -600,13 +601,17 @@ int Engine::run_host(const void *in, void *out, uint32_t images) {
         rc = 2001;
     }
     if (rc) return rc;
-    UQ_CUDA(cudaMemcpyAsync(out, B->ptr[P_.h.output], no, cudaMemcpyDeviceToHost, stream_));
-    UQ_CUDA(cudaEventRecord(ev1_, stream_));
-    cudaError_t e = cudaStreamSynchronize(stream_);
-    if (e != cudaSuccess) {
-        set_error(std::string("inference: ") + cudaGetErrorString(e));
-        return 2001;
+    if ((rc = gather(*B))) return rc;
+    if (gather_ && gather_->active()) {
+        // rank 0 returns the whole gathered batch (rank-major); the other ranks return nothing
+        if (gather_->rank() == 0)
+            UQ_CUDA(cudaMemcpyAsync(out, gather_->root_buffer(no), no * (size_t)gather_->world(),
+                                    cudaMemcpyDeviceToHost, stream_));
+    } else {
+        UQ_CUDA(cudaMemcpyAsync(out, B->ptr[P_.h.output], no, cudaMemcpyDeviceToHost, stream_));
     }
+    UQ_CUDA(cudaEventRecord(ev1_, stream_));
+    if ((rc = finish(ev1_))) return rc;
     UQ_CUDA(cudaEventElapsedTime(&last_ms_, ev0_, ev1_));
     last_images_ = images;
     return device_status();
@@ -639,7 +644,7 @@ int Engine::launch(uint32_t images) {
     UQ_CUDA(cudaSetDevice(device_));
     UQ_CUDA(cudaGraphLaunch(B->exec, stream_));
     last_images_ = images;
-    return 0;
+    return gather(*B);
 }
 
 int Engine::synchronize() {
@@ -656,12 +661,53 @@ int Engine::time_launches(uint32_t images, uint32_t iterations, float *ms) {
     UQ_CUDA(cudaSetDevice(device_));
     UQ_CUDA(cudaStreamSynchronize(stream_));
     UQ_CUDA(cudaEventRecord(ev0_, stream_));
-    for (uint32_t i = 0; i < iterations; i++) UQ_CUDA(cudaGraphLaunch(B->exec, stream_));
+    for (uint32_t i = 0; i < iterations; i++) {
+        UQ_CUDA(cudaGraphLaunch(B->exec, stream_));
+        if ((rc = gather(*B))) return rc;
+    }
     UQ_CUDA(cudaEventRecord(ev1_, stream_));
-    UQ_CUDA(cudaEventSynchronize(ev1_));
+    if ((rc = finish(ev1_))) return rc;
     UQ_CUDA(cudaEventElapsedTime(ms, ev0_, ev1_));
     last_images_ = images;
     return device_status();
+}
+
+int Engine::gather(const BatchCtx &b) {
+    if (!gather_ || !gather_->active()) return 0;
+    return gather_->enqueue(b.ptr[P_.h.output], (size_t)output_bytes() * b.images, stream_);
+}
+
+int Engine::finish(cudaEvent_t ev) {
+    if (gather_ && gather_->active()) {
+        const int rc = gather_->wait(ev, 60.0);
+        if (rc) return rc;
+    } else {
+        const cudaError_t e = cudaEventSynchronize(ev);
+        if (e != cudaSuccess) {
+            set_error(std::string("inference: ") + cudaGetErrorString(e));
+            return 2001;
+        }
+    }
+    return 0;
+}
+
+int Engine::dist_init(int rank, int world, const void *id, uint32_t bytes) {
+    if (!ready_) return 22;
+    if (gather_) return 1003;
+    auto g = std::make_unique<OutputGather>();
+    const int rc = g->init(device_, rank, world, id, bytes);
+    if (rc) return rc;
+    gather_ = std::move(g);
+    return 0;
+}
+
+int Engine::gather_buffer(uint32_t images, void **root) {
+    if (!root) return 1003;
+    *root = nullptr;
+    if (!gather_ || !gather_->active()) return 22;
+    UQ_CUDA(cudaSetDevice(device_));
+    *root = gather_->root_buffer((size_t)output_bytes() * images);
+    return gather_->rank() != 0 || *root ? 0 : 1002;
 }
 
 int Engine::kernel_count(uint32_t images) {

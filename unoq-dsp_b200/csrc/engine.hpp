@@ -14,6 +14,7 @@
 #include <string>
 #include <vector>
 
+#include "gather.hpp"
 #include "plan.hpp"
 
 namespace uq {
@@ -68,6 +69,10 @@ class Engine {
     // Eager (non-graph) passes with a CUDA event after every op; accumulates per-op
     // nanoseconds into op_ns[0..no) and returns the summed pass time in *total_ms.
     int profile_batch(uint32_t images, uint32_t iterations, uint64_t *op_ns, uint32_t n, float *total_ms);
+    // Multi-GPU: join the output gather of a `world`-rank batch-sharded run. From then on every
+    // batch launch ends with the gather of this rank's outputs into rank 0's root buffer.
+    int dist_init(int rank, int world, const void *id, uint32_t bytes);
+    int gather_buffer(uint32_t images, void **root);
 
    private:
     int prepare();
@@ -94,6 +99,9 @@ class Engine {
     uint32_t last_images_ = 0;
     bool profiling_ = false;
     std::vector<uint64_t> ticks_;        // [0] runs, [1] total ns, [2+i] op ns
+    std::unique_ptr<OutputGather> gather_;
+    int gather(const BatchCtx &b);       // enqueue the output gather when multi-rank
+    int finish(cudaEvent_t ev);          // wait for `ev`, bounded when a collective is pending
 };
 
 // Records the last CUDA failure for ug_last_error().
