@@ -358,6 +358,15 @@ def bench_model(lib, dist, name, global_batch, steps, warmup, peaks, want_roofli
         lib.ug_close(handle)
 
 
+def conv_traffic_per_image():
+    """DRAM bytes per image of the conv launches of one MobileNetV4 step, from the committed ncu
+    launch-list summary (profiles/mnv4_b512_launches.md); None when absent."""
+    import re
+    p = ROOT / "profiles" / "mnv4_b512_launches.md"
+    m = re.search(r"conv_dram_bytes_per_image = (\d+)", p.read_text()) if p.is_file() else None
+    return int(m.group(1)) if m else None
+
+
 def load_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.is_file():
@@ -453,6 +462,11 @@ def main():
     roof = res["roofline"]
     if roof is not None:
         roof["peak_source"] = peaks["source"]
+        per_image = conv_traffic_per_image()
+        if per_image and roof.get("kernel") == "conv":
+            roof["traffic"] = per_image * res["per_gpu_batch"]
+            roof["traffic_source"] = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of the conv launches of one "
+                                      "step at batch 512 (profiles/mnv4_b512_launches.md), scaled by images")
     line = {
         "metric": METRIC, "value": round(res["value"], 2), "unit": "images/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(res["ms_per_step"], 4), "higher_is_better": True,
