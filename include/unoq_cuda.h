@@ -67,12 +67,17 @@ UG_API int ug_profile_control(void *session, uint32_t command, void *out, uint32
 UG_API int ug_set_device(int device);
 /* Run `images` independent images (inputs back to back, outputs back to back), host
  * buffers. Pinned buffers from ug_host_alloc give full-bandwidth copies. The first call
- * for a batch size prepares and captures a CUDA graph for it. */
+ * for a batch size prepares and captures a CUDA graph for it. From 512 images the batch runs
+ * as 2 (or, from 2048, 4) pieces whose host-to-device copy, graph and device-to-host copy
+ * overlap on three streams. */
 UG_API int ug_infer_batch(void *session, const void *input, uint32_t images, void *output);
 /* Device-resident variant: `device_input`/`device_output` are this session's device
  * buffers from ug_batch_buffers; nothing crosses PCIe. Asynchronous on the session stream. */
 UG_API int ug_batch_buffers(void *session, uint32_t images, void **device_input, void **device_output);
 UG_API int ug_launch_batch(void *session, uint32_t images);
+/* Copy host images into / results out of that device-resident batch (synchronous). */
+UG_API int ug_upload_batch(void *session, const void *input, uint32_t images);
+UG_API int ug_download_batch(void *session, void *output, uint32_t images);
 UG_API int ug_synchronize(void *session);
 /* Time `iterations` back-to-back ug_launch_batch(images) on the session stream with CUDA
  * events; writes the elapsed milliseconds. */

@@ -175,6 +175,18 @@ int ug_gather_buffer(void *session, uint32_t images, void **root_device_output) 
     return s->engine.gather_buffer(images, root_device_output);
 }
 
+int ug_upload_batch(void *session, const void *input, uint32_t images) {
+    Session *s = static_cast<Session *>(session);
+    if (!s || !input || !images) return 1003;
+    return s->engine.upload(input, images);
+}
+
+int ug_download_batch(void *session, void *output, uint32_t images) {
+    Session *s = static_cast<Session *>(session);
+    if (!s || !output || !images) return 1003;
+    return s->engine.download(output, images);
+}
+
 int ug_synchronize(void *session) {
     Session *s = static_cast<Session *>(session);
     if (!s) return 1003;

@@ -57,6 +57,14 @@ void Engine::release() {
     if (ev0_) cudaEventDestroy(ev0_);
     if (ev1_) cudaEventDestroy(ev1_);
     ev0_ = ev1_ = nullptr;
+    for (auto &row : pipe_ev_)
+        for (auto &e : row) {
+            if (e) cudaEventDestroy(e);
+            e = nullptr;
+        }
+    if (h2d_) cudaStreamDestroy(h2d_);
+    if (d2h_) cudaStreamDestroy(d2h_);
+    h2d_ = d2h_ = nullptr;
     if (stream_) cudaStreamDestroy(stream_);
     stream_ = nullptr;
     steps_.clear();
@@ -88,8 +96,12 @@ int Engine::load(const void *plan, uint32_t bytes, int device) {
     P_ = std::move(P);
     UQ_CUDA(cudaSetDevice(device_));
     UQ_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    UQ_CUDA(cudaStreamCreateWithFlags(&h2d_, cudaStreamNonBlocking));
+    UQ_CUDA(cudaStreamCreateWithFlags(&d2h_, cudaStreamNonBlocking));
     UQ_CUDA(cudaEventCreate(&ev0_));
     UQ_CUDA(cudaEventCreate(&ev1_));
+    for (auto &row : pipe_ev_)
+        for (auto &e : row) UQ_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     UQ_CUDA(cudaMalloc(&d_const_, P_.h.arena_bytes));
     UQ_CUDA(cudaMemcpy(d_const_, P_.arena.data(), P_.h.arena_bytes, cudaMemcpyHostToDevice));
     rc = prepare();
@@ -562,10 +574,11 @@ int Engine::capture(BatchCtx &B) {
     return 0;
 }
 
-int Engine::batch(uint32_t images, BatchCtx **out) {
+int Engine::batch(uint32_t images, BatchCtx **out, uint32_t slot) {
     if (!ready_) return 22;
     if (!images) return 22;
-    auto it = batches_.find(images);
+    const uint64_t key = (uint64_t)slot << 32 | images;
+    auto it = batches_.find(key);
     if (it != batches_.end()) {
         *out = it->second.get();
         return 0;
@@ -582,12 +595,16 @@ int Engine::batch(uint32_t images, BatchCtx **out) {
         return rc;
     }
     *out = B.get();
-    batches_[images] = std::move(B);
+    batches_[key] = std::move(B);
     return 0;
 }
 
 int Engine::run_host(const void *in, void *out, uint32_t images) {
     if (!ready_ || !in || !out) return 22;
+    // Large batches overlap their copies with compute (4 pieces from 2048 images, 2 from 512).
+    if (!profiling_ && images >= 512)
+        return run_pipelined(static_cast<const uint8_t *>(in), static_cast<uint8_t *>(out), images,
+                             images >= 2048 ? 4 : 2);
     BatchCtx *B = nullptr;
     int rc = batch(images, &B);
     if (rc) return rc;
@@ -611,6 +628,60 @@ int Engine::run_host(const void *in, void *out, uint32_t images) {
         UQ_CUDA(cudaMemcpyAsync(out, B->ptr[P_.h.output], no, cudaMemcpyDeviceToHost, stream_));
     }
     UQ_CUDA(cudaEventRecord(ev1_, stream_));
+    if ((rc = finish(ev1_))) return rc;
+    UQ_CUDA(cudaEventElapsedTime(&last_ms_, ev0_, ev1_));
+    last_images_ = images;
+    return device_status();
+}
+
+int Engine::run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint32_t chunks) {
+    const uint32_t c = (images + chunks - 1) / chunks;  // images per piece; the last may be smaller
+    chunks = (images + c - 1) / c;
+    const uint32_t rem = images - (chunks - 1) * c;
+    const size_t ni = input_bytes(), no = output_bytes();
+    BatchCtx *slot[2] = {nullptr, nullptr}, *last = nullptr;
+    int rc = batch(c, &slot[0], 1);
+    if (!rc) rc = batch(c, &slot[1], 2);
+    if (!rc && rem != c) rc = batch(rem, &last, 3);
+    if (rc) return rc;
+    UQ_CUDA(cudaSetDevice(device_));
+    const bool gathering = gather_ && gather_->active();
+    uint8_t *root = gathering ? gather_->root_buffer(no * images) : nullptr;
+    if (gathering && gather_->rank() == 0 && !root) return 1002;
+    // every stream starts after the work already queued on the compute stream
+    UQ_CUDA(cudaEventRecord(ev0_, stream_));
+    UQ_CUDA(cudaStreamWaitEvent(h2d_, ev0_, 0));
+    UQ_CUDA(cudaStreamWaitEvent(d2h_, ev0_, 0));
+    for (uint32_t k = 0; k < chunks; k++) {
+        const int s = (int)(k & 1);
+        BatchCtx *B = (k == chunks - 1 && last) ? last : slot[s];
+        const size_t n = k == chunks - 1 ? rem : c, off = (size_t)k * c;
+        // the slot's previous piece must be computed and read out before its arena is refilled
+        if (k >= 2) UQ_CUDA(cudaStreamWaitEvent(h2d_, pipe_ev_[2][s], 0));
+        UQ_CUDA(cudaMemcpyAsync(B->ptr[P_.h.input], in + off * ni, n * ni, cudaMemcpyHostToDevice, h2d_));
+        UQ_CUDA(cudaEventRecord(pipe_ev_[0][s], h2d_));
+        UQ_CUDA(cudaStreamWaitEvent(stream_, pipe_ev_[0][s], 0));
+        if (cudaGraphLaunch(B->exec, stream_) != cudaSuccess) {
+            set_error("graph launch failed");
+            return 2001;
+        }
+        if (gathering && (rc = gather_->enqueue(B->ptr[P_.h.output], n * no, no * images, off * no, stream_)))
+            return rc;
+        UQ_CUDA(cudaEventRecord(pipe_ev_[1][s], stream_));
+        UQ_CUDA(cudaStreamWaitEvent(d2h_, pipe_ev_[1][s], 0));
+        if (!gathering) {
+            UQ_CUDA(cudaMemcpyAsync(out + off * no, B->ptr[P_.h.output], n * no, cudaMemcpyDeviceToHost, d2h_));
+        } else if (gather_->rank() == 0) {
+            // rank-major result: rank r's images occupy [r * images, (r + 1) * images)
+            for (int r = 0; r < gather_->world(); r++) {
+                const size_t at = ((size_t)r * images + off) * no;
+                UQ_CUDA(cudaMemcpyAsync(out + at, root + at, n * no, cudaMemcpyDeviceToHost, d2h_));
+            }
+        }
+        UQ_CUDA(cudaEventRecord(pipe_ev_[2][s], d2h_));
+    }
+    UQ_CUDA(cudaEventRecord(ev1_, d2h_));
+    UQ_CUDA(cudaStreamWaitEvent(stream_, ev1_, 0));
     if ((rc = finish(ev1_))) return rc;
     UQ_CUDA(cudaEventElapsedTime(&last_ms_, ev0_, ev1_));
     last_images_ = images;
@@ -647,6 +718,27 @@ int Engine::launch(uint32_t images) {
     return gather(*B);
 }
 
+int Engine::upload(const void *in, uint32_t images) {
+    BatchCtx *B = nullptr;
+    int rc = batch(images, &B);
+    if (rc) return rc;
+    UQ_CUDA(cudaSetDevice(device_));
+    UQ_CUDA(cudaMemcpyAsync(B->ptr[P_.h.input], in, (size_t)input_bytes() * images, cudaMemcpyHostToDevice, stream_));
+    UQ_CUDA(cudaStreamSynchronize(stream_));
+    return 0;
+}
+
+int Engine::download(void *out, uint32_t images) {
+    BatchCtx *B = nullptr;
+    int rc = batch(images, &B);
+    if (rc) return rc;
+    UQ_CUDA(cudaSetDevice(device_));
+    UQ_CUDA(cudaMemcpyAsync(out, B->ptr[P_.h.output], (size_t)output_bytes() * images, cudaMemcpyDeviceToHost,
+                            stream_));
+    UQ_CUDA(cudaStreamSynchronize(stream_));
+    return device_status();
+}
+
 int Engine::synchronize() {
     if (!stream_) return 22;
     UQ_CUDA(cudaSetDevice(device_));
@@ -674,7 +766,8 @@ int Engine::time_launches(uint32_t images, uint32_t iterations, float *ms) {
 
 int Engine::gather(const BatchCtx &b) {
     if (!gather_ || !gather_->active()) return 0;
-    return gather_->enqueue(b.ptr[P_.h.output], (size_t)output_bytes() * b.images, stream_);
+    const size_t bytes = (size_t)output_bytes() * b.images;
+    return gather_->enqueue(b.ptr[P_.h.output], bytes, bytes, 0, stream_);
 }
 
 int Engine::finish(cudaEvent_t ev) {

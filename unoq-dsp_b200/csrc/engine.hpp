@@ -60,6 +60,9 @@ class Engine {
     // Device buffers of the batch context (input tensor, output tensor of image 0).
     int buffers(uint32_t images, void **d_in, void **d_out);
     int launch(uint32_t images);   // async on stream_
+    // Host <-> device-resident batch input/output (the context ug_launch_batch replays). Synchronous.
+    int upload(const void *in, uint32_t images);
+    int download(void *out, uint32_t images);
     int synchronize();
     int time_launches(uint32_t images, uint32_t iterations, float *ms);
     int kernel_count(uint32_t images);
@@ -76,7 +79,12 @@ class Engine {
 
    private:
     int prepare();
-    int batch(uint32_t images, BatchCtx **out);
+    // Batch context for `images`; slot > 0 gives further contexts of the same size (own arena and
+    // graph) for the copy/compute pipeline.
+    int batch(uint32_t images, BatchCtx **out, uint32_t slot = 0);
+    // Host batch in `chunks` pieces: H2D of piece k+1, compute of piece k and D2H of piece k-1
+    // run concurrently on three streams, two arena slots alternating.
+    int run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint32_t chunks);
     int plan_arena(BatchCtx &b);
     int capture(BatchCtx &b);
     int run_steps(const BatchCtx &b, cudaStream_t s, bool profile);
@@ -93,7 +101,9 @@ class Engine {
     std::vector<void *> prep_;
     std::vector<Step> steps_;
     std::vector<int> alias_;             // tensor -> storage root (copy ops alias their source)
-    std::map<uint32_t, std::unique_ptr<BatchCtx>> batches_;
+    std::map<uint64_t, std::unique_ptr<BatchCtx>> batches_;  // key: slot << 32 | images
+    cudaStream_t h2d_ = nullptr, d2h_ = nullptr;             // copy streams of the pipeline
+    cudaEvent_t pipe_ev_[3][2] = {};                         // per slot: input landed, computed, output read
     cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
     float last_ms_ = 0.f;
     uint32_t last_images_ = 0;

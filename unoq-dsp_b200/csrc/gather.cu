@@ -130,9 +130,9 @@ int OutputGather::init(int device, int rank, int world, const void *id, uint32_t
     return 0;
 }
 
-uint8_t *OutputGather::root_buffer(size_t slice_bytes) {
+uint8_t *OutputGather::root_buffer(size_t rank_bytes) {
     if (rank_ != 0) return nullptr;
-    const size_t need = slice_bytes * (size_t)world_;
+    const size_t need = rank_bytes * (size_t)world_;
     if (need > root_bytes_) {
         if (root_) cudaFree(root_);
         root_ = nullptr;
@@ -143,10 +143,11 @@ uint8_t *OutputGather::root_buffer(size_t slice_bytes) {
     return root_;
 }
 
-int OutputGather::enqueue(const void *src, size_t slice_bytes, cudaStream_t s) {
+int OutputGather::enqueue(const void *src, size_t bytes, size_t rank_bytes, size_t offset, cudaStream_t s) {
     if (!active()) return 0;
+    if (offset + bytes > rank_bytes) return 1003;
     ncclComm_t comm = static_cast<ncclComm_t>(comm_);
-    uint8_t *dst = root_buffer(slice_bytes);
+    uint8_t *dst = root_buffer(rank_bytes);
     if (rank_ == 0 && !dst) {
         set_error("collective: root buffer allocation failed");
         return 1002;
@@ -155,8 +156,8 @@ int OutputGather::enqueue(const void *src, size_t slice_bytes, cudaStream_t s) {
     ncclResult_t r = nccl().GroupStart();
     if (ok(r) && rank_ == 0)
         for (int peer = 0; peer < world_ && ok(r); peer++)
-            r = nccl().Recv(dst + (size_t)peer * slice_bytes, slice_bytes, ncclInt8, peer, comm, s);
-    if (ok(r)) r = nccl().Send(src, slice_bytes, ncclInt8, 0, comm, s);
+            r = nccl().Recv(dst + (size_t)peer * rank_bytes + offset, bytes, ncclInt8, peer, comm, s);
+    if (ok(r)) r = nccl().Send(src, bytes, ncclInt8, 0, comm, s);
     const ncclResult_t e = nccl().GroupEnd();
     if (!ok(r)) return fail("send/recv", r);
     if (!ok(e)) return fail("group", e);

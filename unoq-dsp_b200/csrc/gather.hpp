@@ -35,10 +35,11 @@ class OutputGather {
     bool active() const { return comm_ != nullptr && world_ > 1; }
     int rank() const { return rank_; }
     int world() const { return world_; }
-    // Rank 0's receive buffer for `slice_bytes` per rank (grown on demand); null elsewhere.
-    uint8_t *root_buffer(size_t slice_bytes);
-    // Enqueue the gather of `slice_bytes` at `src` on stream `s`.
-    int enqueue(const void *src, size_t slice_bytes, cudaStream_t s);
+    // Rank 0's receive buffer for `rank_bytes` per rank (grown on demand); null elsewhere.
+    uint8_t *root_buffer(size_t rank_bytes);
+    // Enqueue on stream `s` the gather of `bytes` at `src` from every rank; rank 0 receives rank
+    // r's bytes at root + r * rank_bytes + offset (offset > 0 when a batch is sent in chunks).
+    int enqueue(const void *src, size_t bytes, size_t rank_bytes, size_t offset, cudaStream_t s);
     // Wait for `ev` (recorded after the gather) with a bound; aborts the communicator on expiry.
     int wait(cudaEvent_t ev, double seconds);
 
