@@ -5,13 +5,18 @@
 // then y = post[clamp(scale(acc, m, s) + yzp)]. Here the +128 is folded into the bias on the
 // host (bias' = bias + 128 * sum w), so the device accumulates signed x * w with dp4a.
 //
-// Block = one output tile (TH rows x TW columns) of one image for CB channels. The input tile
-// plus halo is staged in shared memory with 16-byte loads (zero-point fill at the borders),
-// each input byte leaving HBM once. A thread owns 4 adjacent output pixels x 4 channels; for
-// every kernel row it reads the needed input words once, transposes groups of 4 taps x 4
-// channels with byte permutes so that one dp4a adds 4 taps of one channel, and uses a masked
-// dp4a for a fifth tap. Requantisation is the exact constant form of requant.cuh, with the
-// thread's 4 channel constants held in registers.
+// Block = one output tile (TH rows x 8 columns) of one image for CB channels.
+//  * Fill: the input tile plus halo is read with 16-byte loads (4 pixels x 16 channels per
+//    thread, zero point outside the image), transposed in registers with byte permutes, and
+//    stored as byte planes: plane[channel][row][column], 4 columns per 32-bit word. Each input
+//    byte leaves HBM once per tile.
+//  * Compute: a thread owns one channel x 8 adjacent output pixels x 2 output rows. For every
+//    input row it loads the row's words once, forms the sliding 4-column windows with funnel
+//    shifts, and adds 4 taps per dp4a against the channel's weight words; the 5th tap of a
+//    5-wide row is byte 3 of the next window, so it costs one dp4a and no shift. Each loaded row
+//    feeds both output rows.
+//  * Epilogue: exact requantisation (requant.cuh constants in registers) and the optional post
+//    table; the bytes are staged NHWC in shared memory and written with 16-byte stores.
 #include <cstring>
 #include <vector>
 
@@ -23,18 +28,20 @@ namespace uq {
 
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kTW = 8;   // output columns per tile (one thread row)
+constexpr int kR = 2;    // output rows per thread
 
 struct DwParams {
     const int8_t *x;
     int8_t *y;
-    const uint32_t *wt;     // [C/4][KH][8] transposed weight words (see dw_prepare)
+    const uint32_t *wt;     // [C][KH][2] weight words: taps 0-3 (0 past KW), 5th tap in byte 3
     const EpiChan *epi;     // [C]
     const uint8_t *post;    // 256 bytes or null
     int n, ih, iw, c, oh, ow, pt, pl;
     int lo, hi, xzp;
-    int cb, tw, th;         // channels per block, tile width / height (output pixels)
+    int cb, th;             // channels per block, output rows per tile
     int tiles_x, tiles_y;
+    int ir, pw, plane;      // input rows per tile, words per plane row, words per plane (odd)
 };
 
 __device__ __forceinline__ void transpose4(uint32_t x0, uint32_t x1, uint32_t x2, uint32_t x3, uint32_t (&y)[4]) {
@@ -62,14 +69,16 @@ __device__ __forceinline__ int32_t requant(int32_t acc, const EpiChan &e, int lo
     return v < lo ? lo : (v > hi ? hi : v);
 }
 
-template <int KH, int KW, int SH, int EPI>
-__global__ void __launch_bounds__(kThreads) dw_kernel(const DwParams p) {
+template <int K, int S, int EPI>
+__global__ void __launch_bounds__(512) dw_kernel(const DwParams p) {
     extern __shared__ __align__(16) uint8_t smem[];
-    constexpr int NW = 3 * SH + KW;  // input words per kernel row for 4 output pixels
-    const int cb = p.cb, tw = p.tw, th = p.th;
-    const int ir = (th - 1) * SH + KH, icol = (tw - 1) * SH + KW;
-    uint8_t *sLut = smem;                       // 256 bytes
-    uint8_t *sIn = smem + 256;                  // [ir][icol][cb]
+    constexpr int TWIN = (kTW - 1) * S + K;       // input columns per tile
+    constexpr int NWORD = (TWIN + 3) / 4;         // words per input row
+    constexpr int NWIN = (kTW - 1) * S + 2;       // window starts 0 .. (7*S + 1)
+    const int cb = p.cb, th = p.th;
+    uint8_t *sLut = smem;                                                   // 256 bytes
+    uint32_t *sPlane = reinterpret_cast<uint32_t *>(smem + 256);            // [cb][plane words]
+    uint8_t *sOut = smem + 256 + (size_t)cb * p.plane * 4;                  // [th][8][cb]
 
     int tile = blockIdx.x;
     const int tx = tile % p.tiles_x;
@@ -77,99 +86,124 @@ __global__ void __launch_bounds__(kThreads) dw_kernel(const DwParams p) {
     const int ty = tile % p.tiles_y;
     const int n = tile / p.tiles_y;
     const int c0 = blockIdx.y * cb;
-    const int iy0 = ty * th * SH - p.pt, ix0 = tx * tw * SH - p.pl;
+    const int iy0 = ty * th * S - p.pt, ix0 = tx * kTW * S - p.pl;
 
     if (p.post)
-        for (int i = threadIdx.x; i < 256; i += kThreads) sLut[i] = p.post[i];
-    const uint32_t fillw = 0x01010101u * (uint8_t)p.xzp;
-    const uint4 fill = make_uint4(fillw, fillw, fillw, fillw);
-    const int c16 = cb / 16;
-    for (int i = threadIdx.x; i < ir * icol * c16; i += kThreads) {
-        const int cc = i % c16, pix = i / c16;
-        const int col = pix % icol, row = pix / icol;
-        const int iy = iy0 + row, ix = ix0 + col;
-        uint4 v = fill;
-        if (iy >= 0 && ix >= 0 && iy < p.ih && ix < p.iw)
-            v = __ldg(reinterpret_cast<const uint4 *>(p.x + (((size_t)n * p.ih + iy) * p.iw + ix) * p.c + c0 + cc * 16));
-        *reinterpret_cast<uint4 *>(sIn + (size_t)pix * cb + cc * 16) = v;
-    }
-
-    const int cgs = cb / 4;
-    const int cg = threadIdx.x % cgs;
-    const int slot = threadIdx.x / cgs;
-    const int quads = tw / 4;
-    const int r = slot / quads, q = slot % quads;
-    const int c = c0 + cg * 4;
-    const int oy = ty * th + r;
-    const int ox = tx * tw + q * 4;
-
-    // weights: per kernel row, 4 words of 4 taps (one per channel) + 4 mask words for a 5th tap
-    uint32_t w4[KH][4], wm[KH][4];
-    const uint32_t *wsrc = p.wt + (size_t)(c / 4) * KH * 8;
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) sLut[i] = p.post[i];
+    // ---- fill: unit = (16-channel chunk, input row, 4-column group)
+    {
+        const uint32_t fillw = 0x01010101u * (uint8_t)p.xzp;
+        const uint4 fill = make_uint4(fillw, fillw, fillw, fillw);
+        const int units = (cb / 16) * p.ir * p.pw;
+        for (int u = threadIdx.x; u < units; u += blockDim.x) {
+            const int wc = u % p.pw, rest = u / p.pw;
+            const int row = rest % p.ir, chunk = rest / p.ir;
+            const int iy = iy0 + row;
+            uint4 px[4];
 #pragma unroll
-    for (int ky = 0; ky < KH; ky++)
+            for (int i = 0; i < 4; i++) {
+                const int ix = ix0 + wc * 4 + i;
+                px[i] = fill;
+                if (iy >= 0 && iy < p.ih && ix >= 0 && ix < p.iw)
+                    px[i] = __ldg(reinterpret_cast<const uint4 *>(
+                        p.x + (((size_t)n * p.ih + iy) * p.iw + ix) * p.c + c0 + chunk * 16));
+            }
+            const uint32_t w0[4] = {px[0].x, px[0].y, px[0].z, px[0].w}, w1[4] = {px[1].x, px[1].y, px[1].z, px[1].w};
+            const uint32_t w2[4] = {px[2].x, px[2].y, px[2].z, px[2].w}, w3[4] = {px[3].x, px[3].y, px[3].z, px[3].w};
+            uint32_t *dst = sPlane + (size_t)(chunk * 16) * p.plane + row * p.pw + wc;
 #pragma unroll
-        for (int ch = 0; ch < 4; ch++) {
-            w4[ky][ch] = __ldg(wsrc + ky * 8 + ch);
-            wm[ky][ch] = KW == 5 ? __ldg(wsrc + ky * 8 + 4 + ch) : 0u;
-        }
-    EpiChan e[4];
+            for (int g = 0; g < 4; g++) {
+                uint32_t t[4];
+                transpose4(w0[g], w1[g], w2[g], w3[g], t);
 #pragma unroll
-    for (int ch = 0; ch < 4; ch++) e[ch] = p.epi[c + ch];
-    __syncthreads();
-
-    int acc[4][4];
-#pragma unroll
-    for (int j = 0; j < 4; j++)
-#pragma unroll
-        for (int ch = 0; ch < 4; ch++) acc[j][ch] = 0;
-    const uint8_t *base = sIn + ((size_t)(r * SH) * icol + q * 4 * SH) * cb + cg * 4;
-#pragma unroll
-    for (int ky = 0; ky < KH; ky++) {
-        uint32_t xw[NW];
-#pragma unroll
-        for (int i = 0; i < NW; i++)
-            xw[i] = *reinterpret_cast<const uint32_t *>(base + ((size_t)ky * icol + i) * cb);
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int b = j * SH;
-            uint32_t t[4];
-            transpose4(xw[b], xw[b + 1], xw[b + 2], KW > 3 ? xw[b + 3] : xw[b], t);
-#pragma unroll
-            for (int ch = 0; ch < 4; ch++) {
-                acc[j][ch] = __dp4a((int)t[ch], (int)w4[ky][ch], acc[j][ch]);
-                if (KW == 5) acc[j][ch] = __dp4a((int)xw[b + 4], (int)wm[ky][ch], acc[j][ch]);
+                for (int k = 0; k < 4; k++) dst[(size_t)(g * 4 + k) * p.plane] = t[k];
             }
         }
     }
-    if (r >= th || oy >= p.oh) return;
+
+    // ---- this thread: channel ch, output rows 2 * rg, 2 * rg + 1 of the tile
+    const int ch = threadIdx.x % cb, rg = threadIdx.x / cb;
+    const int c = c0 + ch;
+    uint32_t wa[K], wb[K];
+#pragma unroll
+    for (int ky = 0; ky < K; ky++) {
+        wa[ky] = __ldg(p.wt + ((size_t)c * K + ky) * 2);
+        wb[ky] = K == 5 ? __ldg(p.wt + ((size_t)c * K + ky) * 2 + 1) : 0u;
+    }
+    const EpiChan e = p.epi[c];
+    __syncthreads();
+
+    int acc[kR][kTW];
+#pragma unroll
+    for (int r = 0; r < kR; r++)
+#pragma unroll
+        for (int j = 0; j < kTW; j++) acc[r][j] = 0;
+    const uint32_t *plane = sPlane + (size_t)ch * p.plane + (size_t)(rg * kR * S) * p.pw;
+    // input rows used by the thread's two output rows: (kR - 1) * S + K
+#pragma unroll
+    for (int ir = 0; ir < (kR - 1) * S + K; ir++) {
+        uint32_t wd[NWORD + 1];
+#pragma unroll
+        for (int i = 0; i < NWORD; i++) wd[i] = plane[ir * p.pw + i];
+        wd[NWORD] = 0;
+        uint32_t win[NWIN];
+#pragma unroll
+        for (int s = 0; s < NWIN; s++) win[s] = (s & 3) ? __funnelshift_r(wd[s >> 2], wd[(s >> 2) + 1], 8 * (s & 3)) : wd[s >> 2];
+#pragma unroll
+        for (int r = 0; r < kR; r++) {
+            const int ky = ir - r * S;
+            if (ky < 0 || ky >= K) continue;
+#pragma unroll
+            for (int j = 0; j < kTW; j++) {
+                acc[r][j] = __dp4a((int)win[j * S], (int)wa[ky], acc[r][j]);
+                if (K == 5) acc[r][j] = __dp4a((int)win[j * S + 1], (int)wb[ky], acc[r][j]);
+            }
+        }
+    }
     const uint8_t *lut = p.post ? sLut : nullptr;
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-        if (ox + j >= p.ow) break;
-        uint32_t packed = 0;
+    for (int r = 0; r < kR; r++)
 #pragma unroll
-        for (int ch = 0; ch < 4; ch++) {
-            int32_t v = requant<EPI>(acc[j][ch], e[ch], p.lo, p.hi);
+        for (int j = 0; j < kTW; j++) {
+            int32_t v = requant<EPI>(acc[r][j], e, p.lo, p.hi);
             if (lut) v = (int8_t)lut[v + 128];
-            packed |= (uint32_t)(uint8_t)v << (8 * ch);
+            sOut[((size_t)(rg * kR + r) * kTW + j) * cb + ch] = (uint8_t)v;
         }
-        *reinterpret_cast<uint32_t *>(p.y + (((size_t)n * p.oh + oy) * p.ow + ox + j) * p.c + c) = packed;
+    __syncthreads();
+    // ---- copy-out: 16 channels of one pixel per store
+    const int units = th * kTW * (cb / 16);
+    for (int u = threadIdx.x; u < units; u += blockDim.x) {
+        const int chunk = u % (cb / 16), pix = u / (cb / 16);
+        const int j = pix % kTW, row = pix / kTW;
+        const int oy = ty * th + row, ox = tx * kTW + j;
+        if (oy >= p.oh || ox >= p.ow) continue;
+        *reinterpret_cast<uint4 *>(p.y + (((size_t)n * p.oh + oy) * p.ow + ox) * p.c + c0 + chunk * 16) =
+            *reinterpret_cast<const uint4 *>(sOut + (size_t)pix * cb + chunk * 16);
     }
 }
 
-template <int KH, int KW, int SH>
-void launch_shape(const DwParams &p, int epi, dim3 grid, size_t smem, cudaStream_t s) {
-    if (epi == 0) dw_kernel<KH, KW, SH, 0><<<grid, kThreads, smem, s>>>(p);
-    else if (epi == 1) dw_kernel<KH, KW, SH, 1><<<grid, kThreads, smem, s>>>(p);
-    else dw_kernel<KH, KW, SH, 2><<<grid, kThreads, smem, s>>>(p);
+template <int K, int S>
+void launch_shape(const DwParams &p, int epi, dim3 grid, int threads, size_t smem, cudaStream_t s) {
+    if (epi == 0) dw_kernel<K, S, 0><<<grid, threads, smem, s>>>(p);
+    else if (epi == 1) dw_kernel<K, S, 1><<<grid, threads, smem, s>>>(p);
+    else dw_kernel<K, S, 2><<<grid, threads, smem, s>>>(p);
+}
+
+template <int K, int S>
+bool allow_smem(size_t bytes) {
+    return cudaFuncSetAttribute(dw_kernel<K, S, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) ==
+               cudaSuccess &&
+           cudaFuncSetAttribute(dw_kernel<K, S, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) ==
+               cudaSuccess &&
+           cudaFuncSetAttribute(dw_kernel<K, S, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) ==
+               cudaSuccess;
 }
 
 }  // namespace
 
 struct DwFast {
     DwParams p{};
-    int kh = 3, kw = 3, sh = 1, epi = 0;
+    int k = 3, s = 1, epi = 0, threads = 0;
     size_t smem = 0;
 };
 
@@ -180,66 +214,69 @@ int dw_prepare(const int8_t *w, const int32_t *q, const uint8_t *post_dev, const
     if (!((g.kh == 3 && g.kw == 3) || (g.kh == 5 && g.kw == 5)) || g.sh != g.sw || (g.sh != 1 && g.sh != 2) ||
         g.dh != 1 || g.dw != 1 || g.oc % 16 != 0)
         return 0;
-    const int C = g.oc, K = g.kh;
+    const int C = g.oc, K = g.kh, S = g.sh;
     const int32_t *bias = q + kHead, *mult = bias + C, *shift = mult + C;
     const int yzp = q[13];
-    // weight words: [C/4][KH][ w4 x4 | mask x4 ]
-    std::vector<uint32_t> wt((size_t)C / 4 * K * 8, 0);
+    // weight words per channel and kernel row: taps 0..3 (zero past KW), then tap 4 in byte 3
+    std::vector<uint32_t> wt((size_t)C * K * 2, 0);
     std::vector<EpiChan> epi(C);
     bool fast = true;
     for (int c = 0; c < C; c++) {
         long long sum = 0;
-        for (int t = 0; t < g.kh * g.kw; t++) sum += w[t * C + c];
+        for (int t = 0; t < K * K; t++) sum += w[t * C + c];
         epi[c] = make_epilogue((long long)bias[c] + 128 * sum, mult[c], shift[c], yzp);
         fast &= shift[c] <= -1 && shift[c] >= -15;
+        for (int ky = 0; ky < K; ky++) {
+            uint32_t a = 0;
+            for (int kx = 0; kx < 4 && kx < K; kx++) a |= (uint32_t)(uint8_t)w[(ky * K + kx) * C + c] << (8 * kx);
+            wt[((size_t)c * K + ky) * 2] = a;
+            if (K == 5) wt[((size_t)c * K + ky) * 2 + 1] = (uint32_t)(uint8_t)w[(ky * K + 4) * C + c] << 24;
+        }
     }
-    for (int c4 = 0; c4 < C / 4; c4++)
-        for (int ky = 0; ky < K; ky++)
-            for (int ch = 0; ch < 4; ch++) {
-                const int c = c4 * 4 + ch;
-                uint32_t word = 0;
-                for (int kx = 0; kx < 4 && kx < g.kw; kx++)
-                    word |= (uint32_t)(uint8_t)w[(ky * g.kw + kx) * C + c] << (8 * kx);
-                wt[((size_t)c4 * K + ky) * 8 + ch] = word;
-                if (g.kw == 5) wt[((size_t)c4 * K + ky) * 8 + 4 + ch] = (uint32_t)(uint8_t)w[(ky * 5 + 4) * C + c] << (8 * ch);
-            }
     const int epi_mode = !fast ? 2 : (q[14] >= yzp ? 0 : 1);
     if (epi_mode != 2)
         for (auto &e : epi) e.sh = e.sh >= 32 ? e.sh - 32 : 0;
-    void *dwt = alloc(wt.size() * 4), *de = alloc(epi.size() * sizeof(EpiChan));
-    if (!dwt || !de) return 2001;
-    if (cudaMemcpy(dwt, wt.data(), wt.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemcpy(de, epi.data(), epi.size() * sizeof(EpiChan), cudaMemcpyHostToDevice) != cudaSuccess)
-        return 2001;
+    // Tile: 8 columns; the whole image height when it is at most 32 rows, else 16 rows.
+    const int rg = g.oh <= 32 ? (g.oh + kR - 1) / kR : 8;
+    int cb = 64;
+    while (cb > 16 && (C % cb != 0 || cb * rg > 512)) cb /= 2;
+    if (C % cb != 0 || cb * rg > 512) return 0;
     DwFast *d = new DwFast();
     DwParams &p = d->p;
+    p.cb = cb;
+    p.th = rg * kR;
+    p.tiles_x = (g.ow + kTW - 1) / kTW;
+    p.tiles_y = (g.oh + p.th - 1) / p.th;
+    p.ir = (p.th - 1) * S + K;
+    p.pw = ((kTW - 1) * S + K + 3) / 4;
+    p.plane = p.ir * p.pw;
+    if ((p.plane & 1) == 0) p.plane++;  // odd plane stride: lanes (channels) fall in distinct banks
+    d->k = K, d->s = S, d->epi = epi_mode, d->threads = cb * rg;
+    d->smem = 256 + (size_t)cb * p.plane * 4 + (size_t)p.th * kTW * cb;
+    if (d->smem > 200 * 1024) {
+        delete d;
+        return 0;
+    }
+    if (d->smem > 48 * 1024) {
+        const bool ok = K == 3 ? (S == 1 ? allow_smem<3, 1>(d->smem) : allow_smem<3, 2>(d->smem))
+                               : (S == 1 ? allow_smem<5, 1>(d->smem) : allow_smem<5, 2>(d->smem));
+        if (!ok) {
+            delete d;
+            return 0;
+        }
+    }
+    void *dwt = alloc(wt.size() * 4), *de = alloc(epi.size() * sizeof(EpiChan));
+    if (!dwt || !de ||
+        cudaMemcpy(dwt, wt.data(), wt.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(de, epi.data(), epi.size() * sizeof(EpiChan), cudaMemcpyHostToDevice) != cudaSuccess) {
+        delete d;
+        return 2001;
+    }
     p.wt = static_cast<const uint32_t *>(dwt);
     p.epi = static_cast<const EpiChan *>(de);
     p.post = post_dev;
     p.ih = g.ih, p.iw = g.iw, p.c = C, p.oh = g.oh, p.ow = g.ow, p.pt = g.pt, p.pl = g.pl;
     p.lo = q[14], p.hi = q[15], p.xzp = q[12];
-    p.cb = C % 64 == 0 ? 64 : C % 32 == 0 ? 32 : 16;
-    p.tw = g.ow <= 8 ? 8 : 16;
-    p.th = (kThreads / (p.cb / 4)) / (p.tw / 4);
-    p.tiles_x = (g.ow + p.tw - 1) / p.tw;
-    p.tiles_y = (g.oh + p.th - 1) / p.th;
-    d->kh = g.kh, d->kw = g.kw, d->sh = g.sh, d->epi = epi_mode;
-    const int ir = (p.th - 1) * g.sh + g.kh, icol = (p.tw - 1) * g.sh + g.kw;
-    d->smem = 256 + (size_t)ir * icol * p.cb;
-    if (d->smem > 48 * 1024) {
-        static bool attr = false;
-        if (!attr) {
-            // every instantiation may need more than the default 48 KB
-            cudaFuncSetAttribute(dw_kernel<5, 5, 2, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
-            cudaFuncSetAttribute(dw_kernel<5, 5, 2, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
-            cudaFuncSetAttribute(dw_kernel<5, 5, 2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
-            attr = true;
-        }
-        if (d->smem > 100 * 1024) {
-            delete d;
-            return 0;
-        }
-    }
     *out = d;
     return 0;
 }
@@ -250,10 +287,10 @@ int dw_launch(const DwFast &d, const int8_t *x, int8_t *y, const ConvGeom &g, cu
     p.y = y;
     p.n = g.n;
     dim3 grid((unsigned)(p.n * p.tiles_y * p.tiles_x), (unsigned)(p.c / p.cb));
-    if (d.kh == 3 && d.sh == 1) launch_shape<3, 3, 1>(p, d.epi, grid, d.smem, s);
-    else if (d.kh == 3) launch_shape<3, 3, 2>(p, d.epi, grid, d.smem, s);
-    else if (d.sh == 1) launch_shape<5, 5, 1>(p, d.epi, grid, d.smem, s);
-    else launch_shape<5, 5, 2>(p, d.epi, grid, d.smem, s);
+    if (d.k == 3 && d.s == 1) launch_shape<3, 1>(p, d.epi, grid, d.threads, d.smem, s);
+    else if (d.k == 3) launch_shape<3, 2>(p, d.epi, grid, d.threads, d.smem, s);
+    else if (d.s == 1) launch_shape<5, 1>(p, d.epi, grid, d.threads, d.smem, s);
+    else launch_shape<5, 2>(p, d.epi, grid, d.threads, d.smem, s);
     return 0;
 }
 
