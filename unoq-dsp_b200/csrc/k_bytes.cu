@@ -1,0 +1,411 @@
+// k_bytes.cu -- byte-movement and small integer ops of the plan, vectorised.
+//
+// Plan codes 10 (transpose), 16 (pool), 19 (pack), 20 (concat), 21 (nearest resize),
+// 26 (slice) and 27 (bmm) (runtime/graph.c:306-391, qnn.c:119-153, 1228-1245). All are exact byte
+// permutations or integer arithmetic; results are bit-identical to the reference.
+//
+// The movement kernels work in the widest unit (16, 4 or 1 bytes) that every run length, offset
+// and base address allows, and decode indices once per unit rather than once per byte:
+//  * slice / concat / pack: strided copies of contiguous runs (a channel range of each pixel, a
+//    block of rows, a whole segment);
+//  * transpose: a permutation that reduces to a batched 2-D transpose after merging adjacent
+//    axes goes through a shared-memory tile; any other permutation uses the element-wise path;
+//  * resize: one output pixel's channels per run, from the prepared row / column offsets;
+//  * max pool: 16 channels per thread with __vmaxs4.
+// bmm computes a 32 x 32 output tile per block from shared-memory tiles with the zero points
+// already subtracted.
+#include <algorithm>
+
+#include "kernels.cuh"
+
+namespace uq {
+
+namespace {
+
+constexpr int kT = 256;
+
+inline int unit_for(uint64_t a, uint64_t b = 0, uint64_t c = 0, uint64_t d = 0) {
+    const uint64_t m = a | b | c | d;
+    return (m & 15) == 0 ? 16 : (m & 3) == 0 ? 4 : 1;
+}
+
+template <int V>
+struct Unit;
+template <>
+struct Unit<16> {
+    using T = uint4;
+};
+template <>
+struct Unit<4> {
+    using T = uint32_t;
+};
+template <>
+struct Unit<1> {
+    using T = uint8_t;
+};
+
+// ---------------------------------------------------------------- strided run copy -----------
+// Row r (r = sum idx_d * prod(extent[d+1..])) copies `run` bytes from
+// src + base + sum idx_d * stride[d] to dst + r * dst_stride + dst_base.
+struct RunCopy {
+    int ndim;
+    uint32_t extent[4];
+    uint64_t stride[4];
+    uint64_t base, dst_stride, dst_base;
+    uint64_t rows;
+    uint32_t run;
+};
+
+template <int V>
+__global__ void run_copy_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, RunCopy rc) {
+    using T = typename Unit<V>::T;
+    const uint32_t per_row = rc.run / V;
+    const uint64_t units = rc.rows * per_row;
+    for (uint64_t u = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; u < units; u += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t row = u / per_row;
+        const uint32_t col = (uint32_t)(u - row * per_row);
+        uint64_t rem = row, off = rc.base;
+        for (int d = rc.ndim - 1; d >= 0; d--) {
+            const uint64_t idx = rem % rc.extent[d];
+            rem /= rc.extent[d];
+            off += idx * rc.stride[d];
+        }
+        reinterpret_cast<T *>(dst + rc.dst_base + row * rc.dst_stride)[col] = reinterpret_cast<const T *>(src + off)[col];
+    }
+}
+
+void run_copy(const uint8_t *src, uint8_t *dst, const RunCopy &rc, cudaStream_t s) {
+    if (!rc.rows || !rc.run) return;
+    uint64_t strides = 0;
+    for (int d = 0; d < rc.ndim; d++) strides |= rc.stride[d];
+    const int v = unit_for(rc.run, rc.base | strides, rc.dst_stride | rc.dst_base,
+                           reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst));
+    const uint64_t units = rc.rows * (rc.run / v);
+    if (v == 16) run_copy_kernel<16><<<grid_for(units, kT), kT, 0, s>>>(src, dst, rc);
+    else if (v == 4) run_copy_kernel<4><<<grid_for(units, kT), kT, 0, s>>>(src, dst, rc);
+    else run_copy_kernel<1><<<grid_for(units, kT), kT, 0, s>>>(src, dst, rc);
+}
+
+// ---------------------------------------------------------------- concat (code 20) -----------
+template <int V>
+__global__ void concat_kernel(const uint8_t *__restrict__ a, const uint8_t *__restrict__ b, uint8_t *__restrict__ z,
+                              uint64_t outer, uint32_t ac, uint32_t bc) {
+    using T = typename Unit<V>::T;
+    const uint32_t ua = ac / V, ub = bc / V, row = ua + ub;
+    const uint64_t units = outer * row;
+    for (uint64_t u = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; u < units; u += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t r = u / row;
+        const uint32_t c = (uint32_t)(u - r * row);
+        reinterpret_cast<T *>(z)[u] = c < ua ? reinterpret_cast<const T *>(a)[r * ua + c]
+                                             : reinterpret_cast<const T *>(b)[r * ub + (c - ua)];
+    }
+}
+
+// ---------------------------------------------------------------- transpose (code 10) --------
+// Batched 2-D transpose of elements of `E` bytes: z[b][c][r] = a[b][r][c].
+template <int E>
+__global__ void transpose2d_kernel(const uint8_t *__restrict__ a, uint8_t *__restrict__ z, uint32_t batches, uint32_t rows,
+                                   uint32_t cols) {
+    using T = typename Unit<E>::T;
+    __shared__ T tile[32][33];
+    const uint32_t tiles_r = (rows + 31) / 32, tiles_c = (cols + 31) / 32;
+    const uint64_t tiles = (uint64_t)batches * tiles_r * tiles_c;
+    for (uint64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+        const uint32_t tc = (uint32_t)(t % tiles_c), tr = (uint32_t)((t / tiles_c) % tiles_r);
+        const uint64_t bt = t / ((uint64_t)tiles_c * tiles_r);
+        const T *src = reinterpret_cast<const T *>(a) + bt * rows * cols;
+        T *dst = reinterpret_cast<T *>(z) + bt * rows * cols;
+        const uint32_t c = tc * 32 + threadIdx.x % 32;
+        for (uint32_t i = threadIdx.x / 32; i < 32; i += blockDim.x / 32) {
+            const uint32_t r = tr * 32 + i;
+            if (r < rows && c < cols) tile[i][threadIdx.x % 32] = src[(uint64_t)r * cols + c];
+        }
+        __syncthreads();
+        const uint32_t r = tr * 32 + threadIdx.x % 32;
+        for (uint32_t i = threadIdx.x / 32; i < 32; i += blockDim.x / 32) {
+            const uint32_t cc = tc * 32 + i;
+            if (r < rows && cc < cols) dst[(uint64_t)cc * rows + r] = tile[threadIdx.x % 32][i];
+        }
+        __syncthreads();
+    }
+}
+
+struct Perm5 {
+    int p[5];
+};
+
+__global__ void permute_kernel(const uint8_t *__restrict__ a, uint8_t *__restrict__ z, Shape5 in, Perm5 pm, int elem,
+                               uint64_t count) {
+    const int *perm = pm.p;
+    uint64_t istride[5];
+    uint64_t acc = 1;
+    for (int d = in.rank - 1; d >= 0; d--) {
+        istride[d] = acc;
+        acc *= in.d[d];
+    }
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (uint64_t)gridDim.x * blockDim.x) {
+        uint64_t rem = i, src = 0;
+        for (int d = in.rank - 1; d >= 0; d--) {
+            const uint32_t extent = in.d[perm[d]];
+            const uint64_t idx = rem % extent;
+            rem /= extent;
+            src += idx * istride[perm[d]];
+        }
+        for (int e = 0; e < elem; e++) z[i * elem + e] = a[src * elem + e];
+    }
+}
+
+// ---------------------------------------------------------------- resize (code 21) -----------
+template <int V>
+__global__ void resize_kernel(const uint8_t *__restrict__ a, uint8_t *__restrict__ z, uint64_t pixels, int oh, int ow,
+                              uint32_t c, uint64_t img_bytes, const uint32_t *__restrict__ offsets) {
+    using T = typename Unit<V>::T;
+    const uint32_t per = c / V;
+    const uint64_t units = pixels * per;
+    for (uint64_t u = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; u < units; u += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t pix = u / per;
+        const uint32_t k = (uint32_t)(u - pix * per);
+        const int x = (int)(pix % ow), y = (int)((pix / ow) % oh);
+        const uint64_t img = pix / ((uint64_t)ow * oh);
+        const uint8_t *src = a + img * img_bytes + offsets[y] + offsets[oh + x];
+        reinterpret_cast<T *>(z)[u] = reinterpret_cast<const T *>(src)[k];
+    }
+}
+
+// ---------------------------------------------------------------- pool (code 16) -------------
+// Max starts at -128 and takes valid taps; average sums raw int8 over valid taps and rounds
+// half away from zero with truncating division (qnn.c:1228-1243; global_pool9 agrees).
+__global__ void pool_kernel(const int8_t *__restrict__ x, int8_t *__restrict__ y, ConvGeom g, int is_max, int lo, int hi) {
+    const uint64_t total = (uint64_t)g.n * g.oh * g.ow * g.oc;
+    for (uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (uint64_t)gridDim.x * blockDim.x) {
+        const int c = (int)(idx % g.oc);
+        const uint64_t pix = idx / g.oc;
+        const int ox = (int)(pix % g.ow);
+        const int oy = (int)((pix / g.ow) % g.oh);
+        const uint64_t n = pix / ((uint64_t)g.ow * g.oh);
+        int acc = is_max ? -128 : 0, count = 0;
+        for (int ky = 0; ky < g.kh; ky++) {
+            const int iy = oy * g.sh - g.pt + ky;
+            if (iy < 0 || iy >= g.ih) continue;
+            for (int kx = 0; kx < g.kw; kx++) {
+                const int ix = ox * g.sw - g.pl + kx;
+                if (ix < 0 || ix >= g.iw) continue;
+                const int v = x[((n * g.ih + iy) * g.iw + ix) * g.ic + c];
+                count++;
+                if (is_max) acc = v > acc ? v : acc;
+                else acc += v;
+            }
+        }
+        if (!is_max) {
+            const int half = count / 2;
+            acc = count ? (acc + (acc > 0 ? half : -half)) / count : 0;
+        }
+        y[idx] = (int8_t)dev_clamp(acc, lo, hi);
+    }
+}
+
+// Max pool, 16 channels per thread (ic % 16 == 0): byte-wise signed max, then the clamp.
+__global__ void maxpool16_kernel(const int8_t *__restrict__ x, int8_t *__restrict__ y, ConvGeom g, uint32_t lo4,
+                                 uint32_t hi4) {
+    const int c16 = g.oc / 16;
+    const uint64_t total = (uint64_t)g.n * g.oh * g.ow * c16;
+    for (uint64_t u = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; u < total; u += (uint64_t)gridDim.x * blockDim.x) {
+        const int cg = (int)(u % c16);
+        const uint64_t pix = u / c16;
+        const int ox = (int)(pix % g.ow), oy = (int)((pix / g.ow) % g.oh);
+        const uint64_t n = pix / ((uint64_t)g.ow * g.oh);
+        uint4 m = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
+        for (int ky = 0; ky < g.kh; ky++) {
+            const int iy = oy * g.sh - g.pt + ky;
+            if (iy < 0 || iy >= g.ih) continue;
+            for (int kx = 0; kx < g.kw; kx++) {
+                const int ix = ox * g.sw - g.pl + kx;
+                if (ix < 0 || ix >= g.iw) continue;
+                const uint4 v = __ldg(reinterpret_cast<const uint4 *>(x + ((n * g.ih + iy) * g.iw + ix) * g.ic) + cg);
+                m.x = __vmaxs4(m.x, v.x);
+                m.y = __vmaxs4(m.y, v.y);
+                m.z = __vmaxs4(m.z, v.z);
+                m.w = __vmaxs4(m.w, v.w);
+            }
+        }
+        m.x = __vmins4(__vmaxs4(m.x, lo4), hi4);
+        m.y = __vmins4(__vmaxs4(m.y, lo4), hi4);
+        m.z = __vmins4(__vmaxs4(m.z, lo4), hi4);
+        m.w = __vmins4(__vmaxs4(m.w, lo4), hi4);
+        reinterpret_cast<uint4 *>(y + pix * g.oc)[cg] = m;
+    }
+}
+
+// ---------------------------------------------------------------- bmm (code 27) --------------
+// qnn.c:119-153 computes sum (x + 128) w - (xz + 128) sum w - wz sum (x + 128) + k (xz + 128) wz
+// in wrapping int32, which is sum (x - xz)(w - wz). Block = 32 x 32 outputs of one batch; the
+// operands pass through shared memory 32 reduction steps at a time with the zero points
+// subtracted; each thread accumulates 4 outputs (rows ty + 8 i, column tx).
+__global__ void bmm_kernel(const int8_t *__restrict__ x, const int8_t *__restrict__ w, int8_t *__restrict__ y,
+                           uint32_t batches, int m, int n, int k, int xz, int wz, int yz, int mult, int s, int adj_x,
+                           int adj_y) {
+    __shared__ int16_t xs[32][33], ws[32][33];
+    const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;  // 32 x 8 threads
+    const int tm = (m + 31) / 32, tn = (n + 31) / 32;
+    const uint64_t tiles = (uint64_t)batches * tm * tn;
+    for (uint64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+        const int bn = (int)(t % tn), bm = (int)((t / tn) % tm);
+        const uint64_t bt = t / ((uint64_t)tn * tm);
+        const int8_t *xb = x + bt * (uint64_t)m * k, *wb = w + bt * (uint64_t)k * n;
+        int32_t acc[4] = {0, 0, 0, 0};
+        for (int k0 = 0; k0 < k; k0 += 32) {
+            for (int i = ty; i < 32; i += 8) {
+                // xs[row][kk] = x[bm*32 + row][k0 + kk] - xz ; ws[kk][col] = w[k0 + kk][bn*32 + col] - wz
+                const int r = bm * 32 + i, kk = k0 + tx;
+                xs[i][tx] = (r < m && kk < k) ? (int16_t)(xb[adj_x ? (uint64_t)kk * m + r : (uint64_t)r * k + kk] - xz) : 0;
+                const int kr = k0 + i, cc = bn * 32 + tx;
+                ws[i][tx] = (kr < k && cc < n) ? (int16_t)(wb[adj_y ? (uint64_t)cc * k + kr : (uint64_t)kr * n + cc] - wz)
+                                               : 0;
+            }
+            __syncthreads();
+#pragma unroll 8
+            for (int kk = 0; kk < 32; kk++) {
+                const int wv = ws[kk][tx];
+#pragma unroll
+                for (int i = 0; i < 4; i++) acc[i] += (int)xs[ty + 8 * i][kk] * wv;
+            }
+            __syncthreads();
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int r = bm * 32 + ty + 8 * i, c = bn * 32 + tx;
+            if (r < m && c < n)
+                y[bt * (uint64_t)m * n + (uint64_t)r * n + c] = (int8_t)dev_clamp(dev_scale(acc[i], mult, s) + yz, -128, 127);
+        }
+    }
+}
+
+// ---------------------------------------------------------------- pack (code 19) -------------
+template <int V>
+__global__ void pack_kernel(Segments segs, uint8_t *__restrict__ z, uint32_t z_bytes, int images) {
+    using T = typename Unit<V>::T;
+    const uint32_t per = z_bytes / V;
+    const uint64_t units = (uint64_t)per * images;
+    for (uint64_t u = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; u < units; u += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t img = u / per;
+        const uint32_t off = (uint32_t)(u - img * per) * V;
+        int s = 0;
+        while (s + 1 < segs.count && off >= segs.dst_offset[s + 1]) s++;
+        reinterpret_cast<T *>(z)[u] =
+            *reinterpret_cast<const T *>(segs.src[s] + img * segs.bytes[s] + (off - segs.dst_offset[s]));
+    }
+}
+
+}  // namespace
+
+void launch_pool(const int8_t *x, int8_t *y, const ConvGeom &g, int is_max, int lo, int hi, cudaStream_t s) {
+    if (is_max && g.ic == g.oc && g.oc % 16 == 0 && unit_for(reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) == 16) {
+        const uint64_t total = (uint64_t)g.n * g.oh * g.ow * (g.oc / 16);
+        maxpool16_kernel<<<grid_for(total, kT), kT, 0, s>>>(x, y, g, 0x01010101u * (uint8_t)lo, 0x01010101u * (uint8_t)hi);
+        return;
+    }
+    const uint64_t total = (uint64_t)g.n * g.oh * g.ow * g.oc;
+    pool_kernel<<<grid_for(total, kT), kT, 0, s>>>(x, y, g, is_max, lo, hi);
+}
+
+void launch_bmm(const int8_t *x, const int8_t *w, int8_t *y, size_t batches, int m, int n, int k, const int32_t q7[7],
+                cudaStream_t s) {
+    const uint64_t tiles = (uint64_t)batches * ((m + 31) / 32) * ((n + 31) / 32);
+    bmm_kernel<<<grid_for(tiles, 1), kT, 0, s>>>(x, w, y, (uint32_t)batches, m, n, k, q7[0], q7[1], q7[2], q7[3], q7[4],
+                                                  q7[5], q7[6]);
+}
+
+void launch_permute(const uint8_t *a, uint8_t *z, const Shape5 &in, const int perm[5], int elem_bytes, cudaStream_t s) {
+    uint64_t count = 1;
+    for (int d = 0; d < in.rank; d++) count *= in.d[d];
+    // Merge runs of input axes that stay adjacent and in order in the output.
+    int groups[5][2], ng = 0;  // [first input axis, last input axis] per output group
+    for (int d = 0; d < in.rank; d++) {
+        if (ng && perm[d] == groups[ng - 1][1] + 1) groups[ng - 1][1] = perm[d];
+        else groups[ng][0] = groups[ng][1] = perm[d], ng++;
+    }
+    auto extent = [&](int g) {
+        uint64_t e = 1;
+        for (int d = groups[g][0]; d <= groups[g][1]; d++) e *= in.d[d];
+        return e;
+    };
+    // batched 2-D transpose: output groups (B, C, R) with input order (B, R, C)
+    bool t2 = false;
+    uint64_t B = 1, R = 0, Cc = 0;
+    if (ng == 2 && groups[0][0] > groups[1][0]) t2 = true, R = extent(1), Cc = extent(0);
+    if (ng == 3 && groups[0][0] == 0 && groups[1][0] > groups[2][0]) t2 = true, B = extent(0), R = extent(2), Cc = extent(1);
+    if (t2 && B * R * Cc == count && R < (1u << 31) && Cc < (1u << 31)) {
+        const uint64_t tiles = B * ((R + 31) / 32) * ((Cc + 31) / 32);
+        const unsigned grid = (unsigned)std::min<uint64_t>(tiles, 148ull * 16);
+        if (elem_bytes == 1) transpose2d_kernel<1><<<grid, kT, 0, s>>>(a, z, (uint32_t)B, (uint32_t)R, (uint32_t)Cc);
+        else if (elem_bytes == 4) transpose2d_kernel<4><<<grid, kT, 0, s>>>(a, z, (uint32_t)B, (uint32_t)R, (uint32_t)Cc);
+        else t2 = false;
+        if (t2) return;
+    }
+    Perm5 p;
+    for (int d = 0; d < 5; d++) p.p[d] = perm[d];
+    permute_kernel<<<grid_for(count, kT), kT, 0, s>>>(a, z, in, p, elem_bytes, count);
+}
+
+void launch_slice(const uint8_t *a, uint8_t *z, const Shape5 &in, const Shape5 &out, const uint32_t begin[5],
+                  cudaStream_t s) {
+    uint64_t istride[5], acc = 1;
+    for (int d = in.rank - 1; d >= 0; d--) istride[d] = acc, acc *= in.d[d];
+    int k = -1;  // innermost sliced axis
+    for (int d = 0; d < in.rank; d++)
+        if (out.d[d] != in.d[d]) k = d;
+    RunCopy rc{};
+    if (k < 0) {
+        rc.ndim = 0, rc.rows = 1, rc.run = (uint32_t)acc;
+    } else {
+        // run: out.d[k] * (full trailing axes) contiguous bytes; rows over the axes before k
+        rc.run = (uint32_t)(out.d[k] * istride[k]);
+        rc.base = begin[k] * istride[k];
+        rc.rows = 1;
+        // axes before k, merged into at most 4 mixed-radix digits (leading ones first)
+        int nd = 0;
+        for (int d = 0; d < k; d++) {
+            rc.base += (uint64_t)begin[d] * istride[d];
+            if (out.d[d] == 1) continue;
+            rc.rows *= out.d[d];
+            rc.extent[nd] = out.d[d];  // k <= 4, so at most 4 digits
+            rc.stride[nd] = istride[d];
+            nd++;
+        }
+        rc.ndim = nd;
+    }
+    rc.dst_stride = rc.run;
+    run_copy(a, z, rc, s);
+}
+
+void launch_concat(const uint8_t *a, const uint8_t *b, uint8_t *z, size_t outer, size_t ac, size_t bc, cudaStream_t s) {
+    const int v = unit_for(ac, bc, reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+                                       reinterpret_cast<uintptr_t>(z));
+    const uint64_t units = outer * (ac + bc) / v;
+    if (v == 16) concat_kernel<16><<<grid_for(units, kT), kT, 0, s>>>(a, b, z, outer, (uint32_t)ac, (uint32_t)bc);
+    else if (v == 4) concat_kernel<4><<<grid_for(units, kT), kT, 0, s>>>(a, b, z, outer, (uint32_t)ac, (uint32_t)bc);
+    else concat_kernel<1><<<grid_for(units, kT), kT, 0, s>>>(a, b, z, outer, (uint32_t)ac, (uint32_t)bc);
+}
+
+void launch_resize(const uint8_t *a, uint8_t *z, int n, int ih, int iw, int c, int oh, int ow, const uint32_t *offsets,
+                   cudaStream_t s) {
+    const uint64_t pixels = (uint64_t)n * oh * ow, img = (uint64_t)ih * iw * c;
+    const int v = unit_for((uint64_t)c, img, reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(z));
+    const uint64_t units = pixels * (c / v);
+    if (v == 16) resize_kernel<16><<<grid_for(units, kT), kT, 0, s>>>(a, z, pixels, oh, ow, (uint32_t)c, img, offsets);
+    else if (v == 4) resize_kernel<4><<<grid_for(units, kT), kT, 0, s>>>(a, z, pixels, oh, ow, (uint32_t)c, img, offsets);
+    else resize_kernel<1><<<grid_for(units, kT), kT, 0, s>>>(a, z, pixels, oh, ow, (uint32_t)c, img, offsets);
+}
+
+void launch_pack(const Segments &segs, uint8_t *z, uint32_t z_bytes, int images, cudaStream_t s) {
+    uint64_t m = z_bytes | reinterpret_cast<uintptr_t>(z);
+    for (int i = 0; i < segs.count; i++) m |= segs.bytes[i] | segs.dst_offset[i] | reinterpret_cast<uintptr_t>(segs.src[i]);
+    const int v = unit_for(m);
+    const uint64_t units = (uint64_t)z_bytes / v * images;
+    if (v == 16) pack_kernel<16><<<grid_for(units, kT), kT, 0, s>>>(segs, z, z_bytes, images);
+    else if (v == 4) pack_kernel<4><<<grid_for(units, kT), kT, 0, s>>>(segs, z, z_bytes, images);
+    else pack_kernel<1><<<grid_for(units, kT), kT, 0, s>>>(segs, z, z_bytes, images);
+}
+
+}  // namespace uq

@@ -114,39 +114,6 @@ __global__ void depthwise_kernel(const int8_t *__restrict__ x, const int8_t *__r
     }
 }
 
-// ---------------------------------------------------------------- code 16 -------------
-// Max starts at -128 and takes valid taps; average sums raw int8 over valid taps and rounds
-// half away from zero with truncating division (qnn.c:1228-1243; global_pool9 agrees).
-__global__ void pool_kernel(const int8_t *__restrict__ x, int8_t *__restrict__ y, ConvGeom g, int is_max, int lo, int hi) {
-    const uint64_t total = (uint64_t)g.n * g.oh * g.ow * g.oc;
-    for (uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-         idx += (uint64_t)gridDim.x * blockDim.x) {
-        const int c = (int)(idx % g.oc);
-        const uint64_t pix = idx / g.oc;
-        const int ox = (int)(pix % g.ow);
-        const int oy = (int)((pix / g.ow) % g.oh);
-        const uint64_t n = pix / ((uint64_t)g.ow * g.oh);
-        int acc = is_max ? -128 : 0, count = 0;
-        for (int ky = 0; ky < g.kh; ky++) {
-            const int iy = oy * g.sh - g.pt + ky;
-            if (iy < 0 || iy >= g.ih) continue;
-            for (int kx = 0; kx < g.kw; kx++) {
-                const int ix = ox * g.sw - g.pl + kx;
-                if (ix < 0 || ix >= g.iw) continue;
-                const int v = x[((n * g.ih + iy) * g.iw + ix) * g.ic + c];
-                count++;
-                if (is_max) acc = v > acc ? v : acc;
-                else acc += v;
-            }
-        }
-        if (!is_max) {
-            const int half = count / 2;
-            acc = (acc + (acc > 0 ? half : -half)) / count;
-        }
-        y[idx] = (int8_t)dev_clamp(acc, lo, hi);
-    }
-}
-
 // ---------------------------------------------------------------- code 17 -------------
 // qnn.c:1082-1088: table softmax, one thread per row.
 __global__ void softmax_table_kernel(const int8_t *__restrict__ x, int8_t *__restrict__ y, size_t rows, int width,
@@ -277,96 +244,7 @@ __global__ void mean_kernel(const int8_t *__restrict__ x, int8_t *__restrict__ y
     }
 }
 
-// ---------------------------------------------------------------- code 27 -------------
-// qnn.c:119-153 computes sum (x + 128) w - (xz + 128) sum w - wz sum (x + 128) + k (xz + 128) wz
-// in wrapping int32, which is sum (x - xz)(w - wz); one thread per output element.
-__global__ void bmm_kernel(const int8_t *__restrict__ x, const int8_t *__restrict__ w, int8_t *__restrict__ y, size_t batches,
-                           int m, int n, int k, int xz, int wz, int yz, int mult, int s, int adj_x, int adj_y) {
-    const size_t total = batches * (size_t)m * n;
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-        const int c = (int)(i % n);
-        const int r = (int)((i / n) % m);
-        const size_t bt = i / ((size_t)m * n);
-        const int8_t *xb = x + bt * (size_t)m * k, *wb = w + bt * (size_t)k * n;
-        int32_t v = 0;
-        for (int t = 0; t < k; t++) {
-            const int xv = xb[adj_x ? (size_t)t * m + r : (size_t)r * k + t];
-            const int wv = wb[adj_y ? (size_t)c * k + t : (size_t)t * n + c];
-            v += (xv - xz) * (wv - wz);
-        }
-        y[i] = (int8_t)dev_clamp(dev_scale(v, mult, s) + yz, -128, 127);
-    }
-}
-
 // ---------------------------------------------------------------- byte movement -------
-struct Perm5 {
-    int p[5];
-};
-
-__global__ void permute_kernel(const uint8_t *__restrict__ a, uint8_t *__restrict__ z, Shape5 in, Perm5 pm, int elem,
-                               uint64_t count) {
-    const int *perm = pm.p;
-    uint64_t istride[5];
-    uint64_t acc = 1;
-    for (int d = in.rank - 1; d >= 0; d--) {
-        istride[d] = acc;
-        acc *= in.d[d];
-    }
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (uint64_t)gridDim.x * blockDim.x) {
-        uint64_t rem = i, src = 0;
-        for (int d = in.rank - 1; d >= 0; d--) {
-            const uint32_t extent = in.d[perm[d]];
-            const uint64_t idx = rem % extent;
-            rem /= extent;
-            src += idx * istride[perm[d]];
-        }
-        for (int e = 0; e < elem; e++) z[i * elem + e] = a[src * elem + e];
-    }
-}
-
-__global__ void slice_kernel(const uint8_t *__restrict__ a, uint8_t *__restrict__ z, Shape5 in, Shape5 out, uint4 b03,
-                             uint32_t b4, uint64_t count) {
-    const uint32_t begin[5] = {b03.x, b03.y, b03.z, b03.w, b4};
-    uint64_t istride[5];
-    uint64_t acc = 1;
-    for (int d = in.rank - 1; d >= 0; d--) {
-        istride[d] = acc;
-        acc *= in.d[d];
-    }
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (uint64_t)gridDim.x * blockDim.x) {
-        uint64_t rem = i, src = 0;
-        for (int d = out.rank - 1; d >= 0; d--) {
-            const uint64_t idx = rem % out.d[d];
-            rem /= out.d[d];
-            src += (idx + begin[d]) * istride[d];
-        }
-        z[i] = a[src];
-    }
-}
-
-__global__ void concat_kernel(const uint8_t *__restrict__ a, const uint8_t *__restrict__ b, uint8_t *__restrict__ z,
-                              uint64_t outer, uint64_t ac, uint64_t bc) {
-    const uint64_t row = ac + bc, total = outer * row;
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
-        const uint64_t r = i / row, c = i % row;
-        z[i] = c < ac ? a[r * ac + c] : b[r * bc + (c - ac)];
-    }
-}
-
-__global__ void resize_kernel(const uint8_t *__restrict__ a, uint8_t *__restrict__ z, int n, int ih, int iw, int c, int oh,
-                              int ow, const uint32_t *__restrict__ offsets) {
-    const uint64_t total = (uint64_t)n * oh * ow * c;
-    const uint64_t stride = (uint64_t)ih * iw * c;
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
-        const int ch = (int)(i % c);
-        const uint64_t pix = i / c;
-        const int x = (int)(pix % ow);
-        const int y = (int)((pix / ow) % oh);
-        const uint64_t img = pix / ((uint64_t)ow * oh);
-        z[i] = a[img * stride + offsets[y] + offsets[oh + x] + ch];
-    }
-}
-
 __global__ void pad_kernel(const uint8_t *__restrict__ a, uint8_t *__restrict__ z, int images, uint4 ad, uint4 zd, int4 lo4,
                            int8_t value) {
     const uint64_t zimg = (uint64_t)zd.x * zd.y * zd.z * zd.w, aimg = (uint64_t)ad.x * ad.y * ad.z * ad.w;
@@ -388,17 +266,6 @@ __global__ void pad_kernel(const uint8_t *__restrict__ a, uint8_t *__restrict__ 
     }
 }
 
-__global__ void pack_kernel(Segments segs, uint8_t *__restrict__ z, uint32_t z_bytes, int images) {
-    const uint64_t total = (uint64_t)z_bytes * images;
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
-        const uint64_t img = i / z_bytes;
-        const uint32_t off = (uint32_t)(i % z_bytes);
-        int s = 0;
-        while (s + 1 < segs.count && off >= segs.dst_offset[s + 1]) s++;
-        z[i] = segs.src[s][img * segs.bytes[s] + (off - segs.dst_offset[s])];
-    }
-}
-
 }  // namespace
 
 void launch_conv_simt(const int8_t *x, const int8_t *w_packed, int8_t *y, const ConvGeom &g, const Requant &r,
@@ -415,11 +282,6 @@ void launch_depthwise(const int8_t *x, const int8_t *w, int8_t *y, const ConvGeo
         const uint64_t total = (uint64_t)g.n * g.oh * g.ow * g.oc;
         depthwise_kernel<1><<<grid_for(total, kThreads), kThreads, 0, s>>>(x, w, y, g, r);
     }
-}
-
-void launch_pool(const int8_t *x, int8_t *y, const ConvGeom &g, int is_max, int lo, int hi, cudaStream_t s) {
-    const uint64_t total = (uint64_t)g.n * g.oh * g.ow * g.oc;
-    pool_kernel<<<grid_for(total, kThreads), kThreads, 0, s>>>(x, y, g, is_max, lo, hi);
 }
 
 void launch_softmax_table(const int8_t *x, int8_t *y, size_t rows, int width, const int32_t *table, int lo, int hi,
@@ -449,49 +311,12 @@ void launch_mean(const int8_t *x, int8_t *y, size_t batches, int channels, const
                                                                             q5[3], q5[4]);
 }
 
-void launch_bmm(const int8_t *x, const int8_t *w, int8_t *y, size_t batches, int m, int n, int k, const int32_t q7[7],
-                cudaStream_t s) {
-    const size_t total = batches * (size_t)m * n;
-    bmm_kernel<<<grid_for(total, kThreads), kThreads, 0, s>>>(x, w, y, batches, m, n, k, q7[0], q7[1], q7[2], q7[3], q7[4],
-                                                             q7[5], q7[6]);
-}
-
-void launch_permute(const uint8_t *a, uint8_t *z, const Shape5 &in, const int perm[5], int elem_bytes, cudaStream_t s) {
-    uint64_t count = 1;
-    for (int d = 0; d < in.rank; d++) count *= in.d[d];
-    Perm5 p;
-    for (int d = 0; d < 5; d++) p.p[d] = perm[d];
-    permute_kernel<<<grid_for(count, kThreads), kThreads, 0, s>>>(a, z, in, p, elem_bytes, count);
-}
-
-void launch_slice(const uint8_t *a, uint8_t *z, const Shape5 &in, const Shape5 &out, const uint32_t begin[5],
-                  cudaStream_t s) {
-    uint64_t count = 1;
-    for (int d = 0; d < out.rank; d++) count *= out.d[d];
-    slice_kernel<<<grid_for(count, kThreads), kThreads, 0, s>>>(a, z, in, out, make_uint4(begin[0], begin[1], begin[2], begin[3]),
-                                                               begin[4], count);
-}
-
-void launch_concat(const uint8_t *a, const uint8_t *b, uint8_t *z, size_t outer, size_t ac, size_t bc, cudaStream_t s) {
-    concat_kernel<<<grid_for(outer * (ac + bc), kThreads), kThreads, 0, s>>>(a, b, z, outer, ac, bc);
-}
-
-void launch_resize(const uint8_t *a, uint8_t *z, int n, int ih, int iw, int c, int oh, int ow, const uint32_t *offsets,
-                   cudaStream_t s) {
-    const uint64_t total = (uint64_t)n * oh * ow * c;
-    resize_kernel<<<grid_for(total, kThreads), kThreads, 0, s>>>(a, z, n, ih, iw, c, oh, ow, offsets);
-}
-
 void launch_pad(const uint8_t *a, uint8_t *z, int images, const uint32_t ad[4], const uint32_t zd[4], const int32_t pads[8],
                 int8_t value, cudaStream_t s) {
     const uint64_t total = (uint64_t)zd[0] * zd[1] * zd[2] * zd[3] * images;
     pad_kernel<<<grid_for(total, kThreads), kThreads, 0, s>>>(a, z, images, make_uint4(ad[0], ad[1], ad[2], ad[3]),
                                                              make_uint4(zd[0], zd[1], zd[2], zd[3]),
                                                              make_int4(pads[0], pads[2], pads[4], pads[6]), value);
-}
-
-void launch_pack(const Segments &segs, uint8_t *z, uint32_t z_bytes, int images, cudaStream_t s) {
-    pack_kernel<<<grid_for((uint64_t)z_bytes * images, kThreads), kThreads, 0, s>>>(segs, z, z_bytes, images);
 }
 
 void launch_copy(const void *src, void *dst, size_t bytes, cudaStream_t s) {
