@@ -308,12 +308,11 @@ __device__ __forceinline__ uint32_t pack_sat_s8x4(int32_t v0, int32_t v1, int32_
     return d;
 }
 
-// Requantise 16 accumulators (columns c0..c0+15 of one row) and pack them as int8. The clamp to
-// [lo, hi] (both within int8) is applied per byte after a saturating pack, which gives the same
-// bytes as clamping the int32 values.
+// Requantise 16 accumulators (columns c0..c0+15 of one row), clamp to [lo, hi] and pack them as
+// int8 (the clamp is two integer min/max per value; byte-SIMD min/max would be emulated).
 template <int EPI>
 __device__ __forceinline__ uint4 epilogue_chunk(const uint32_t (&r)[16], const EpiSoA &E, const uint8_t *lut, int c0,
-                                                uint32_t lo4, uint32_t hi4) {
+                                                int lo, int hi) {
     uint32_t packed[4];
     const longlong2 *K2 = reinterpret_cast<const longlong2 *>(E.k + c0);
     const int4 *M4 = reinterpret_cast<const int4 *>(E.m + c0);
@@ -352,8 +351,9 @@ __device__ __forceinline__ uint4 epilogue_chunk(const uint32_t (&r)[16], const E
                 v[i] = ((int32_t)(p >> 32)) >> ss[i];
             }
         }
+#pragma unroll
+        for (int i = 0; i < 4; i++) v[i] = min(max(v[i], lo), hi);
         uint32_t w = pack_sat_s8x4(v[0], v[1], v[2], v[3]);
-        w = __vmins4(__vmaxs4(w, lo4), hi4);
         if (lut)
             w = (uint32_t)lut[(w & 0xFF) ^ 0x80] | (uint32_t)lut[((w >> 8) & 0xFF) ^ 0x80] << 8 |
                 (uint32_t)lut[((w >> 16) & 0xFF) ^ 0x80] << 16 | (uint32_t)lut[(w >> 24) ^ 0x80] << 24;
@@ -725,7 +725,6 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
         const int half = e >> 2;                  // which 16-column chunks this warp takes
         const int row = quarter * 32 + lane;
         const uint8_t *lut = p.post ? sLut : nullptr;
-        const uint32_t lo4 = 0x01010101u * (uint32_t)(uint8_t)p.lo, hi4 = 0x01010101u * (uint32_t)(uint8_t)p.hi;
         const int n0 = ntile * p.bn;
         const int cols = min(p.bn, p.oc - n0);
         const int live_chunks = (cols + 15) / 16;
@@ -758,7 +757,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
                 for (int ci = 0; ci < my_chunks; ci++) {
                     const bool more = ci + 1 < my_chunks;
                     if (more) tmem_ld16_nowait(taddr + (ci + 1) * 16, rb);
-                    const uint4 v = epilogue_chunk<EPI>(ra, E, lut, c0 + ci * 16, lo4, hi4);
+                    const uint4 v = epilogue_chunk<EPI>(ra, E, lut, c0 + ci * 16, p.lo, p.hi);
                     st_shared16(smem_u32(stage + (size_t)lane * p.box + ((ci ^ swz_row) << 4)), v);
                     if (more) tmem_wait_ld(rb);
 #pragma unroll
@@ -796,7 +795,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
                 while (ci < live_chunks) {
                     const int next = ci + 2;
                     if (next < live_chunks) tmem_ld16_nowait(taddr + next * 16, rb);
-                    const uint4 v = epilogue_chunk<EPI>(ra, E, lut, ci * 16, lo4, hi4);
+                    const uint4 v = epilogue_chunk<EPI>(ra, E, lut, ci * 16, p.lo, p.hi);
                     st_shared16(smem_u32(stage + (size_t)row * (p.bn + 16) + ci * 16), v);
                     if (next < live_chunks) tmem_wait_ld(rb);
 #pragma unroll

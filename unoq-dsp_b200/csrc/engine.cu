@@ -6,6 +6,7 @@
 #include <mutex>
 #include <numeric>
 
+#include "conv_small.cuh"
 #include "conv_tc.cuh"
 #include "dw.cuh"
 #include "kernels.cuh"
@@ -149,11 +150,24 @@ int Engine::prepare() {
                 const int32_t *dq = reinterpret_cast<const int32_t *>(dconst(o.p[0]));
                 Requant r{dq + kHead, dq + kHead + g.oc, dq + kHead + 2 * g.oc,
                           o.p[1] ? dconst(o.p[1] - 1) : nullptr, q[13], q[14], q[15]};
+                const uint32_t ta = o.a, tz = o.out;
+                ConvSmall *sm = nullptr;
+                int rc = conv_small_prepare(P.s8(o.b), q, r.post, g, [this](size_t n) { return prep_alloc(n); }, &sm);
+                if (rc) return rc;
+                if (sm) {
+                    std::shared_ptr<ConvSmall> keep(sm, conv_small_free);
+                    st.run = [keep, g, ta, tz](const BatchCtx &B, cudaStream_t s) -> int {
+                        ConvGeom gb = g;
+                        gb.n = g.n * (int)B.images;
+                        return conv_small_launch(*keep, reinterpret_cast<const int8_t *>(B.ptr[ta]),
+                                                 reinterpret_cast<int8_t *>(B.ptr[tz]), gb, s);
+                    };
+                    break;
+                }
                 ConvTc *tc = nullptr;
-                int rc = conv_tc_prepare(P.s8(o.b), q, r.post, g, [this](size_t n) { return prep_alloc(n); }, &tc);
+                rc = conv_tc_prepare(P.s8(o.b), q, r.post, g, [this](size_t n) { return prep_alloc(n); }, &tc);
                 if (rc) return rc;
                 const int8_t *w = reinterpret_cast<const int8_t *>(dconst(o.b));
-                const uint32_t ta = o.a, tz = o.out;
                 if (tc) {
                     std::shared_ptr<ConvTc> keep(tc, conv_tc_free);
                     st.run = [keep, g, ta, tz](const BatchCtx &B, cudaStream_t s) -> int {
