@@ -272,6 +272,7 @@ def all_cases(scale=1):
                                                     padding=(1, 0, 2, 3), act="relu6")),
         ("conv_rgb_band", lambda r: conv_case(r, (1, 10 * s, 16, 3), 16, (3, 3), (2, 2), xq=(0.02, 9))),
         ("conv_ic8_band", lambda r: conv_case(r, (1, 6 * s, 10, 8), 24, (3, 3), (1, 1))),
+        ("conv_rgb_odd_width", lambda r: conv_case(r, (1, 9 * s, 13, 3), 16, (3, 3), (2, 2), xq=(0.02, -5))),
         ("conv_ic8_small", lambda r: conv_case(r, (1, 9 * s, 11, 8), 16, (3, 3), (1, 1))),
         ("conv_ic16_small_post", lambda r: conv_post_case(r, (1, 8 * s, 10, 16), 8, (3, 3), (2, 2))),
         ("conv_fc", lambda r: conv_case(r, (1, 1, 1, 96), 40, (1, 1), (1, 1), act="none")),

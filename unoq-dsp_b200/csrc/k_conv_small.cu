@@ -76,8 +76,39 @@ __global__ void __launch_bounds__(kThreads) conv_small_kernel(const SmallParams 
     if (p.post)
         for (int i = threadIdx.x; i < 256; i += kThreads) sLut[i] = p.post[i];
     for (int i = threadIdx.x; i < p.oc; i += kThreads) sEpi[i] = p.epi[i];
-    // band fill: one pixel (IC4 words) per unit
     const uint32_t fillw = 0x01010101u * (uint8_t)p.xzp;
+    if (IC4 == 1 && p.ic == 3) {
+        // RGB: image-aligned groups of 4 pixels are 3 aligned words; unpack to one word per pixel
+        const int g0 = (ix0 >= 0 ? ix0 : ix0 - 3) / 4;  // floor(ix0 / 4)
+        const int groups = (ix0 + p.bc - 1 - g0 * 4) / 4 + 1;
+        for (int u = threadIdx.x; u < p.br * groups; u += kThreads) {
+            const int r = u / groups, gx = g0 + (u - r * groups);
+            const int iy = iy0 + r, x4 = gx * 4;
+            uint32_t v[4] = {fillw, fillw, fillw, fillw};
+            if (iy >= 0 && iy < p.ih) {
+                const int8_t *row = p.x + ((size_t)n * p.ih + iy) * p.iw * 3;
+                if (x4 >= 0 && x4 + 4 <= p.iw && (p.iw & 3) == 0) {  // 4-byte aligned words
+                    const uint32_t *src = reinterpret_cast<const uint32_t *>(row + x4 * 3);
+                    const uint32_t a = __ldg(src), b = __ldg(src + 1), c = __ldg(src + 2);
+                    v[0] = a & 0x00FFFFFFu;
+                    v[1] = __byte_perm(a, b, 0x0543) & 0x00FFFFFFu;
+                    v[2] = __byte_perm(b, c, 0x0432) & 0x00FFFFFFu;
+                    v[3] = c >> 8;
+                } else {
+                    for (int k = 0; k < 4; k++) {
+                        const int ix = x4 + k;
+                        if (ix >= 0 && ix < p.iw)
+                            v[k] = (uint32_t)(uint8_t)__ldg(row + ix * 3) | (uint32_t)(uint8_t)__ldg(row + ix * 3 + 1) << 8 |
+                                   (uint32_t)(uint8_t)__ldg(row + ix * 3 + 2) << 16;
+                    }
+                }
+            }
+            for (int k = 0; k < 4; k++) {
+                const int c = x4 + k - ix0;
+                if (c >= 0 && c < p.bc) sBand[r * p.bc + c] = v[k];
+            }
+        }
+    } else
     for (int u = threadIdx.x; u < p.br * p.bc; u += kThreads) {
         const int r = u / p.bc, c = u - r * p.bc;
         const int iy = iy0 + r, ix = ix0 + c;
@@ -107,10 +138,11 @@ __global__ void __launch_bounds__(kThreads) conv_small_kernel(const SmallParams 
 #pragma unroll
         for (int q = 0; q < IC4; q++) sBand[u * IC4 + q] = v[q];
     }
-    // this thread: output pixels x0 .. x0 + 3 of tile row py, channels og * OCT .. + OCT - 1
+    // this thread: output pixels px0 + s * j (j < 4) of tile row py, channels og * OCT .. + OCT - 1;
+    // s = tw / 4, so the lanes of a warp read neighbouring band pixels for every tap
     const int og = threadIdx.x % p.groups, quad = threadIdx.x / p.groups;
     const int quads_x = p.tw / kPix;
-    const int py = quad / quads_x, px0 = (quad - py * quads_x) * kPix;
+    const int py = quad / quads_x, px0 = quad - py * quads_x;
     uint32_t w[OCT][9][IC4];
     const uint4 *wsrc = reinterpret_cast<const uint4 *>(p.w + (size_t)og * OCT * 9 * IC4);
 #pragma unroll
@@ -122,6 +154,7 @@ __global__ void __launch_bounds__(kThreads) conv_small_kernel(const SmallParams 
     __syncthreads();
     const int oy = ty * p.th + py, ox0 = tx * p.tw + px0;
     if (py >= p.th || oy >= p.oh || ox0 >= p.ow) return;
+    const int pstep = quads_x;  // columns between a thread's pixels
     int acc[kPix][OCT];
 #pragma unroll
     for (int j = 0; j < kPix; j++)
@@ -136,7 +169,7 @@ __global__ void __launch_bounds__(kThreads) conv_small_kernel(const SmallParams 
                 const uint32_t *b = sBand + ((py * S + ky) * p.bc + px0 * S + kx) * IC4 + q;
                 int xv[kPix];
 #pragma unroll
-                for (int j = 0; j < kPix; j++) xv[j] = (int)b[j * S * IC4];
+                for (int j = 0; j < kPix; j++) xv[j] = (int)b[j * pstep * S * IC4];
 #pragma unroll
                 for (int o = 0; o < OCT; o++)
 #pragma unroll
@@ -156,8 +189,8 @@ __global__ void __launch_bounds__(kThreads) conv_small_kernel(const SmallParams 
     }
 #pragma unroll
     for (int j = 0; j < kPix; j++) {
-        if (ox0 + j >= p.ow) break;
-        int8_t *dst = p.y + (((size_t)n * p.oh + oy) * p.ow + ox0 + j) * p.oc + og * OCT;
+        if (ox0 + j * pstep >= p.ow) break;
+        int8_t *dst = p.y + (((size_t)n * p.oh + oy) * p.ow + ox0 + j * pstep) * p.oc + og * OCT;
         if (OCT == 8) *reinterpret_cast<uint2 *>(dst) = make_uint2(packed[j][0], packed[j][1]);
         else if (OCT == 4) *reinterpret_cast<uint32_t *>(dst) = packed[j][0];
         else *reinterpret_cast<uint16_t *>(dst) = (uint16_t)packed[j][0];
