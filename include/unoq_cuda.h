@@ -35,6 +35,19 @@ UG_API int ug_load(const void *plan, uint32_t bytes);
 /* Replaces ug_run (runtime/graph.c:438-448): one image, host buffers, synchronous.
  * A failing run clears the loaded state (reload required), as in the reference. */
 UG_API int ug_run(const void *input, uint32_t input_bytes, void *output, uint32_t output_bytes);
+/* Allocation-free variant of ug_run (no counterpart in the reference). Same arguments, checks
+ * and error codes as ug_run, but the activations live in a fixed 16 MiB device array of this
+ * library (the reference's own arena bound, runtime/graph.h:7) instead of memory allocated per
+ * batch size, and the ops are launched directly rather than through an instantiated CUDA graph:
+ * no cudaMalloc, cudaFree, graph instantiation or other allocating call happens in a call. For
+ * callers that may not allocate device memory once running: real-time loops, hosts that forbid
+ * allocation after start-up, memory-capped processes. The first call for a loaded graph is its
+ * set-up call (host-side layout, the array's device address, first use of the kernels); make it
+ * before any stream capture and before allocation is forbidden. A plan whose one-image
+ * activations exceed 16 MiB gets 20 and stays loaded. Nothing in the array must start at zero.
+ * Overlapping calls on one device would race on the shared array; the graph ABI's lock
+ * serialises them within a process. */
+UG_API int ug_run_static(const void *input, uint32_t input_bytes, void *output, uint32_t output_bytes);
 /* Replace ug_input_bytes / ug_output_bytes (runtime/graph.c:263-264); 0 when nothing loaded. */
 UG_API uint32_t ug_input_bytes(void);
 UG_API uint32_t ug_output_bytes(void);

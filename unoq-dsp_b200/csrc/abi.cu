@@ -54,6 +54,19 @@ int ug_run(const void *input, uint32_t input_bytes, void *output, uint32_t outpu
     return rc;
 }
 
+int ug_run_static(const void *input, uint32_t input_bytes, void *output, uint32_t output_bytes) {
+    std::lock_guard<std::mutex> lk(g_graph_mu);
+    if (!g_graph || !g_graph->ready() || !input || !output || input_bytes != g_graph->input_bytes() ||
+        output_bytes != g_graph->output_bytes())
+        return 22;
+    const int rc = g_graph->run_static(input, output);
+    if (rc && rc != 20) {  // as ug_run: a failed run requires a reload; an oversized plan just is refused
+        delete g_graph;
+        g_graph = nullptr;
+    }
+    return rc;
+}
+
 uint32_t ug_input_bytes(void) {
     std::lock_guard<std::mutex> lk(g_graph_mu);
     return g_graph ? g_graph->input_bytes() : 0;

@@ -69,6 +69,8 @@ void Engine::release() {
     if (stream_) cudaStreamDestroy(stream_);
     stream_ = nullptr;
     steps_.clear();
+    static_ = BatchCtx();  // the static arena is not owned; its layout belongs to this plan
+    static_replicated_.clear();
     ready_ = false;
 }
 
@@ -434,6 +436,31 @@ int Engine::prepare() {
 // lives from its first producer to its last reader; groups whose lifetimes intersect never
 // share bytes. Constants read as activations are replicated per image once, up front.
 int Engine::plan_arena(BatchCtx &B) {
+    std::vector<size_t> offset;
+    std::vector<uint32_t> replicated;
+    size_t total = 0;
+    layout(B.images, offset, replicated, total);
+    const Plan &P = P_;
+    const uint32_t nt = P.h.nt;
+    B.arena_bytes = std::max<size_t>(total, kAlign);
+    UQ_CUDA(cudaMalloc(&B.arena, B.arena_bytes));
+    B.ptr.assign(nt, nullptr);
+    for (uint32_t t = 0; t < nt; t++)
+        B.ptr[t] = offset[t] != kNoOffset ? B.arena + offset[t] : d_const_ + P.ts[t].offset;
+    for (uint32_t r : replicated) {
+        const size_t bytes = P.ts[r].bytes;
+        for (uint32_t i = 0; i < B.images; i++)
+            UQ_CUDA(cudaMemcpyAsync(B.ptr[r] + i * bytes, d_const_ + P.ts[r].offset, bytes, cudaMemcpyDeviceToDevice,
+                                    stream_));
+    }
+    UQ_CUDA(cudaStreamSynchronize(stream_));
+    return 0;
+}
+
+// Arena layout for `images` images (host only): offset[t] of every tensor stored in the arena
+// (kNoOffset for constants read in place), the replicated constants and the total bytes.
+void Engine::layout(uint32_t images, std::vector<size_t> &offset, std::vector<uint32_t> &replicated,
+                    size_t &total_out) const {
     const Plan &P = P_;
     const uint32_t nt = P.h.nt;
     std::vector<int> root(nt);
@@ -470,7 +497,7 @@ int Engine::plan_arena(BatchCtx &B) {
         if (is_const && !replicate[r]) continue;
         if (gid[r] < 0) {
             gid[r] = (int)groups.size();
-            groups.push_back({r, align_up((size_t)P.ts[r].bytes * B.images, kAlign), is_const ? -1 : P.birth[r],
+            groups.push_back({r, align_up((size_t)P.ts[r].bytes * images, kAlign), is_const ? -1 : P.birth[r],
                               is_const ? (int)P.h.no : P.death[r], 0});
         }
         Group &g = groups[gid[r]];
@@ -502,22 +529,13 @@ int Engine::plan_arena(BatchCtx &B) {
         total = std::max(total, off + g.size);
         placed.push_back(gi);
     }
-    B.arena_bytes = std::max<size_t>(total, kAlign);
-    UQ_CUDA(cudaMalloc(&B.arena, B.arena_bytes));
-    B.ptr.assign(nt, nullptr);
-    for (uint32_t t = 0; t < nt; t++) {
-        if (gid[t] >= 0) B.ptr[t] = B.arena + groups[gid[t]].offset;
-        else B.ptr[t] = d_const_ + P.ts[t].offset;
-    }
-    for (const Group &g : groups) {
-        if (!P.ts[g.root].flags) continue;
-        const size_t bytes = P.ts[g.root].bytes;
-        for (uint32_t i = 0; i < B.images; i++)
-            UQ_CUDA(cudaMemcpyAsync(B.arena + g.offset + i * bytes, d_const_ + P.ts[g.root].offset, bytes,
-                                    cudaMemcpyDeviceToDevice, stream_));
-    }
-    UQ_CUDA(cudaStreamSynchronize(stream_));
-    return 0;
+    offset.assign(nt, kNoOffset);
+    for (uint32_t t = 0; t < nt; t++)
+        if (gid[t] >= 0) offset[t] = groups[gid[t]].offset;
+    replicated.clear();
+    for (const Group &g : groups)
+        if (P.ts[g.root].flags) replicated.push_back((uint32_t)g.root);
+    total_out = total;
 }
 
 int Engine::run_steps(const BatchCtx &B, cudaStream_t s, bool profile) {
@@ -699,6 +717,48 @@ int Engine::run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint
     if ((rc = finish(ev1_))) return rc;
     UQ_CUDA(cudaEventElapsedTime(&last_ms_, ev0_, ev1_));
     last_images_ = images;
+    return device_status();
+}
+
+// Fixed device arena of the allocation-free entry point (ug_run_static): the reference's own
+// arena bound (runtime/graph.h:7). Nothing in it needs to start at zero: every activation is
+// written before it is read, and replicated constants are copied in at every call.
+__device__ __align__(256) uint8_t g_static_arena[kStaticArenaBytes];
+
+int Engine::run_static(const void *in, void *out) {
+    if (!ready_ || !in || !out) return 22;
+    UQ_CUDA(cudaSetDevice(device_));
+    if (!static_.arena) {
+        // set-up, once per engine: host-side layout and the arena's device address; no allocation
+        std::vector<size_t> offset;
+        size_t total = 0;
+        layout(1, offset, static_replicated_, total);
+        if (total > kStaticArenaBytes) {
+            set_error("plan needs " + std::to_string(total) + " bytes of activation arena; the static arena holds " +
+                      std::to_string(kStaticArenaBytes));
+            return 20;
+        }
+        void *base = nullptr;
+        UQ_CUDA(cudaGetSymbolAddress(&base, g_static_arena));
+        static_.images = 1;
+        static_.arena_bytes = kStaticArenaBytes;
+        static_.ptr.assign(P_.h.nt, nullptr);
+        for (uint32_t t = 0; t < P_.h.nt; t++)
+            static_.ptr[t] = offset[t] != kNoOffset ? static_cast<uint8_t *>(base) + offset[t] : d_const_ + P_.ts[t].offset;
+        static_.arena = static_cast<uint8_t *>(base);
+    }
+    for (uint32_t r : static_replicated_)
+        UQ_CUDA(cudaMemcpyAsync(static_.ptr[r], d_const_ + P_.ts[r].offset, P_.ts[r].bytes, cudaMemcpyDeviceToDevice,
+                                stream_));
+    UQ_CUDA(cudaMemcpyAsync(static_.ptr[P_.h.input], in, input_bytes(), cudaMemcpyHostToDevice, stream_));
+    int rc = run_steps(static_, stream_, false);
+    if (rc) return rc;
+    UQ_CUDA(cudaMemcpyAsync(out, static_.ptr[P_.h.output], output_bytes(), cudaMemcpyDeviceToHost, stream_));
+    const cudaError_t e = cudaStreamSynchronize(stream_);
+    if (e != cudaSuccess) {
+        set_error(std::string("inference: ") + cudaGetErrorString(e));
+        return 2001;
+    }
     return device_status();
 }
 

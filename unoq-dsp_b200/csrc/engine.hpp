@@ -19,6 +19,9 @@
 
 namespace uq {
 
+constexpr size_t kStaticArenaBytes = (size_t)16 << 20;  // fixed arena of run_static (runtime/graph.h:7)
+constexpr size_t kNoOffset = ~(size_t)0;
+
 struct BatchCtx;
 
 // One plan op lowered to device work. `run` enqueues its kernels on the stream and returns 0
@@ -57,6 +60,11 @@ class Engine {
 
     // Host buffers; `pinned` skips the staging copy. Synchronous.
     int run_host(const void *in, void *out, uint32_t images);
+    // One image through the fixed device arena g_static_arena (kStaticArenaBytes), with no device
+    // allocation: eager launches on the engine stream, host buffers, synchronous. The first call
+    // lays the plan out (host) and looks up the arena's address; calls that overlap on one device
+    // share the arena and must be serialised by the caller.
+    int run_static(const void *in, void *out);
     // Device buffers of the batch context (input tensor, output tensor of image 0).
     int buffers(uint32_t images, void **d_in, void **d_out);
     int launch(uint32_t images);   // async on stream_
@@ -86,6 +94,7 @@ class Engine {
     // run concurrently on three streams, two arena slots alternating.
     int run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint32_t chunks);
     int plan_arena(BatchCtx &b);
+    void layout(uint32_t images, std::vector<size_t> &offset, std::vector<uint32_t> &replicated, size_t &total) const;
     int capture(BatchCtx &b);
     int run_steps(const BatchCtx &b, cudaStream_t s, bool profile);
     void release();
@@ -110,6 +119,8 @@ class Engine {
     bool profiling_ = false;
     std::vector<uint64_t> ticks_;        // [0] runs, [1] total ns, [2+i] op ns
     std::unique_ptr<OutputGather> gather_;
+    BatchCtx static_;                    // one-image context over g_static_arena (not owned)
+    std::vector<uint32_t> static_replicated_;
     int gather(const BatchCtx &b);       // enqueue the output gather when multi-rank
     int finish(cudaEvent_t ev);          // wait for `ev`, bounded when a collective is pending
 };

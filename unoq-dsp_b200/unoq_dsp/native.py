@@ -36,6 +36,7 @@ _SIGNATURES = {
     "ug_host_free": (None, [C.c_void_p]),
     "ug_validate_plan": (C.c_int, [C.c_void_p, C.c_uint32]),
     "ug_batch_kernel_count": (C.c_int, [C.c_void_p, C.c_uint32]),
+    "ug_run_static": (C.c_int, [C.c_void_p, C.c_uint32, C.c_void_p, C.c_uint32]),
     "ug_upload_batch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32]),
     "ug_download_batch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32]),
     "ug_dist_unique_id": (C.c_int, [C.c_void_p, C.c_uint32]),
