@@ -52,18 +52,24 @@ namespace {
 constexpr int kBM = 128;              // pixels per tile = TMEM lanes
 constexpr int kBK = 128;              // reduction bytes per stage (one 128-byte swizzle row)
 constexpr int kStageBytes = kBM * kBK;
-constexpr int kProducerWarps = 8;
-constexpr int kEpilogueWarps = 8;     // two warps per TMEM lane quarter, alternating 16-column chunks
-constexpr int kMmaWarp = kProducerWarps + kEpilogueWarps;
-constexpr int kThreads = (kMmaWarp + 1) * 32;
-constexpr int kProducers = kProducerWarps * 32;
-// 16-byte-chunk producers: thread t builds chunk t % 8 of rows t / 8 + kRowStep * i, i < kRowIters.
-constexpr int kRowStep = kProducers / 8;
-constexpr int kRowIters = kBM / kRowStep;
-// word-assembly producers: thread t builds chunks t / kBM + kChunkStep * k of row t % kBM.
-constexpr int kChunkStep = kProducers / kBM;
-static_assert(kBM % kRowStep == 0 && kProducers % kBM == 0, "producer mapping");
+constexpr int kEpilogueWarps = 8;     // two warps per TMEM lane quarter, column halves
 constexpr int kEpilogues = kEpilogueWarps * 32;
+// Producer warps: 4 for pointwise convs (their copies are light; fewer warps leave each thread more
+// registers for the epilogue), 8 for band / gather convs (assembly-heavy). Roles by warp index:
+// producers [0, PW), epilogue [PW, PW + 8), MMA issuer PW + 8.
+template <int PW>
+struct Roles {
+    static constexpr int kProducerWarps = PW;
+    static constexpr int kMmaWarp = PW + kEpilogueWarps;
+    static constexpr int kThreads = (kMmaWarp + 1) * 32;
+    static constexpr int kProducers = PW * 32;
+    // 16-byte-chunk producers: thread t builds chunk t % 8 of rows t / 8 + kRowStep * i, i < kRowIters.
+    static constexpr int kRowStep = kProducers / 8;
+    static constexpr int kRowIters = kBM / kRowStep;
+    // word-assembly producers: thread t builds chunks t / kBM + kChunkStep * k of row t % kBM.
+    static constexpr int kChunkStep = kProducers / kBM;
+    static_assert(kBM % kRowStep == 0 && kProducers % kBM == 0, "producer mapping");
+};
 constexpr int kMaxSmem = 227 * 1024;
 constexpr int kWeightBudget = 96 * 1024;
 
@@ -362,8 +368,11 @@ __device__ __forceinline__ uint4 epilogue_chunk(const uint32_t (&r)[16], const E
     return make_uint4(packed[0], packed[1], packed[2], packed[3]);
 }
 
-template <int EPI>
-__global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_constant__ Params p) {
+template <int EPI, int PW>
+__global__ void __launch_bounds__(Roles<PW>::kThreads, 1) conv_tc_kernel(const __grid_constant__ Params p) {
+    constexpr int kProducerWarps = Roles<PW>::kProducerWarps, kMmaWarp = Roles<PW>::kMmaWarp;
+    constexpr int kProducers = Roles<PW>::kProducers, kRowStep = Roles<PW>::kRowStep;
+    constexpr int kRowIters = Roles<PW>::kRowIters, kChunkStep = Roles<PW>::kChunkStep;
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte aligned base, formed by pointer arithmetic on the __shared__ array so that every
     // pointer derived from it stays in the shared address space (ld.shared, not generic loads).
@@ -841,6 +850,7 @@ struct ConvTc {
     Params p{};
     int n_tiles = 1;
     size_t smem = 0;
+    int producer_warps = 8;
 };
 
 // Band geometry of a layer. Each band row holds one input row (iw*ic bytes, a multiple of 16 so
@@ -1019,12 +1029,11 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
     }
     static bool attr_set = false;
     if (!attr_set) {
-        if (cudaFuncSetAttribute(conv_tc_kernel<kRelu>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
-                cudaSuccess ||
-            cudaFuncSetAttribute(conv_tc_kernel<kTies>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
-                cudaSuccess ||
-            cudaFuncSetAttribute(conv_tc_kernel<kGeneral>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
-                cudaSuccess)
+        auto allow = [](auto fn) {
+            return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) == cudaSuccess;
+        };
+        if (!allow(conv_tc_kernel<kRelu, 4>) || !allow(conv_tc_kernel<kTies, 4>) || !allow(conv_tc_kernel<kGeneral, 4>) ||
+            !allow(conv_tc_kernel<kRelu, 8>) || !allow(conv_tc_kernel<kTies, 8>) || !allow(conv_tc_kernel<kGeneral, 8>))
             return 2001;
         attr_set = true;
     }
@@ -1063,6 +1072,7 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
     p.tab_bytes = tab_bytes;
     p.epi_mode = epi_mode;
     c->n_tiles = n_tiles;
+    c->producer_warps = mode == kPointwise ? 4 : 8;
     c->smem = layout().total;
     *out = c;
     return 0;
@@ -1112,9 +1122,17 @@ int conv_tc_launch(const ConvTc &c, const int8_t *x, int8_t *y, const ConvGeom &
     if (per_tile < 1) per_tile = 1;
     if (per_tile > m_tiles) per_tile = m_tiles;
     dim3 grid(per_tile, c.n_tiles);
-    if (p.epi_mode == kRelu) conv_tc_kernel<kRelu><<<grid, kThreads, c.smem, s>>>(p);
-    else if (p.epi_mode == kTies) conv_tc_kernel<kTies><<<grid, kThreads, c.smem, s>>>(p);
-    else conv_tc_kernel<kGeneral><<<grid, kThreads, c.smem, s>>>(p);
+    if (c.producer_warps == 4) {
+        constexpr int T = Roles<4>::kThreads;
+        if (p.epi_mode == kRelu) conv_tc_kernel<kRelu, 4><<<grid, T, c.smem, s>>>(p);
+        else if (p.epi_mode == kTies) conv_tc_kernel<kTies, 4><<<grid, T, c.smem, s>>>(p);
+        else conv_tc_kernel<kGeneral, 4><<<grid, T, c.smem, s>>>(p);
+    } else {
+        constexpr int T = Roles<8>::kThreads;
+        if (p.epi_mode == kRelu) conv_tc_kernel<kRelu, 8><<<grid, T, c.smem, s>>>(p);
+        else if (p.epi_mode == kTies) conv_tc_kernel<kTies, 8><<<grid, T, c.smem, s>>>(p);
+        else conv_tc_kernel<kGeneral, 8><<<grid, T, c.smem, s>>>(p);
+    }
     return 0;
 }
 
