@@ -633,10 +633,13 @@ int Engine::batch(uint32_t images, BatchCtx **out, uint32_t slot) {
 
 int Engine::run_host(const void *in, void *out, uint32_t images) {
     if (!ready_ || !in || !out) return 22;
-    // Large batches overlap their copies with compute (4 pieces from 2048 images, 2 from 512).
-    if (!profiling_ && images >= 512)
-        return run_pipelined(static_cast<const uint8_t *>(in), static_cast<uint8_t *>(out), images,
-                             images >= 2048 ? 4 : 2);
+    // Large batches overlap their copies with compute, in pieces of about 512 images (2 to 16):
+    // small enough that the first copy and the last read-back are short, large enough that the
+    // graph runs as efficiently as on the whole batch.
+    if (!profiling_ && images >= 512) {
+        const uint32_t pieces = std::min<uint32_t>(16, std::max<uint32_t>(2, (images + 256) / 512));
+        return run_pipelined(static_cast<const uint8_t *>(in), static_cast<uint8_t *>(out), images, pieces);
+    }
     BatchCtx *B = nullptr;
     int rc = batch(images, &B);
     if (rc) return rc;

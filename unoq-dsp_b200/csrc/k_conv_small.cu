@@ -58,9 +58,8 @@ __device__ __forceinline__ int32_t requant(int32_t acc, const EpiChan &e, int lo
     return v < lo ? lo : (v > hi ? hi : v);
 }
 
-template <int IC4, int S, int EPI>
+template <int IC4, int OCT, int S, int EPI>
 __global__ void __launch_bounds__(kThreads) conv_small_kernel(const SmallParams p) {
-    constexpr int OCT = 8 / IC4;
     extern __shared__ __align__(16) uint8_t smem[];
     uint8_t *sLut = smem;                                              // 256 bytes
     EpiChan *sEpi = reinterpret_cast<EpiChan *>(smem + 256);           // [oc]
@@ -197,18 +196,18 @@ __global__ void __launch_bounds__(kThreads) conv_small_kernel(const SmallParams 
     }
 }
 
-template <int IC4, int S>
+template <int IC4, int OCT, int S>
 void launch_s(const SmallParams &p, int epi, dim3 grid, size_t smem, cudaStream_t s) {
-    if (epi == 0) conv_small_kernel<IC4, S, 0><<<grid, kThreads, smem, s>>>(p);
-    else if (epi == 1) conv_small_kernel<IC4, S, 1><<<grid, kThreads, smem, s>>>(p);
-    else conv_small_kernel<IC4, S, 2><<<grid, kThreads, smem, s>>>(p);
+    if (epi == 0) conv_small_kernel<IC4, OCT, S, 0><<<grid, kThreads, smem, s>>>(p);
+    else if (epi == 1) conv_small_kernel<IC4, OCT, S, 1><<<grid, kThreads, smem, s>>>(p);
+    else conv_small_kernel<IC4, OCT, S, 2><<<grid, kThreads, smem, s>>>(p);
 }
 
 }  // namespace
 
 struct ConvSmall {
     SmallParams p{};
-    int ic4 = 1, s = 1, epi = 0;
+    int ic4 = 1, oct = 8, s = 1, epi = 0;
     size_t smem = 0;
 };
 
@@ -220,7 +219,9 @@ int conv_small_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *
     if (g.kh != 3 || g.kw != 3 || g.dh != 1 || g.dw != 1 || g.sh != g.sw || (g.sh != 1 && g.sh != 2)) return 0;
     const int ic4 = g.ic <= 4 ? 1 : g.ic <= 8 ? 2 : g.ic <= 16 ? 4 : 0;
     if (!ic4) return 0;
-    const int oct = 8 / ic4, oc = g.oc;
+    // output channels per thread: 8 / ic4 (72 weight words in registers); 4 for 1-word pixels when
+    // the layer has at most 16 output channels (more threads per tile, measured faster there)
+    const int oct = (ic4 == 1 && g.oc <= 16) ? 4 : 8 / ic4, oc = g.oc;
     if (oc % oct != 0) return 0;
     const int groups = oc / oct;
     if (groups > 32 || (groups & (groups - 1)) != 0) return 0;   // power of two, divides the block
@@ -260,7 +261,7 @@ int conv_small_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *
     p.br = (p.th - 1) * g.sh + 3;
     p.bc = (p.tw - 1) * g.sw + 3;
     p.groups = groups;
-    c->ic4 = ic4, c->s = g.sh, c->epi = epi_mode;
+    c->ic4 = ic4, c->oct = oct, c->s = g.sh, c->epi = epi_mode;
     c->smem = 256 + (size_t)oc * sizeof(EpiChan) + (size_t)p.br * p.bc * ic4 * 4;
     void *dw = alloc(wt.size() * 4), *de = alloc(epi.size() * sizeof(EpiChan));
     if (!dw || !de || cudaMemcpy(dw, wt.data(), wt.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
@@ -283,9 +284,14 @@ int conv_small_launch(const ConvSmall &c, const int8_t *x, int8_t *y, const Conv
     p.y = y;
     p.n = g.n;
     const dim3 grid((unsigned)((size_t)p.n * p.tiles_y * p.tiles_x));
-    if (c.ic4 == 1) c.s == 1 ? launch_s<1, 1>(p, c.epi, grid, c.smem, s) : launch_s<1, 2>(p, c.epi, grid, c.smem, s);
-    else if (c.ic4 == 2) c.s == 1 ? launch_s<2, 1>(p, c.epi, grid, c.smem, s) : launch_s<2, 2>(p, c.epi, grid, c.smem, s);
-    else c.s == 1 ? launch_s<4, 1>(p, c.epi, grid, c.smem, s) : launch_s<4, 2>(p, c.epi, grid, c.smem, s);
+    if (c.ic4 == 1 && c.oct == 4)
+        c.s == 1 ? launch_s<1, 4, 1>(p, c.epi, grid, c.smem, s) : launch_s<1, 4, 2>(p, c.epi, grid, c.smem, s);
+    else if (c.ic4 == 1)
+        c.s == 1 ? launch_s<1, 8, 1>(p, c.epi, grid, c.smem, s) : launch_s<1, 8, 2>(p, c.epi, grid, c.smem, s);
+    else if (c.ic4 == 2)
+        c.s == 1 ? launch_s<2, 4, 1>(p, c.epi, grid, c.smem, s) : launch_s<2, 4, 2>(p, c.epi, grid, c.smem, s);
+    else
+        c.s == 1 ? launch_s<4, 2, 1>(p, c.epi, grid, c.smem, s) : launch_s<4, 2, 2>(p, c.epi, grid, c.smem, s);
     return 0;
 }
 
