@@ -240,8 +240,9 @@ def softmax_table_case(rng, rows, width, scale=0.05):
     return pw.build(x, z), _rand_input(rng, (1, rows, width))
 
 
-def block_case(rng, hw=14, c=32, expand=96):
-    """Inverted-residual block: pw expand -> dw 3x3 -> pw project -> residual add."""
+def block_case(rng, hw=14, c=32, expand=96, conv_second=False):
+    """Inverted-residual block: pw expand -> dw 3x3 -> pw project -> residual add (the projection
+    is the add's first operand, or its second with conv_second)."""
     x_shape = (1, hw, hw, c)
     pw = PlanWriter()
     x = pw.tensor(x_shape)
@@ -255,7 +256,7 @@ def block_case(rng, hw=14, c=32, expand=96):
     q = synth.add_parameters(0.06, 2, 0.05, -3, 0.07, 0, -128, 127)
     qi = pw.tensor((520,), "i4", q)
     z = pw.tensor(x_shape)
-    pw.op(18, p, x, z, (qi, 0, 0, 0))
+    pw.op(18, x if conv_second else p, p if conv_second else x, z, (qi, 0, 0, 0))
     return pw.build(x, z, version=2), _rand_input(rng, x_shape)
 
 
@@ -312,4 +313,5 @@ def all_cases(scale=1):
         ("softmax_exact", lambda r: softmax_exact_case(r, 10 * s, 100)),
         ("softmax_table", lambda r: softmax_table_case(r, 6 * s, 33)),
         ("block", lambda r: block_case(r, hw=7 * s)),
+        ("block_conv_second", lambda r: block_case(r, hw=5 * s, c=48, expand=64, conv_second=True)),
     ]

@@ -99,3 +99,19 @@ def test_object_detector_matches_reference_pipeline():
         batch = det.detect_batch(dc.pipeline_images(320), score_threshold=0.0, max_results=30)
     assert got == gold["detect"]
     assert [flat(b) for b in batch] == gold["detect"]
+
+
+def test_models_identical_with_and_without_add_fusion(native, golden_models, monkeypatch):
+    """Both bundled models with residual adds fused into conv epilogues and with separate adds."""
+    from unoq_dsp import load
+    for name, shape in MODELS:
+        plan = load(model_path(name)).plan
+        x = seeded(shape, 0)
+        with NativeSession(native, plan) as s:
+            fused = s.run(x)
+        monkeypatch.setenv("UNOQ_FUSE_ADD", "0")
+        with NativeSession(native, plan) as s:
+            separate = s.run(x)
+        monkeypatch.delenv("UNOQ_FUSE_ADD")
+        np.testing.assert_array_equal(fused, golden_models[f"{name}/y0"])
+        np.testing.assert_array_equal(separate, golden_models[f"{name}/y0"])

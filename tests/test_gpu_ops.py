@@ -81,3 +81,20 @@ def test_snapshot_and_profile(native, golden_ops):
     inp = np.empty(x.size, dtype=np.int8)
     assert native.ug_snapshot(0, inp.ctypes.data, inp.nbytes) == 0
     np.testing.assert_array_equal(inp, x)
+
+
+@pytest.mark.parametrize("name", ["block", "block_conv_second"])
+def test_fused_residual_add_matches_unfused(name, native, oracle, monkeypatch):
+    """A residual add computed in the projection conv's epilogue gives the bytes of the separate
+    add kernel (UNOQ_FUSE_ADD=0) and of the oracle, at batch 1 and in a batch."""
+    rng = np.random.default_rng(17)
+    plan, x0 = dict(opcases.all_cases(2))[name](rng)
+    xs = np.stack([x0] + [rng.integers(-128, 128, size=x0.shape, dtype=np.int64).astype(np.int8) for _ in range(5)])
+    expect = oracle.run(plan, xs, 6)
+    with NativeSession(native, plan) as s:
+        fused = s.run(xs, 6)
+    monkeypatch.setenv("UNOQ_FUSE_ADD", "0")
+    with NativeSession(native, plan) as s:
+        separate = s.run(xs, 6)
+    np.testing.assert_array_equal(fused, expect)
+    np.testing.assert_array_equal(separate, expect)

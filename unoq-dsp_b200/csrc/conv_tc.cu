@@ -111,6 +111,13 @@ struct Params {
     int store_tma;             // 1: staged tile leaves by TMA tensor store; 0: cooperative stores
     int box;                   // TMA store box: columns of one epilogue warp (max(16, bn / 2)) x 32 rows
     int out_bytes;             // output staging: per-warp double buffers (TMA) or two whole tiles
+    // Fused residual add (plan code 18 consuming this conv's output; 0 / null when not fused):
+    // y = clamp(scale(T_conv[v + 128] + T_res[r + 128]) + zp) with the add's two 256-entry tables.
+    const int8_t *res;         // residual tensor [M][oc] (the add's other operand)
+    const int32_t *add_tab;    // the add's q block on the device: tables at +8 (input a), +264 (input b)
+    int res_side;              // 0: this conv is the add's input a (table at +8), 1: input b
+    EpiChan add_epi;           // the add's scale as requant.cuh constants (bias 0)
+    int add_lo, add_hi;
     int swz;                   // staging swizzle: 0 none (16 B rows), 1 = 32 B, 2 = 64 B, 3 = 128 B span
 };
 
@@ -122,7 +129,7 @@ __host__ __device__ inline size_t warp_stage_bytes(int box) { return ((size_t)32
 
 // Shared-memory carve-up, identical on host (sizing) and device.
 struct Layout {
-    size_t a, b, out, band, epi, lut, tab, bars, total;
+    size_t a, b, out, band, epi, lut, addt, tab, bars, total;
     __host__ __device__ Layout(int stages, int kc, int bn, int band_bytes, int nbands, int fill_bytes, int tab_bytes,
                                int out_bytes) {
         size_t o = 0;
@@ -138,6 +145,8 @@ struct Layout {
         o = epi + (size_t)bn * sizeof(EpiChan);
         lut = o;
         o += 256;
+        addt = (o + 15) & ~(size_t)15;  // fused-add tables: conv side, residual side (256 int32 each)
+        o = addt + 2048;
         tab = (o + 15) & ~(size_t)15;
         o = tab + (size_t)tab_bytes;
         bars = (o + 7) & ~(size_t)7;
@@ -318,7 +327,9 @@ __device__ __forceinline__ uint32_t pack_sat_s8x4(int32_t v0, int32_t v1, int32_
 // int8 (the clamp is two integer min/max per value; byte-SIMD min/max would be emulated).
 template <int EPI>
 __device__ __forceinline__ uint4 epilogue_chunk(const uint32_t (&r)[16], const EpiSoA &E, const uint8_t *lut, int c0,
-                                                int lo, int hi) {
+                                                int lo, int hi, const Params *fp = nullptr, const int32_t *tabs = nullptr,
+                                                uint4 res = make_uint4(0, 0, 0, 0)) {
+    const uint32_t resw[4] = {res.x, res.y, res.z, res.w};
     uint32_t packed[4];
     const longlong2 *K2 = reinterpret_cast<const longlong2 *>(E.k + c0);
     const int4 *M4 = reinterpret_cast<const int4 *>(E.m + c0);
@@ -358,15 +369,23 @@ __device__ __forceinline__ uint4 epilogue_chunk(const uint32_t (&r)[16], const E
             }
         }
 #pragma unroll
-        for (int i = 0; i < 4; i++) v[i] = min(max(v[i], lo), hi);
-        uint32_t w = pack_sat_s8x4(v[0], v[1], v[2], v[3]);
-        if (lut)
-            w = (uint32_t)lut[(w & 0xFF) ^ 0x80] | (uint32_t)lut[((w >> 8) & 0xFF) ^ 0x80] << 8 |
-                (uint32_t)lut[((w >> 16) & 0xFF) ^ 0x80] << 16 | (uint32_t)lut[(w >> 24) ^ 0x80] << 24;
-        packed[g] = w;
+        for (int i = 0; i < 4; i++) {
+            v[i] = min(max(v[i], lo), hi);
+            if (lut) v[i] = (int8_t)lut[v[i] + 128];
+            if (fp) {  // fused residual add: the add's two tables, then its scale and clamp
+                const int rv = (int)(int8_t)(resw[g] >> (8 * i));
+                const int32_t sum = (int32_t)((uint32_t)tabs[v[i] + 128] + (uint32_t)tabs[256 + rv + 128]);
+                v[i] = epilogue_one(sum, fp->add_epi, fp->add_lo, fp->add_hi);
+            }
+        }
+        packed[g] = pack_sat_s8x4(v[0], v[1], v[2], v[3]);
     }
     return make_uint4(packed[0], packed[1], packed[2], packed[3]);
 }
+
+// A fused residual add (qnn.c:175-183) runs inside epilogue_chunk on the requantised int32 values:
+// y = clamp(scale(T_conv[v + 128] + T_res[r + 128]) + zp) with the add's scale as requant.cuh
+// constants; rows past M (the last tile) read no residual and are never stored.
 
 template <int EPI, int PW>
 __global__ void __launch_bounds__(Roles<PW>::kThreads, 1) conv_tc_kernel(const __grid_constant__ Params p) {
@@ -388,6 +407,7 @@ __global__ void __launch_bounds__(Roles<PW>::kThreads, 1) conv_tc_kernel(const _
     int *sI = reinterpret_cast<int *>(sK + p.bn);
     const EpiSoA E{sK, sI, sI + p.bn, sI + 2 * p.bn, sI + 3 * p.bn, sI + 4 * p.bn, sI + 5 * p.bn};
     uint8_t *sLut = smem + L.lut;
+    int32_t *sAdd = reinterpret_cast<int32_t *>(smem + L.addt);  // [0,256) conv side, [256,512) residual
     int *sTab = reinterpret_cast<int *>(smem + L.tab);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
     uint64_t *full = bars, *empty = bars + S;
@@ -435,6 +455,11 @@ __global__ void __launch_bounds__(Roles<PW>::kThreads, 1) conv_tc_kernel(const _
     }
     if (p.post)
         for (int i = threadIdx.x; i < 256; i += blockDim.x) sLut[i] = p.post[i];
+    if (p.res)
+        for (int i = threadIdx.x; i < 512; i += blockDim.x) {
+            const int side = (i >> 8) ^ p.res_side;  // conv side first
+            sAdd[i] = p.add_tab[8 + 256 * side + (i & 255)];
+        }
     if (p.mode == kBand)
         for (int i = threadIdx.x; i < (p.tab_bytes >> 2); i += blockDim.x) sTab[i] = p.tab[i];
     if (warp == kMmaWarp) {  // the MMA warp owns the TMEM allocation
@@ -766,7 +791,16 @@ __global__ void __launch_bounds__(Roles<PW>::kThreads, 1) conv_tc_kernel(const _
                 for (int ci = 0; ci < my_chunks; ci++) {
                     const bool more = ci + 1 < my_chunks;
                     if (more) tmem_ld16_nowait(taddr + (ci + 1) * 16, rb);
-                    const uint4 v = epilogue_chunk<EPI>(ra, E, lut, c0 + ci * 16, p.lo, p.hi);
+                    uint4 v;
+                    if (p.res) {
+                        const int row = mt * kBM + quarter * 32 + lane;
+                        uint4 rr = make_uint4(0, 0, 0, 0);  // rows past M read no residual (never stored)
+                        if (row < p.M)
+                            rr = __ldg(reinterpret_cast<const uint4 *>(p.res + (size_t)row * p.oc + n0 + c0 + ci * 16));
+                        v = epilogue_chunk<EPI>(ra, E, lut, c0 + ci * 16, p.lo, p.hi, &p, sAdd, rr);
+                    } else {
+                        v = epilogue_chunk<EPI>(ra, E, lut, c0 + ci * 16, p.lo, p.hi);
+                    }
                     st_shared16(smem_u32(stage + (size_t)lane * p.box + ((ci ^ swz_row) << 4)), v);
                     if (more) tmem_wait_ld(rb);
 #pragma unroll
@@ -851,6 +885,7 @@ struct ConvTc {
     int n_tiles = 1;
     size_t smem = 0;
     int producer_warps = 8;
+    bool fused = false;  // a residual add is fused into the epilogue
 };
 
 // Band geometry of a layer. Each band row holds one input row (iw*ic bytes, a multiple of 16 so
@@ -893,8 +928,9 @@ static bool band_geometry(const ConvGeom &g, BandGeom &bg) {
 }
 
 int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *post_dev, const ConvGeom &g,
-                    const std::function<void *(size_t)> &alloc, ConvTc **out) {
+                    const std::function<void *(size_t)> &alloc, ConvTc **out, const FusedAdd *add) {
     *out = nullptr;
+    if (add && (g.oc % 16 != 0)) return 0;  // fused add needs whole 16-byte column chunks (TMA store)
     const char *env = std::getenv("UNOQ_CONV_TC");
     if (env && env[0] == '0') return 0;
     const int K = g.kh * g.kw * g.ic;
@@ -1057,6 +1093,14 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
     p.n_acc = bn <= 128 ? 4 : 2;
     p.tmem_cols = std::max(32, p.n_acc * bn);
     p.store_tma = store_tma;
+    if (add) {
+        p.add_tab = add->q_dev;
+        p.res_side = add->conv_is_b ? 1 : 0;
+        p.add_epi = make_epilogue(0, add->q_host[0], add->q_host[1], add->q_host[2]);
+        p.add_lo = add->q_host[3];
+        p.add_hi = add->q_host[4];
+        c->fused = true;
+    }
     p.box = box;
     p.out_bytes = out_bytes;
     p.swz = p.box == 128 ? 3 : p.box == 64 ? 2 : p.box == 32 ? 1 : 0;
@@ -1094,10 +1138,13 @@ static EncodeTiled encoder() {
     return fn;
 }
 
-int conv_tc_launch(const ConvTc &c, const int8_t *x, int8_t *y, const ConvGeom &g, cudaStream_t s) {
+int conv_tc_launch(const ConvTc &c, const int8_t *x, int8_t *y, const ConvGeom &g, cudaStream_t s,
+                   const int8_t *res) {
     Params p = c.p;
     p.x = x;
     p.y = y;
+    p.res = c.fused ? res : nullptr;
+    if (c.fused && !res) return 2001;
     if ((long long)g.n * g.oh * g.ow >= (1ll << 31)) return 2001;  // pixel indices are 31-bit
     p.M = g.n * g.oh * g.ow;
     if (p.store_tma) {

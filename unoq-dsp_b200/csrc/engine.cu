@@ -127,6 +127,10 @@ int Engine::prepare() {
     alias_.resize(nt);
     std::iota(alias_.begin(), alias_.end(), 0);
     steps_.clear();
+    birth_ = P.birth;
+    fused_.assign(P.h.no, 0);
+    const char *fuse_env = std::getenv("UNOQ_FUSE_ADD");
+    fuse_adds_ = !(fuse_env && fuse_env[0] == '0');
     for (uint32_t i = 0; i < P.h.no; i++) {
         const Op o = P.ops[i];
         const Tensor a = P.ts[o.a], b = P.ts[o.b], z = P.ts[o.out];
@@ -166,7 +170,36 @@ int Engine::prepare() {
                     };
                     break;
                 }
+                // Residual add fused into the epilogue when the next op is an add whose one input is
+                // this conv's output and nothing else reads that output.
                 ConvTc *tc = nullptr;
+                if (i + 1 < P.h.no && P.ops[i + 1].code == 18 && o.out != P.h.output && P.death[o.out] == (int)i + 1 &&
+                    fuse_adds_) {
+                    const Op &n = P.ops[i + 1];
+                    const bool is_a = n.a == o.out, is_b = n.b == o.out;
+                    const uint32_t res = is_a ? n.b : n.a;
+                    if (is_a != is_b && P.ts[res].bytes == z.bytes && P.ts[n.out].bytes == z.bytes &&
+                        P.ts[res].type == z.type && P.ts[n.out].type == z.type) {
+                        const FusedAdd fa{P.q(n.p[0]), reinterpret_cast<const int32_t *>(dconst(n.p[0])), is_b};
+                        rc = conv_tc_prepare(P.s8(o.b), q, r.post, g, [this](size_t n2) { return prep_alloc(n2); }, &tc,
+                                             &fa);
+                        if (rc) return rc;
+                        if (tc) {
+                            std::shared_ptr<ConvTc> keep(tc, conv_tc_free);
+                            const uint32_t tout = n.out, tres = res;
+                            st.run = [keep, g, ta, tout, tres](const BatchCtx &B, cudaStream_t s) -> int {
+                                ConvGeom gb = g;
+                                gb.n = g.n * (int)B.images;
+                                return conv_tc_launch(*keep, reinterpret_cast<const int8_t *>(B.ptr[ta]),
+                                                      reinterpret_cast<int8_t *>(B.ptr[tout]), gb, s,
+                                                      reinterpret_cast<const int8_t *>(B.ptr[tres]));
+                            };
+                            fused_.at(i + 1) = 1;
+                            birth_[n.out] = (int)i;  // written during this op now
+                            break;
+                        }
+                    }
+                }
                 rc = conv_tc_prepare(P.s8(o.b), q, r.post, g, [this](size_t n) { return prep_alloc(n); }, &tc);
                 if (rc) return rc;
                 const int8_t *w = reinterpret_cast<const int8_t *>(dconst(o.b));
@@ -392,6 +425,10 @@ int Engine::prepare() {
                 break;
             }
             case 18: {
+                if (fused_[i]) {  // computed in the previous conv's epilogue
+                    st.run = nullptr;
+                    break;
+                }
                 const int32_t *dq = reinterpret_cast<const int32_t *>(dconst(o.p[0]));
                 const uint32_t ta = o.a, tb = o.b, tz = o.out, zb = z.bytes;
                 st.run = [=](const BatchCtx &B, cudaStream_t s) -> int {
@@ -497,12 +534,12 @@ void Engine::layout(uint32_t images, std::vector<size_t> &offset, std::vector<ui
         if (is_const && !replicate[r]) continue;
         if (gid[r] < 0) {
             gid[r] = (int)groups.size();
-            groups.push_back({r, align_up((size_t)P.ts[r].bytes * images, kAlign), is_const ? -1 : P.birth[r],
+            groups.push_back({r, align_up((size_t)P.ts[r].bytes * images, kAlign), is_const ? -1 : birth_[r],
                               is_const ? (int)P.h.no : P.death[r], 0});
         }
         Group &g = groups[gid[r]];
         if (!is_const) {
-            g.birth = std::min(g.birth, P.birth[t]);
+            g.birth = std::min(g.birth, birth_[t]);
             g.death = std::max(g.death, P.death[t]);
         }
         gid[t] = gid[r];

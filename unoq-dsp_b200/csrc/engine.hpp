@@ -110,6 +110,9 @@ class Engine {
     std::vector<void *> prep_;
     std::vector<Step> steps_;
     std::vector<int> alias_;             // tensor -> storage root (copy ops alias their source)
+    std::vector<int> birth_;             // tensor birth op, moved earlier for fused outputs
+    std::vector<char> fused_;            // op computed inside the previous op's kernel
+    bool fuse_adds_ = true;              // UNOQ_FUSE_ADD=0 keeps every add separate
     std::map<uint64_t, std::unique_ptr<BatchCtx>> batches_;  // key: slot << 32 | images
     cudaStream_t h2d_ = nullptr, d2h_ = nullptr;             // copy streams of the pipeline
     cudaEvent_t pipe_ev_[3][2] = {};                         // per slot: input landed, computed, output read
