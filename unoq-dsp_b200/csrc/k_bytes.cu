@@ -12,8 +12,8 @@
 //    axes goes through a shared-memory tile; any other permutation uses the element-wise path;
 //  * resize: one output pixel's channels per run, from the prepared row / column offsets;
 //  * max pool: 16 channels per thread with __vmaxs4.
-// bmm computes a 32 x 32 output tile per block from shared-memory tiles with the zero points
-// already subtracted.
+// bmm keeps a whole batch matrix's operands (zero points subtracted) in shared memory and gives
+// each thread a 4 x 4 register tile; large matrices use a 32 x 32 tiled path.
 #include <algorithm>
 
 #include "kernels.cuh"
@@ -239,9 +239,71 @@ __global__ void maxpool16_kernel(const int8_t *__restrict__ x, int8_t *__restric
 
 // ---------------------------------------------------------------- bmm (code 27) --------------
 // qnn.c:119-153 computes sum (x + 128) w - (xz + 128) sum w - wz sum (x + 128) + k (xz + 128) wz
-// in wrapping int32, which is sum (x - xz)(w - wz). Block = 32 x 32 outputs of one batch; the
-// operands pass through shared memory 32 reduction steps at a time with the zero points
-// subtracted; each thread accumulates 4 outputs (rows ty + 8 i, column tx).
+// in wrapping int32, which is sum (x - xz)(w - wz). Block = one batch matrix, up to 64 output rows
+// at a time: both operands, zero points subtracted, sit in shared memory as int16 (X rows x K,
+// W K x N, both stored K-major per output index), and each thread accumulates a 4 x 4 register
+// tile of outputs. Matrices too large for the shared-memory budget use the 32 x 32 tiled path.
+constexpr int kBmmRows = 64;       // output rows per block pass
+constexpr int kBmmSmem = 48 * 1024;
+
+__global__ void bmm_small_kernel(const int8_t *__restrict__ x, const int8_t *__restrict__ w, int8_t *__restrict__ y,
+                                 uint32_t batches, int m, int n, int k, int xz, int wz, int yz, int mult, int s,
+                                 int adj_x, int adj_y) {
+    extern __shared__ int16_t bsm[];
+    const int kpad = k | 1;                        // odd stride: rows fall in distinct banks
+    int16_t *ws = bsm;                             // [n][kpad]  (w[t][c] at ws[c * kpad + t])
+    int16_t *xs = bsm + (size_t)n * kpad;          // [kBmmRows][kpad]
+    const int tiles_r = (n + 3) / 4;               // 4-column groups
+    for (uint32_t job = blockIdx.x; job < batches * (uint32_t)((m + kBmmRows - 1) / kBmmRows); job += gridDim.x) {
+        const uint32_t bt = job / ((m + kBmmRows - 1) / kBmmRows);
+        const int r0 = (int)(job % ((m + kBmmRows - 1) / kBmmRows)) * kBmmRows;
+        const int rows = min(kBmmRows, m - r0);
+        const int8_t *xb = x + (size_t)bt * m * k, *wb = w + (size_t)bt * k * n;
+        for (int i = threadIdx.x; i < n * k; i += blockDim.x) {
+            const int c = i / k, t = i - c * k;
+            ws[c * kpad + t] = (int16_t)(wb[adj_y ? (size_t)c * k + t : (size_t)t * n + c] - wz);
+        }
+        for (int i = threadIdx.x; i < rows * k; i += blockDim.x) {
+            const int r = i / k, t = i - r * k;
+            xs[r * kpad + t] = (int16_t)(xb[adj_x ? (size_t)t * m + r0 + r : (size_t)(r0 + r) * k + t] - xz);
+        }
+        __syncthreads();
+        // thread -> 4 rows (rb * 4 ..) x 4 columns (cb * 4 ..)
+        const int groups = ((rows + 3) / 4) * tiles_r;
+        for (int gi = threadIdx.x; gi < groups; gi += blockDim.x) {
+            const int rb = gi / tiles_r, cb = gi - rb * tiles_r;
+            int acc[4][4] = {};
+            for (int t = 0; t < k; t++) {
+                int xv[4], wv[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int r = min(rb * 4 + i, rows - 1), c = min(cb * 4 + i, n - 1);
+                    xv[i] = xs[r * kpad + t];
+                    wv[i] = ws[c * kpad + t];
+                }
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+#pragma unroll
+                    for (int j = 0; j < 4; j++) acc[i][j] += xv[i] * wv[j];
+            }
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int r = rb * 4 + i;
+                if (r >= rows) break;
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int c = cb * 4 + j;
+                    if (c < n)
+                        y[((size_t)bt * m + r0 + r) * n + c] =
+                            (int8_t)dev_clamp(dev_scale(acc[i][j], mult, s) + yz, -128, 127);
+                }
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// 32 x 32 output tile per block, operands through shared memory 32 reduction steps at a time.
 __global__ void bmm_kernel(const int8_t *__restrict__ x, const int8_t *__restrict__ w, int8_t *__restrict__ y,
                            uint32_t batches, int m, int n, int k, int xz, int wz, int yz, int mult, int s, int adj_x,
                            int adj_y) {
@@ -256,7 +318,6 @@ __global__ void bmm_kernel(const int8_t *__restrict__ x, const int8_t *__restric
         int32_t acc[4] = {0, 0, 0, 0};
         for (int k0 = 0; k0 < k; k0 += 32) {
             for (int i = ty; i < 32; i += 8) {
-                // xs[row][kk] = x[bm*32 + row][k0 + kk] - xz ; ws[kk][col] = w[k0 + kk][bn*32 + col] - wz
                 const int r = bm * 32 + i, kk = k0 + tx;
                 xs[i][tx] = (r < m && kk < k) ? (int16_t)(xb[adj_x ? (uint64_t)kk * m + r : (uint64_t)r * k + kk] - xz) : 0;
                 const int kr = k0 + i, cc = bn * 32 + tx;
@@ -311,6 +372,13 @@ void launch_pool(const int8_t *x, int8_t *y, const ConvGeom &g, int is_max, int 
 
 void launch_bmm(const int8_t *x, const int8_t *w, int8_t *y, size_t batches, int m, int n, int k, const int32_t q7[7],
                 cudaStream_t s) {
+    const size_t smem = ((size_t)n + kBmmRows) * (size_t)(k | 1) * sizeof(int16_t);
+    if (smem <= (size_t)kBmmSmem) {
+        const uint64_t jobs = (uint64_t)batches * ((m + kBmmRows - 1) / kBmmRows);
+        bmm_small_kernel<<<grid_for(jobs, 1), kT, smem, s>>>(x, w, y, (uint32_t)batches, m, n, k, q7[0], q7[1], q7[2],
+                                                             q7[3], q7[4], q7[5], q7[6]);
+        return;
+    }
     const uint64_t tiles = (uint64_t)batches * ((m + 31) / 32) * ((n + 31) / 32);
     bmm_kernel<<<grid_for(tiles, 1), kT, 0, s>>>(x, w, y, (uint32_t)batches, m, n, k, q7[0], q7[1], q7[2], q7[3], q7[4],
                                                   q7[5], q7[6]);
