@@ -35,6 +35,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <numeric>
+#include <type_traits>
 #include <vector>
 
 #include <cuda.h>
@@ -52,15 +53,17 @@ namespace {
 constexpr int kBM = 128;              // pixels per tile = TMEM lanes
 constexpr int kBK = 128;              // reduction bytes per stage (one 128-byte swizzle row)
 constexpr int kStageBytes = kBM * kBK;
-constexpr int kEpilogueWarps = 8;     // two warps per TMEM lane quarter, column halves
-constexpr int kEpilogues = kEpilogueWarps * 32;
-// Producer warps: 4 for pointwise convs (their copies are light; fewer warps leave each thread more
-// registers for the epilogue), 8 for band / gather convs (assembly-heavy). Roles by warp index:
-// producers [0, PW), epilogue [PW, PW + 8), MMA issuer PW + 8.
-template <int PW>
+// Warp roles by index: producers [0, PW), epilogue [PW, PW + EW), MMA issuer PW + EW.
+// PW = 4 for pointwise convs (light copies; fewer warps leave more registers), 8 for band / gather
+// convs (assembly-heavy). EW = 8 or 16 epilogue warps: EW / 4 warps per TMEM lane quarter, each
+// taking a contiguous column part of the tile.
+template <int PW, int EW = 8>
 struct Roles {
     static constexpr int kProducerWarps = PW;
-    static constexpr int kMmaWarp = PW + kEpilogueWarps;
+    static constexpr int kEpilogueWarps = EW;
+    static constexpr int kEpilogues = EW * 32;
+    static constexpr int kParts = EW / 4;
+    static constexpr int kMmaWarp = PW + EW;
     static constexpr int kThreads = (kMmaWarp + 1) * 32;
     static constexpr int kProducers = PW * 32;
     // 16-byte-chunk producers: thread t builds chunk t % 8 of rows t / 8 + kRowStep * i, i < kRowIters.
@@ -387,11 +390,13 @@ __device__ __forceinline__ uint4 epilogue_chunk(const uint32_t (&r)[16], const E
 // y = clamp(scale(T_conv[v + 128] + T_res[r + 128]) + zp) with the add's scale as requant.cuh
 // constants; rows past M (the last tile) read no residual and are never stored.
 
-template <int EPI, int PW>
-__global__ void __launch_bounds__(Roles<PW>::kThreads, 1) conv_tc_kernel(const __grid_constant__ Params p) {
-    constexpr int kProducerWarps = Roles<PW>::kProducerWarps, kMmaWarp = Roles<PW>::kMmaWarp;
-    constexpr int kProducers = Roles<PW>::kProducers, kRowStep = Roles<PW>::kRowStep;
-    constexpr int kRowIters = Roles<PW>::kRowIters, kChunkStep = Roles<PW>::kChunkStep;
+template <int EPI, int PW, int EW>
+__global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(const __grid_constant__ Params p) {
+    using R = Roles<PW, EW>;
+    constexpr int kProducerWarps = R::kProducerWarps, kMmaWarp = R::kMmaWarp;
+    constexpr int kProducers = R::kProducers, kRowStep = R::kRowStep;
+    constexpr int kRowIters = R::kRowIters, kChunkStep = R::kChunkStep;
+    constexpr int kEpilogueWarps = R::kEpilogueWarps, kEpilogues = R::kEpilogues, kParts = R::kParts;
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte aligned base, formed by pointer arithmetic on the __shared__ array so that every
     // pointer derived from it stays in the shared address space (ld.shared, not generic loads).
@@ -756,7 +761,7 @@ __global__ void __launch_bounds__(Roles<PW>::kThreads, 1) conv_tc_kernel(const _
         const int e = warp - kProducerWarps;
         const int et = threadIdx.x - kProducers;  // 0..kEpilogues-1
         const int quarter = e & 3;                // TMEM lanes 32*quarter .. +31 (warp id % 4 rule)
-        const int half = e >> 2;                  // which 16-column chunks this warp takes
+        const int half = e >> 2;                  // which column part of the tile this warp takes
         const int row = quarter * 32 + lane;
         const uint8_t *lut = p.post ? sLut : nullptr;
         const int n0 = ntile * p.bn;
@@ -830,13 +835,13 @@ __global__ void __launch_bounds__(Roles<PW>::kThreads, 1) conv_tc_kernel(const _
                 uint8_t *stage = sOut + (size_t)(lt & 1) * out_stride(p.bn);
                 const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.bn);
                 uint32_t ra[16], rb[16];
-                int ci = half;
+                int ci = half;  // chunks half, half + kParts, ...
                 if (ci < live_chunks) {
                     tmem_ld16_nowait(taddr + ci * 16, ra);
                     tmem_wait_ld(ra);
                 }
                 while (ci < live_chunks) {
-                    const int next = ci + 2;
+                    const int next = ci + kParts;
                     if (next < live_chunks) tmem_ld16_nowait(taddr + next * 16, rb);
                     const uint4 v = epilogue_chunk<EPI>(ra, E, lut, ci * 16, p.lo, p.hi);
                     st_shared16(smem_u32(stage + (size_t)row * (p.bn + 16) + ci * 16), v);
@@ -885,6 +890,7 @@ struct ConvTc {
     int n_tiles = 1;
     size_t smem = 0;
     int producer_warps = 8;
+    int epilogue_warps = 8;
     bool fused = false;  // a residual add is fused into the epilogue
 };
 
@@ -954,8 +960,11 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
     const int tab_bytes = mode != kBand ? 16 : g.ic % 16 == 0 ? kc * 8 * 4 : (K32 / 4) * 32;
     int stages = 8, nbands = 0;
     const bool store_tma = (g.oc % 16) == 0;
-    const int box = std::max(16, bn / 2);
-    const int out_bytes = store_tma ? (int)(2 * kEpilogueWarps * warp_stage_bytes(box)) : (int)(2 * out_stride(bn));
+    // epilogue warps: 16 for pointwise convs (4 producer warps leave room; more warps hide the
+    // epilogue's latency), 8 for the other modes (8 producer warps)
+    const int ew = mode == kPointwise ? 16 : 8;
+    const int box = std::max(16, bn / (ew / 4));
+    const int out_bytes = store_tma ? (int)(2 * ew * warp_stage_bytes(box)) : (int)(2 * out_stride(bn));
     auto layout = [&]() {
         return Layout(stages, kc, bn, mode == kBand ? (int)bg.bytes() : 0, nbands, mode == kBand ? bg.fill_bytes : 0,
                       tab_bytes, out_bytes);
@@ -1068,8 +1077,11 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
         auto allow = [](auto fn) {
             return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) == cudaSuccess;
         };
-        if (!allow(conv_tc_kernel<kRelu, 4>) || !allow(conv_tc_kernel<kTies, 4>) || !allow(conv_tc_kernel<kGeneral, 4>) ||
-            !allow(conv_tc_kernel<kRelu, 8>) || !allow(conv_tc_kernel<kTies, 8>) || !allow(conv_tc_kernel<kGeneral, 8>))
+        if (!allow(conv_tc_kernel<kRelu, 4, 8>) || !allow(conv_tc_kernel<kTies, 4, 8>) ||
+            !allow(conv_tc_kernel<kGeneral, 4, 8>) || !allow(conv_tc_kernel<kRelu, 8, 8>) ||
+            !allow(conv_tc_kernel<kTies, 8, 8>) || !allow(conv_tc_kernel<kGeneral, 8, 8>) ||
+            !allow(conv_tc_kernel<kRelu, 4, 16>) || !allow(conv_tc_kernel<kTies, 4, 16>) ||
+            !allow(conv_tc_kernel<kGeneral, 4, 16>))
             return 2001;
         attr_set = true;
     }
@@ -1117,6 +1129,7 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
     p.epi_mode = epi_mode;
     c->n_tiles = n_tiles;
     c->producer_warps = mode == kPointwise ? 4 : 8;
+    c->epilogue_warps = ew;
     c->smem = layout().total;
     *out = c;
     return 0;
@@ -1169,17 +1182,16 @@ int conv_tc_launch(const ConvTc &c, const int8_t *x, int8_t *y, const ConvGeom &
     if (per_tile < 1) per_tile = 1;
     if (per_tile > m_tiles) per_tile = m_tiles;
     dim3 grid(per_tile, c.n_tiles);
-    if (c.producer_warps == 4) {
-        constexpr int T = Roles<4>::kThreads;
-        if (p.epi_mode == kRelu) conv_tc_kernel<kRelu, 4><<<grid, T, c.smem, s>>>(p);
-        else if (p.epi_mode == kTies) conv_tc_kernel<kTies, 4><<<grid, T, c.smem, s>>>(p);
-        else conv_tc_kernel<kGeneral, 4><<<grid, T, c.smem, s>>>(p);
-    } else {
-        constexpr int T = Roles<8>::kThreads;
-        if (p.epi_mode == kRelu) conv_tc_kernel<kRelu, 8><<<grid, T, c.smem, s>>>(p);
-        else if (p.epi_mode == kTies) conv_tc_kernel<kTies, 8><<<grid, T, c.smem, s>>>(p);
-        else conv_tc_kernel<kGeneral, 8><<<grid, T, c.smem, s>>>(p);
-    }
+    auto go = [&](auto pw, auto ew) {
+        constexpr int PWv = decltype(pw)::value, EWv = decltype(ew)::value;
+        constexpr int T = Roles<PWv, EWv>::kThreads;
+        if (p.epi_mode == kRelu) conv_tc_kernel<kRelu, PWv, EWv><<<grid, T, c.smem, s>>>(p);
+        else if (p.epi_mode == kTies) conv_tc_kernel<kTies, PWv, EWv><<<grid, T, c.smem, s>>>(p);
+        else conv_tc_kernel<kGeneral, PWv, EWv><<<grid, T, c.smem, s>>>(p);
+    };
+    if (c.producer_warps == 4 && c.epilogue_warps == 16) go(std::integral_constant<int, 4>{}, std::integral_constant<int, 16>{});
+    else if (c.producer_warps == 4) go(std::integral_constant<int, 4>{}, std::integral_constant<int, 8>{});
+    else go(std::integral_constant<int, 8>{}, std::integral_constant<int, 8>{});
     return 0;
 }
 
