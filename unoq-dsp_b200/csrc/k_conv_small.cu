@@ -80,8 +80,10 @@ __global__ void __launch_bounds__(kThreads) conv_small_kernel(const SmallParams 
         // RGB: image-aligned groups of 4 pixels are 3 aligned words; unpack to one word per pixel
         const int g0 = (ix0 >= 0 ? ix0 : ix0 - 3) / 4;  // floor(ix0 / 4)
         const int groups = (ix0 + p.bc - 1 - g0 * 4) / 4 + 1;
+        // unit = (band row, 4-pixel group), row fastest: the lanes' word stores then fall 1 band row
+        // apart (an odd word count when bc is odd) instead of 4 words apart
         for (int u = threadIdx.x; u < p.br * groups; u += kThreads) {
-            const int r = u / groups, gx = g0 + (u - r * groups);
+            const int gi = u / p.br, r = u - gi * p.br, gx = g0 + gi;
             const int iy = iy0 + r, x4 = gx * 4;
             uint32_t v[4] = {fillw, fillw, fillw, fillw};
             if (iy >= 0 && iy < p.ih) {
@@ -261,6 +263,7 @@ int conv_small_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *
     p.tiles_y = (g.oh + p.th - 1) / p.th;
     p.br = (p.th - 1) * g.sh + 3;
     p.bc = (p.tw - 1) * g.sw + 3;
+    if ((p.bc & 1) == 0) p.bc++;  // odd row length: a column of band words spans distinct banks
     p.groups = groups;
     c->ic4 = ic4, c->oct = oct, c->s = g.sh, c->epi = epi_mode;
     c->smem = 256 + (size_t)oc * sizeof(EpiChan) + (size_t)p.br * p.bc * ic4 * 4;
