@@ -10,6 +10,8 @@ Writes:
                  reference's output (ug_load + ug_run of libug_ref.so).
 * models.npz  -- for the two bundled models: the SHA-256 of the plan, seeded input images
                  (regenerated from the seed, not stored) and the reference's raw outputs.
+* configs.npz -- the §8 parity configurations (tests/configcases.py): SHA-256 of each plan and
+                 of the reference's output for input seeds 0 and 1 (tensors are regenerated).
 * codes.npz   -- for each malformed-plan variant of tests/plancorrupt.py (regenerated at test
                  time, identified by SHA-256), the reference loader's error code.
 
@@ -26,6 +28,7 @@ ROOT = Path(__file__).resolve().parents[2]
 sys.path[:0] = [str(ROOT), str(ROOT / "unoq-dsp_b200"), str(ROOT / "tests")]
 
 from oracle.oracle import Reference  # noqa: E402
+import configcases  # noqa: E402
 import opcases  # noqa: E402
 import plancorrupt  # noqa: E402
 
@@ -49,6 +52,16 @@ def main():
         arrays[f"{name}/x"] = np.ascontiguousarray(x).reshape(-1).view(np.int8)
         arrays[f"{name}/y"] = y
     np.savez_compressed(OUT / "ops.npz", **arrays)
+
+    carrays = {}
+    for name, _ in configcases.config_cases():
+        plan, xs, _ = configcases.build(name)
+        carrays[f"{name}/plan_sha256"] = np.frombuffer(hashlib.sha256(plan).digest(), dtype=np.uint8)
+        for seed in (0, 1):
+            y = ref.run(plan, configcases.image(xs, seed))
+            carrays[f"{name}/y{seed}_sha256"] = np.frombuffer(hashlib.sha256(y.tobytes()).digest(), dtype=np.uint8)
+    np.savez_compressed(OUT / "configs.npz", **carrays)
+
 
     from unoq_dsp.bundle import load
     marrays = {}
