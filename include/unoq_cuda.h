@@ -123,6 +123,62 @@ UG_API int ug_dist_init(void *session, int rank, int world, const void *id, uint
 /* Rank 0's device buffer holding the gathered outputs of `images` per rank (NULL on others). */
 UG_API int ug_gather_buffer(void *session, uint32_t images, void **root_device_output);
 
+/* ---- On-device preprocessing and decoding (extension). ------------------------------------
+ * The byte table of the image APIs (the reference's modern.py:10-18 profile_lookup and
+ * vision.py:20-29 image_lookup: input byte of channel c = table[pixel][c]) and the one-to-one
+ * YOLO decoder (modern.py:75-103: distance-to-grid boxes, sigmoid scores, two-stage top-k) run
+ * as kernels on the session stream. The host keeps the float-valued pieces that depend only on
+ * the model (the tables below, computed with the host decoder's own float32 expressions) and the
+ * per-image finish (score threshold, letterbox geometry). */
+
+/* Per-channel input table, `table[256 * channels]` with entry [pixel * channels + c]; NULL (or
+ * 0 channels) removes it. While set, every input handed to this session (ug_infer,
+ * ug_infer_batch, ug_upload_batch, ug_detect_batch) is uint8 pixels of the input shape, mapped
+ * through the table on the device before the network runs. channels: 1..16, dividing the input
+ * tensor's bytes. */
+UG_API int ug_set_input_table(void *session, const void *table, uint32_t channels);
+
+#define UG_YOLO_MAX_LEVELS 4
+typedef struct {
+    uint32_t box_offset;    /* byte offset of the level's (h, w, 4) int8 distances in one image's output */
+    uint32_t score_offset;  /* byte offset of the level's (h, w, classes) int8 logits */
+    uint32_t height, width; /* grid cells */
+    float stride;           /* input pixels per cell */
+    float distance[256];    /* [q + 128]: dequantised distance, (float(q) - zero_point) * scale in float32 */
+    float score[256];       /* [q + 128]: the host decoder's float32 sigmoid of the dequantised logit */
+    uint16_t rank[256];     /* [q + 128]: order code of score[] over all levels: equal scores share a code,
+                               a larger score has a larger code; codes < 1024 */
+} UgYoloLevel;
+
+typedef struct {
+    uint32_t levels;        /* 1..UG_YOLO_MAX_LEVELS, anchors numbered level-major, then row-major cells */
+    uint32_t classes;       /* 1..4096 */
+    uint32_t candidates;    /* anchors kept by the first stage (the reference keeps 300); 1..512 */
+    uint32_t reserved;      /* 0 */
+    UgYoloLevel level[UG_YOLO_MAX_LEVELS];
+} UgYoloDecode;
+
+/* One decoded (anchor, class) pair, in the reference's order: score descending, then first-stage
+ * position, then class. Records past the available pairs have anchor = 0xFFFFFFFF. */
+typedef struct {
+    uint32_t anchor;
+    uint32_t class_id;
+    float score;
+    float box[4];           /* x_min, y_min, x_max, y_max in input pixels: (grid -/+ distance) * stride */
+    uint32_t reserved;
+} UgDetectionRecord;
+
+/* Install (or, with NULL, remove) the YOLO decoder for this session's plan; the levels' tensors
+ * must lie inside the plan's output and the anchors number at most 32768. */
+UG_API int ug_set_yolo_decode(void *session, const UgYoloDecode *decode);
+/* `images` inputs (host) -> network -> decode; writes images x k records (host), k in 1..512.
+ * Same pipelining as ug_infer_batch; multi-rank sessions decode their own shard (no gather). */
+UG_API int ug_detect_batch(void *session, const void *input, uint32_t images, uint32_t k, UgDetectionRecord *records);
+/* Device-resident variant over the ug_upload_batch context: network + decode on the session
+ * stream (asynchronous); ug_detect_buffer gives the device records of (images, k). */
+UG_API int ug_launch_detect(void *session, uint32_t images, uint32_t k);
+UG_API int ug_detect_buffer(void *session, uint32_t images, uint32_t k, void **device_records);
+
 /* Last CUDA error string seen by the library (empty if none). */
 UG_API const char *ug_last_error(void);
 

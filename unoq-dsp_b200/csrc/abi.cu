@@ -245,6 +245,41 @@ int ug_profile_batch(void *session, uint32_t images, uint32_t iterations, uint64
     return s->engine.profile_batch(images, iterations, op_ns, count, total_ms);
 }
 
+int ug_set_input_table(void *session, const void *table, uint32_t channels) {
+    Session *s = static_cast<Session *>(session);
+    if (!s) return 1003;
+    const int rc = s->engine.set_input_table(table, channels);
+    return rc == 22 ? 1003 : rc;
+}
+
+int ug_set_yolo_decode(void *session, const UgYoloDecode *decode) {
+    Session *s = static_cast<Session *>(session);
+    if (!s) return 1003;
+    const int rc = s->engine.set_yolo_decode(decode);
+    return rc == 22 ? 1003 : rc;
+}
+
+int ug_detect_batch(void *session, const void *input, uint32_t images, uint32_t k, UgDetectionRecord *records) {
+    Session *s = static_cast<Session *>(session);
+    if (!s || !input || !images || !records) return 1003;
+    const int rc = s->engine.detect_host(input, images, k, records);
+    return rc == 22 ? 1003 : rc;
+}
+
+int ug_launch_detect(void *session, uint32_t images, uint32_t k) {
+    Session *s = static_cast<Session *>(session);
+    if (!s || !images) return 1003;
+    const int rc = s->engine.launch_detect(images, k);
+    return rc == 22 ? 1003 : rc;
+}
+
+int ug_detect_buffer(void *session, uint32_t images, uint32_t k, void **device_records) {
+    Session *s = static_cast<Session *>(session);
+    if (!s || !images) return 1003;
+    const int rc = s->engine.detect_buffer(images, k, device_records);
+    return rc == 22 ? 1003 : rc;
+}
+
 const char *ug_last_error(void) { return uq::last_error(); }
 
 }  // extern "C"

@@ -2,6 +2,7 @@
 #include "engine.hpp"
 
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <mutex>
 #include <numeric>
@@ -49,8 +50,16 @@ void Engine::release() {
         if (b.arena) cudaFree(b.arena);
         if (b.host_in) cudaFreeHost(b.host_in);
         if (b.host_out) cudaFreeHost(b.host_out);
+        if (b.pixels) cudaFree(b.pixels);
+        if (b.records) cudaFree(b.records);
     }
     batches_.clear();
+    if (d_table_) cudaFree(d_table_);
+    if (d_yolo_) cudaFree(d_yolo_);
+    d_table_ = nullptr;
+    d_yolo_ = nullptr;
+    table_channels_ = 0;
+    yolo_ = YoloShape();
     for (void *p : prep_) cudaFree(p);
     prep_.clear();
     if (d_const_) cudaFree(d_const_);
@@ -668,36 +677,47 @@ int Engine::batch(uint32_t images, BatchCtx **out, uint32_t slot) {
     return 0;
 }
 
-int Engine::run_host(const void *in, void *out, uint32_t images) {
+int Engine::run_host(const void *in, void *out, uint32_t images) { return run_batch_host(in, out, images, 0); }
+
+int Engine::run_batch_host(const void *in, void *out, uint32_t images, uint32_t k) {
     if (!ready_ || !in || !out) return 22;
+    if (k && !yolo_.levels) return 22;
     // Large batches overlap their copies with compute, in pieces of about 512 images (2 to 16):
     // small enough that the first copy and the last read-back are short, large enough that the
     // graph runs as efficiently as on the whole batch.
     if (!profiling_ && images >= 512) {
         const uint32_t pieces = std::min<uint32_t>(16, std::max<uint32_t>(2, (images + 256) / 512));
-        return run_pipelined(static_cast<const uint8_t *>(in), static_cast<uint8_t *>(out), images, pieces);
+        return run_pipelined(static_cast<const uint8_t *>(in), static_cast<uint8_t *>(out), images, pieces, k);
     }
     BatchCtx *B = nullptr;
     int rc = batch(images, &B);
+    if (!rc) rc = stage_buffers(*B, k != 0);
     if (rc) return rc;
     UQ_CUDA(cudaSetDevice(device_));
     const size_t ni = (size_t)input_bytes() * images, no = (size_t)output_bytes() * images;
     UQ_CUDA(cudaEventRecord(ev0_, stream_));
-    UQ_CUDA(cudaMemcpyAsync(B->ptr[P_.h.input], in, ni, cudaMemcpyHostToDevice, stream_));
+    UQ_CUDA(cudaMemcpyAsync(landing(*B), in, ni, cudaMemcpyHostToDevice, stream_));
+    if ((rc = stage_in(*B, stream_))) return rc;
     if (profiling_) rc = run_steps(*B, stream_, true);
     else if (cudaGraphLaunch(B->exec, stream_) != cudaSuccess) {
         set_error("graph launch failed");
         rc = 2001;
     }
     if (rc) return rc;
-    if ((rc = gather(*B))) return rc;
-    if (gather_ && gather_->active()) {
-        // rank 0 returns the whole gathered batch (rank-major); the other ranks return nothing
-        if (gather_->rank() == 0)
-            UQ_CUDA(cudaMemcpyAsync(out, gather_->root_buffer(no), no * (size_t)gather_->world(),
-                                    cudaMemcpyDeviceToHost, stream_));
+    if (k) {
+        if ((rc = stage_out(*B, k, stream_))) return rc;
+        UQ_CUDA(cudaMemcpyAsync(out, B->records, sizeof(UgDetectionRecord) * k * images, cudaMemcpyDeviceToHost,
+                                stream_));
     } else {
-        UQ_CUDA(cudaMemcpyAsync(out, B->ptr[P_.h.output], no, cudaMemcpyDeviceToHost, stream_));
+        if ((rc = gather(*B))) return rc;
+        if (gather_ && gather_->active()) {
+            // rank 0 returns the whole gathered batch (rank-major); the other ranks return nothing
+            if (gather_->rank() == 0)
+                UQ_CUDA(cudaMemcpyAsync(out, gather_->root_buffer(no), no * (size_t)gather_->world(),
+                                        cudaMemcpyDeviceToHost, stream_));
+        } else {
+            UQ_CUDA(cudaMemcpyAsync(out, B->ptr[P_.h.output], no, cudaMemcpyDeviceToHost, stream_));
+        }
     }
     UQ_CUDA(cudaEventRecord(ev1_, stream_));
     if ((rc = finish(ev1_))) return rc;
@@ -706,43 +726,48 @@ int Engine::run_host(const void *in, void *out, uint32_t images) {
     return device_status();
 }
 
-int Engine::run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint32_t chunks) {
+int Engine::run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint32_t chunks, uint32_t k) {
     const uint32_t c = (images + chunks - 1) / chunks;  // images per piece; the last may be smaller
     chunks = (images + c - 1) / c;
     const uint32_t rem = images - (chunks - 1) * c;
-    const size_t ni = input_bytes(), no = output_bytes();
+    const size_t ni = input_bytes(), no = k ? sizeof(UgDetectionRecord) * k : output_bytes();
     BatchCtx *slot[2] = {nullptr, nullptr}, *last = nullptr;
     int rc = batch(c, &slot[0], 1);
     if (!rc) rc = batch(c, &slot[1], 2);
     if (!rc && rem != c) rc = batch(rem, &last, 3);
+    for (BatchCtx *b : {slot[0], slot[1], last})
+        if (!rc && b) rc = stage_buffers(*b, k != 0);
     if (rc) return rc;
     UQ_CUDA(cudaSetDevice(device_));
-    const bool gathering = gather_ && gather_->active();
+    const bool gathering = !k && gather_ && gather_->active();
     uint8_t *root = gathering ? gather_->root_buffer(no * images) : nullptr;
     if (gathering && gather_->rank() == 0 && !root) return 1002;
     // every stream starts after the work already queued on the compute stream
     UQ_CUDA(cudaEventRecord(ev0_, stream_));
     UQ_CUDA(cudaStreamWaitEvent(h2d_, ev0_, 0));
     UQ_CUDA(cudaStreamWaitEvent(d2h_, ev0_, 0));
-    for (uint32_t k = 0; k < chunks; k++) {
-        const int s = (int)(k & 1);
-        BatchCtx *B = (k == chunks - 1 && last) ? last : slot[s];
-        const size_t n = k == chunks - 1 ? rem : c, off = (size_t)k * c;
+    for (uint32_t piece = 0; piece < chunks; piece++) {
+        const int s = (int)(piece & 1);
+        BatchCtx *B = (piece == chunks - 1 && last) ? last : slot[s];
+        const size_t n = piece == chunks - 1 ? rem : c, off = (size_t)piece * c;
         // the slot's previous piece must be computed and read out before its arena is refilled
-        if (k >= 2) UQ_CUDA(cudaStreamWaitEvent(h2d_, pipe_ev_[2][s], 0));
-        UQ_CUDA(cudaMemcpyAsync(B->ptr[P_.h.input], in + off * ni, n * ni, cudaMemcpyHostToDevice, h2d_));
+        if (piece >= 2) UQ_CUDA(cudaStreamWaitEvent(h2d_, pipe_ev_[2][s], 0));
+        UQ_CUDA(cudaMemcpyAsync(landing(*B), in + off * ni, n * ni, cudaMemcpyHostToDevice, h2d_));
         UQ_CUDA(cudaEventRecord(pipe_ev_[0][s], h2d_));
         UQ_CUDA(cudaStreamWaitEvent(stream_, pipe_ev_[0][s], 0));
+        if ((rc = stage_in(*B, stream_))) return rc;
         if (cudaGraphLaunch(B->exec, stream_) != cudaSuccess) {
             set_error("graph launch failed");
             return 2001;
         }
+        if (k && (rc = stage_out(*B, k, stream_))) return rc;
         if (gathering && (rc = gather_->enqueue(B->ptr[P_.h.output], n * no, no * images, off * no, stream_)))
             return rc;
         UQ_CUDA(cudaEventRecord(pipe_ev_[1][s], stream_));
         UQ_CUDA(cudaStreamWaitEvent(d2h_, pipe_ev_[1][s], 0));
         if (!gathering) {
-            UQ_CUDA(cudaMemcpyAsync(out + off * no, B->ptr[P_.h.output], n * no, cudaMemcpyDeviceToHost, d2h_));
+            const void *src = k ? static_cast<const void *>(B->records) : B->ptr[P_.h.output];
+            UQ_CUDA(cudaMemcpyAsync(out + off * no, src, n * no, cudaMemcpyDeviceToHost, d2h_));
         } else if (gather_->rank() == 0) {
             // rank-major result: rank r's images occupy [r * images, (r + 1) * images)
             for (int r = 0; r < gather_->world(); r++) {
@@ -816,8 +841,9 @@ int Engine::device_status() {
 int Engine::buffers(uint32_t images, void **d_in, void **d_out) {
     BatchCtx *B = nullptr;
     int rc = batch(images, &B);
+    if (!rc) rc = stage_buffers(*B, false);
     if (rc) return rc;
-    if (d_in) *d_in = B->ptr[P_.h.input];
+    if (d_in) *d_in = landing(*B);
     if (d_out) *d_out = B->ptr[P_.h.output];
     return 0;
 }
@@ -826,7 +852,9 @@ int Engine::launch(uint32_t images) {
     BatchCtx *B = nullptr;
     int rc = batch(images, &B);
     if (rc) return rc;
+    if ((rc = stage_buffers(*B, false))) return rc;
     UQ_CUDA(cudaSetDevice(device_));
+    if ((rc = stage_in(*B, stream_))) return rc;
     UQ_CUDA(cudaGraphLaunch(B->exec, stream_));
     last_images_ = images;
     return gather(*B);
@@ -835,9 +863,10 @@ int Engine::launch(uint32_t images) {
 int Engine::upload(const void *in, uint32_t images) {
     BatchCtx *B = nullptr;
     int rc = batch(images, &B);
+    if (!rc) rc = stage_buffers(*B, false);
     if (rc) return rc;
     UQ_CUDA(cudaSetDevice(device_));
-    UQ_CUDA(cudaMemcpyAsync(B->ptr[P_.h.input], in, (size_t)input_bytes() * images, cudaMemcpyHostToDevice, stream_));
+    UQ_CUDA(cudaMemcpyAsync(landing(*B), in, (size_t)input_bytes() * images, cudaMemcpyHostToDevice, stream_));
     UQ_CUDA(cudaStreamSynchronize(stream_));
     return 0;
 }
@@ -863,11 +892,13 @@ int Engine::synchronize() {
 int Engine::time_launches(uint32_t images, uint32_t iterations, float *ms) {
     BatchCtx *B = nullptr;
     int rc = batch(images, &B);
+    if (!rc) rc = stage_buffers(*B, false);
     if (rc) return rc;
     UQ_CUDA(cudaSetDevice(device_));
     UQ_CUDA(cudaStreamSynchronize(stream_));
     UQ_CUDA(cudaEventRecord(ev0_, stream_));
     for (uint32_t i = 0; i < iterations; i++) {
+        if ((rc = stage_in(*B, stream_))) return rc;
         UQ_CUDA(cudaGraphLaunch(B->exec, stream_));
         if ((rc = gather(*B))) return rc;
     }
@@ -876,6 +907,125 @@ int Engine::time_launches(uint32_t images, uint32_t iterations, float *ms) {
     UQ_CUDA(cudaEventElapsedTime(ms, ev0_, ev1_));
     last_images_ = images;
     return device_status();
+}
+
+int Engine::stage_buffers(BatchCtx &b, bool records) {
+    if (table_channels_ && !b.pixels) UQ_CUDA(cudaMalloc(&b.pixels, (size_t)input_bytes() * b.images));
+    if (records && !b.records)
+        UQ_CUDA(cudaMalloc(&b.records, sizeof(UgDetectionRecord) * kMaxDetections * b.images));
+    return 0;
+}
+
+int Engine::stage_in(const BatchCtx &b, cudaStream_t s) {
+    if (!table_channels_) return 0;
+    launch_pixel_table(b.pixels, reinterpret_cast<int8_t *>(b.ptr[P_.h.input]), (size_t)input_bytes() * b.images,
+                       d_table_, table_channels_, s);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        set_error(std::string("input table launch: ") + cudaGetErrorString(e));
+        return 2001;
+    }
+    return 0;
+}
+
+int Engine::stage_out(const BatchCtx &b, uint32_t k, cudaStream_t s) {
+    launch_yolo_topk(reinterpret_cast<const int8_t *>(b.ptr[P_.h.output]), output_bytes(), b.images, d_yolo_, yolo_, k,
+                     b.records, s);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        set_error(std::string("decoder launch: ") + cudaGetErrorString(e));
+        return 2001;
+    }
+    return 0;
+}
+
+int Engine::set_input_table(const void *table, uint32_t channels) {
+    if (!ready_) return 22;
+    UQ_CUDA(cudaSetDevice(device_));
+    UQ_CUDA(cudaStreamSynchronize(stream_));
+    if (!table || !channels) {
+        table_channels_ = 0;
+        return 0;
+    }
+    if (channels > kMaxTableChannels || input_bytes() % channels) {
+        set_error("input table: channels must be 1.." + std::to_string(kMaxTableChannels) +
+                  " and divide the input tensor's bytes");
+        return 22;
+    }
+    if (!d_table_) UQ_CUDA(cudaMalloc(&d_table_, 256 * kMaxTableChannels));
+    UQ_CUDA(cudaMemcpy(d_table_, table, 256 * (size_t)channels, cudaMemcpyHostToDevice));
+    table_channels_ = channels;
+    return 0;
+}
+
+int Engine::set_yolo_decode(const UgYoloDecode *d) {
+    if (!ready_) return 22;
+    UQ_CUDA(cudaSetDevice(device_));
+    UQ_CUDA(cudaStreamSynchronize(stream_));
+    if (!d) {
+        yolo_ = YoloShape();
+        return 0;
+    }
+    auto bad = [](const std::string &why) {
+        set_error("YOLO decoder: " + why);
+        return 22;
+    };
+    if (d->levels < 1 || d->levels > UG_YOLO_MAX_LEVELS) return bad("levels must be 1..4");
+    if (d->classes < 1 || d->classes > 4096) return bad("classes must be 1..4096");
+    if (d->candidates < 1 || d->candidates > kMaxDetections) return bad("candidates must be 1..512");
+    if (d->reserved) return bad("reserved field must be 0");
+    const uint64_t ob = output_bytes();
+    uint64_t anchors = 0;
+    bool vec = d->classes % 16 == 0;
+    for (uint32_t l = 0; l < d->levels; l++) {
+        const UgYoloLevel &v = d->level[l];
+        const uint64_t cells = (uint64_t)v.height * v.width;
+        if (!cells) return bad("empty grid");
+        if ((uint64_t)v.box_offset + cells * 4 > ob || (uint64_t)v.score_offset + cells * d->classes > ob)
+            return bad("level " + std::to_string(l) + " lies outside the output tensor");
+        if (!std::isfinite(v.stride) || !(v.stride > 0.f)) return bad("stride must be finite and positive");
+        for (int q = 0; q < 256; q++)
+            if (v.rank[q] >= kRankCodes) return bad("order codes must be below 1024");
+        vec = vec && v.score_offset % 16 == 0;
+        anchors += cells;
+    }
+    if (anchors > kMaxAnchors) return bad("more than 32768 anchors");
+    if (!d_yolo_) UQ_CUDA(cudaMalloc(&d_yolo_, sizeof(UgYoloDecode)));
+    UQ_CUDA(cudaMemcpy(d_yolo_, d, sizeof(UgYoloDecode), cudaMemcpyHostToDevice));
+    yolo_.levels = d->levels;
+    yolo_.classes = d->classes;
+    yolo_.anchors = (uint32_t)anchors;
+    yolo_.candidates = d->candidates;
+    yolo_.vec = vec;
+    return 0;
+}
+
+int Engine::detect_host(const void *in, uint32_t images, uint32_t k, void *records) {
+    if (!yolo_.levels || !k || k > kMaxDetections) return 22;
+    return run_batch_host(in, records, images, k);
+}
+
+int Engine::launch_detect(uint32_t images, uint32_t k) {
+    if (!yolo_.levels || !k || k > kMaxDetections) return 22;
+    BatchCtx *B = nullptr;
+    int rc = batch(images, &B);
+    if (!rc) rc = stage_buffers(*B, true);
+    if (rc) return rc;
+    UQ_CUDA(cudaSetDevice(device_));
+    if ((rc = stage_in(*B, stream_))) return rc;
+    UQ_CUDA(cudaGraphLaunch(B->exec, stream_));
+    last_images_ = images;
+    return stage_out(*B, k, stream_);
+}
+
+int Engine::detect_buffer(uint32_t images, uint32_t k, void **records) {
+    if (!yolo_.levels || !k || k > kMaxDetections || !records) return 22;
+    BatchCtx *B = nullptr;
+    int rc = batch(images, &B);
+    if (!rc) rc = stage_buffers(*B, true);
+    if (rc) return rc;
+    *records = B->records;
+    return 0;
 }
 
 int Engine::gather(const BatchCtx &b) {
@@ -921,7 +1071,7 @@ int Engine::kernel_count(uint32_t images) {
     BatchCtx *B = nullptr;
     int rc = batch(images, &B);
     if (rc) return -rc;
-    return B->kernel_nodes;
+    return B->kernel_nodes + (table_channels_ ? 1 : 0);
 }
 
 int Engine::snapshot(uint32_t tensor, void *out, uint32_t bytes) {

@@ -14,6 +14,7 @@
 #include <string>
 #include <vector>
 
+#include "decode.cuh"
 #include "gather.hpp"
 #include "plan.hpp"
 
@@ -40,6 +41,8 @@ struct BatchCtx {
     cudaGraphExec_t exec = nullptr;
     int kernel_nodes = 0;
     uint8_t *host_in = nullptr, *host_out = nullptr;  // pinned staging for pageable callers
+    uint8_t *pixels = nullptr;           // uint8 input landing buffer while an input table is set
+    UgDetectionRecord *records = nullptr;  // images x kMaxDetections decoder records
 };
 
 class Engine {
@@ -84,6 +87,13 @@ class Engine {
     // batch launch ends with the gather of this rank's outputs into rank 0's root buffer.
     int dist_init(int rank, int world, const void *id, uint32_t bytes);
     int gather_buffer(uint32_t images, void **root);
+    // On-device preparation and decoding (include/unoq_cuda.h). The table maps uploaded pixels to
+    // the input tensor before the graph; the decoder turns the output tensor into k records.
+    int set_input_table(const void *table, uint32_t channels);
+    int set_yolo_decode(const UgYoloDecode *decode);
+    int detect_host(const void *in, uint32_t images, uint32_t k, void *records);
+    int launch_detect(uint32_t images, uint32_t k);
+    int detect_buffer(uint32_t images, uint32_t k, void **records);
 
    private:
     int prepare();
@@ -92,7 +102,13 @@ class Engine {
     int batch(uint32_t images, BatchCtx **out, uint32_t slot = 0);
     // Host batch in `chunks` pieces: H2D of piece k+1, compute of piece k and D2H of piece k-1
     // run concurrently on three streams, two arena slots alternating.
-    int run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint32_t chunks);
+    // k > 0: the output is k decoder records per image instead of the output tensor.
+    int run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint32_t chunks, uint32_t k = 0);
+    int run_batch_host(const void *in, void *out, uint32_t images, uint32_t k);
+    int stage_buffers(BatchCtx &b, bool records);
+    uint8_t *landing(const BatchCtx &b) const { return table_channels_ ? b.pixels : b.ptr[P_.h.input]; }
+    int stage_in(const BatchCtx &b, cudaStream_t s);              // pixel table, when set
+    int stage_out(const BatchCtx &b, uint32_t k, cudaStream_t s); // YOLO decode into b.records
     int plan_arena(BatchCtx &b);
     void layout(uint32_t images, std::vector<size_t> &offset, std::vector<uint32_t> &replicated, size_t &total) const;
     int capture(BatchCtx &b);
@@ -124,6 +140,10 @@ class Engine {
     std::unique_ptr<OutputGather> gather_;
     BatchCtx static_;                    // one-image context over g_static_arena (not owned)
     std::vector<uint32_t> static_replicated_;
+    int8_t *d_table_ = nullptr;          // [256][channels] input table (device)
+    uint32_t table_channels_ = 0;        // 0: inputs are the int8 input tensor itself
+    UgYoloDecode *d_yolo_ = nullptr;     // installed decoder (device)
+    YoloShape yolo_;                     // its host-checked shape; levels == 0 when none
     int gather(const BatchCtx &b);       // enqueue the output gather when multi-rank
     int finish(cudaEvent_t ev);          // wait for `ev`, bounded when a collective is pending
 };

@@ -6,8 +6,10 @@ Follows the reference's src/unoq_dsp/modern.py:
 * ``YOLODecoder`` (modern.py:58-103): distance-to-grid boxes, sigmoid scores, two-stage top-k.
 
 The arithmetic is float32 in the same operation order as the reference, so the tables, boxes and
-scores are identical to the reference's for identical int8 outputs. Only image conversion and
-output interpretation run on the host; every network op runs in the CUDA graph.
+scores are identical to the reference's for identical int8 outputs. Image resizing and the final
+per-detection geometry run on the host; the byte table and the top-k decode can run on the GPU
+(``profile_pixels`` + ``Session.set_input_table``, ``YOLODecoder.device_config`` + ``finish``),
+fed with the same float32 tables the host decoder computes, so both paths give identical results.
 """
 from functools import lru_cache
 
@@ -73,6 +75,13 @@ def _letterbox(image, oh, ow):
 
 def prepare_profile(image, spec, profile):
     """One image -> (1, H, W, 3) quantised input and the letterbox geometry (or None)."""
+    pixels, table, geometry = profile_pixels(image, spec, profile)
+    return table[pixels[0], np.arange(3)][None], geometry
+
+
+def profile_pixels(image, spec, profile):
+    """One image -> ((1, H, W, 3) uint8 resized pixels, (256, 3) byte table, geometry or None):
+    ``prepare_profile`` before its table lookup, for a GPU that applies the table."""
     image = _as_rgb_image(image)
     width, height = image.size
     if not width or not height:
@@ -96,7 +105,7 @@ def prepare_profile(image, spec, profile):
     q = spec["quantization"]
     table = profile_lookup(tuple(float(v) for v in mean), tuple(float(v) for v in std), q["scale"], q["zero_point"],
                            np.dtype(spec["dtype"]).str)
-    return table[pixels, np.arange(3)][None], geometry
+    return pixels[None], table, geometry
 
 
 class YOLODecoder:
@@ -137,12 +146,72 @@ class YOLODecoder:
         q = spec["quantization"]
         return (value[0].astype("f4") - q["zero_point"]) * q["scale"]
 
-    def decode(self, outputs, *, geometry, score_threshold=.25, max_results=20, iou_threshold=None):
-        from .vision import Detection
+    @staticmethod
+    def check_options(score_threshold=.25, max_results=20, iou_threshold=None):
+        """The decode options' validation (modern.py:80-83); returns max_results."""
         if iou_threshold is not None:
             raise ValueError("The one-to-one YOLO head does not use NMS; omit iou_threshold")
         if not 0 <= score_threshold <= 1 or type(max_results) is not int or not 1 <= max_results <= 300:
             raise ValueError("Invalid confidence or result limit")
+        return max_results
+
+    def _tables(self, name):
+        """Per-level float32 tables over the 256 int8 codes, by the host decoder's own expressions."""
+        q = self.specs[name]["quantization"]
+        return (np.arange(-128, 128, dtype=np.int8).astype("f4") - q["zero_point"]) * q["scale"]
+
+    def device_config(self, candidates=300):
+        """The decoder as a native.UgYoloDecode for Session.set_yolo_decode: tensor offsets in the
+        packed output, distance and sigmoid-score tables computed exactly as ``decode`` computes
+        them, and order codes of the scores (np.unique ranks) so the GPU compares integers."""
+        from .native import YOLO_MAX_LEVELS, UgYoloDecode
+        if len(self.strides) > YOLO_MAX_LEVELS:
+            raise UnsupportedModel("Too many detector levels for the GPU decoder")
+        config = UgYoloDecode(levels=len(self.strides), classes=self.classes, candidates=candidates)
+        scores = []
+        for level in range(len(self.strides)):
+            logits = self._tables(self.names[2 * level + 1])
+            scores.append(1 / (1 + np.exp(-np.clip(logits, -80, 80))))
+        _, codes = np.unique(np.stack(scores), return_inverse=True)
+        codes = codes.reshape(len(self.strides), 256)
+        for level, stride in enumerate(self.strides):
+            box, score = self.specs[self.names[2 * level]], self.specs[self.names[2 * level + 1]]
+            if "packed_offset" not in box or "packed_offset" not in score:
+                raise UnsupportedModel("GPU decoding needs packed detector outputs")
+            lv = config.level[level]
+            lv.box_offset, lv.score_offset = box["packed_offset"], score["packed_offset"]
+            lv.height, lv.width = self.height // stride, self.width // stride
+            lv.stride = stride
+            lv.distance[:] = self._tables(self.names[2 * level]).tolist()
+            lv.score[:] = scores[level].tolist()
+            lv.rank[:] = codes[level].tolist()
+        return config
+
+    def finish(self, records, *, geometry, score_threshold=.25, max_results=20, iou_threshold=None):
+        """Detections from the GPU decoder's records of one image: ``decode`` after its top-k."""
+        from .native import NO_ANCHOR
+        from .vision import Detection
+        self.check_options(score_threshold, max_results, iou_threshold)
+        detections = []
+        for record in records[:max_results]:
+            if record["anchor"] == NO_ANCHOR:
+                break
+            confidence = float(record["score"])
+            if confidence < score_threshold:
+                break
+            category = int(record["class_id"])
+            box = np.array(record["box"], dtype="f4")
+            box[[0, 2]] = (box[[0, 2]] - geometry["left"]) / (geometry["ratio"] * geometry["width"])
+            box[[1, 3]] = (box[[1, 3]] - geometry["top"]) / (geometry["ratio"] * geometry["height"])
+            box = np.clip(box, 0, 1)
+            if not np.all(np.isfinite(box)) or box[2] <= box[0] or box[3] <= box[1]:
+                continue
+            detections.append(Detection(category, self.labels[category], confidence, tuple(float(v) for v in box)))
+        return detections
+
+    def decode(self, outputs, *, geometry, score_threshold=.25, max_results=20, iou_threshold=None):
+        from .vision import Detection
+        self.check_options(score_threshold, max_results, iou_threshold)
         all_boxes, all_scores = [], []
         for level, stride in enumerate(self.strides):
             dist = self._dequantised(outputs, self.names[2 * level])

@@ -8,7 +8,30 @@ import ctypes as C
 import os
 from pathlib import Path
 
+import numpy as np
+
 from .errors import DSPError
+
+YOLO_MAX_LEVELS = 4
+
+
+class UgYoloLevel(C.Structure):
+    """include/unoq_cuda.h UgYoloLevel."""
+    _fields_ = [("box_offset", C.c_uint32), ("score_offset", C.c_uint32), ("height", C.c_uint32),
+                ("width", C.c_uint32), ("stride", C.c_float), ("distance", C.c_float * 256),
+                ("score", C.c_float * 256), ("rank", C.c_uint16 * 256)]
+
+
+class UgYoloDecode(C.Structure):
+    """include/unoq_cuda.h UgYoloDecode."""
+    _fields_ = [("levels", C.c_uint32), ("classes", C.c_uint32), ("candidates", C.c_uint32),
+                ("reserved", C.c_uint32), ("level", UgYoloLevel * YOLO_MAX_LEVELS)]
+
+
+# include/unoq_cuda.h UgDetectionRecord (32 bytes); anchor 0xFFFFFFFF marks "no pair"
+RECORD_DTYPE = np.dtype([("anchor", "<u4"), ("class_id", "<u4"), ("score", "<f4"), ("box", "<f4", (4,)),
+                         ("reserved", "<u4")])
+NO_ANCHOR = 0xFFFFFFFF
 
 DEFAULT_LIBRARY = Path(__file__).resolve().parents[1] / "lib" / "libunoq_cuda.so"
 
@@ -44,6 +67,11 @@ _SIGNATURES = {
     "ug_gather_buffer": (C.c_int, [C.c_void_p, C.c_uint32, C.POINTER(C.c_void_p)]),
     "ug_profile_batch": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.POINTER(C.c_uint64), C.c_uint32,
                                    C.POINTER(C.c_float)]),
+    "ug_set_input_table": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32]),
+    "ug_set_yolo_decode": (C.c_int, [C.c_void_p, C.POINTER(UgYoloDecode)]),
+    "ug_detect_batch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]),
+    "ug_launch_detect": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32]),
+    "ug_detect_buffer": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.POINTER(C.c_void_p)]),
     "ug_last_error": (C.c_char_p, []),
 }
 

@@ -4,8 +4,13 @@ The reference's src/unoq_dsp/vision.py surface: ``ImageClassifier.classify``,
 ``ObjectDetector.detect``, ``Detection``, ``SSDDecoder`` (fixed anchors + NMS), ``prepare_image``
 and ``image_lookup``. Float32 arithmetic follows the reference's operation order, so labels,
 scores and boxes are identical for identical int8 network outputs. The batch methods
-(``classify_batch``, ``detect_batch``) are this backend's extension: one ``ug_infer_batch`` call
-for N images, then the same per-image decoding.
+(``classify_batch``, ``detect_batch``) are this backend's extension: one GPU call for N images,
+then the same per-image decoding.
+
+With ``on_device=True`` (the default) the byte table runs on the GPU (the host only resizes and
+uploads uint8 pixels), and the one-to-one YOLO decoder's top-k runs on the GPU too, returning a
+few records per image instead of the raw head outputs; ``on_device=False`` keeps the table and
+the decoding on the host. Both give identical results.
 """
 import base64
 import time
@@ -39,6 +44,12 @@ def image_lookup(dtype, mean, std, scale, zero):
 
 def prepare_image(image, spec, normalization):
     """Bilinear resize to the input shape, then the lookup table (vision.py:32-51)."""
+    pixels, table, size = image_pixels(image, spec, normalization)
+    return table[pixels[0], np.arange(3)][None], size
+
+
+def image_pixels(image, spec, normalization):
+    """``prepare_image`` before its table lookup: ((1, H, W, 3) uint8 pixels, (256, 3) table, size)."""
     from PIL import Image
     if isinstance(image, np.ndarray):
         if image.dtype != np.uint8 or image.ndim != 3 or image.shape[2] != 3:
@@ -58,7 +69,7 @@ def prepare_image(image, spec, normalization):
     q = spec["quantization"]
     table = image_lookup(np.dtype(spec["dtype"]).str, tuple(float(v) for v in mean.reshape(-1)),
                          tuple(float(v) for v in std.reshape(-1)), q["scale"], q["zero_point"])
-    return table[pixels, np.arange(3)][None], image.size
+    return pixels[None], table, image.size
 
 
 @dataclass(frozen=True)
@@ -157,6 +168,13 @@ class SSDDecoder:
         return result
 
 
+def _device_input(session, pixels, table):
+    """Install `table` on the session's GPU (once per distinct table) and pass the pixels on."""
+    if session.input_table is None or session.input_table is not table and not np.array_equal(session.input_table, table):
+        session.set_input_table(table)
+    return pixels
+
+
 def _timings(t0, t1, t2, t3):
     return {"preprocess_ms": (t1 - t0) / 1e6, "inference_and_transfer_ms": (t2 - t1) / 1e6,
             "postprocess_ms": (t3 - t2) / 1e6, "total_ms": (t3 - t0) / 1e6}
@@ -166,33 +184,55 @@ class ObjectDetector:
     """Bundle-driven detector: preprocessing and anchors from the metadata, network on the GPU,
     box decoding on the host (top-k for the one-to-one YOLO head, NMS for fixed-anchor SSD)."""
 
-    def __init__(self, model, *, library=None, pipeline="rpc"):
+    def __init__(self, model, *, library=None, pipeline="rpc", on_device=True):
         model = resolve(model)
         task = model.metadata.get("task", {})
         self.profile = task.get("preprocessing")
+        self.on_device = bool(on_device)
+        self.device_decode = False
         if task.get("kind") == "yolo_one_to_one":
             from .modern import YOLODecoder
             self.decoder = YOLODecoder(task, model.metadata.get("outputs", []), model.metadata["input"]["shape"])
         else:
             self.decoder = SSDDecoder(task)
         self.session = Session(model, library=library, pipeline=pipeline)
+        if self.on_device and task.get("kind") == "yolo_one_to_one":
+            self.session.set_yolo_decode(self.decoder.device_config())
+            self.device_decode = True
         self.last_timings = {}
 
     def _prepare(self, image, options):
+        spec = self.session.metadata["input"]
         if self.profile:
-            from .modern import prepare_profile
-            x, geometry = prepare_profile(image, self.session.metadata["input"], self.profile)
+            from .modern import prepare_profile, profile_pixels
+            if self.on_device:
+                pixels, table, geometry = profile_pixels(image, spec, self.profile)
+                x = _device_input(self.session, pixels, table)
+            else:
+                x, geometry = prepare_profile(image, spec, self.profile)
             return x, dict(options, geometry=geometry)
-        x, _ = prepare_image(image, self.session.metadata["input"], self.decoder.task["normalization"])
+        if self.on_device:
+            pixels, table, _ = image_pixels(image, spec, self.decoder.task["normalization"])
+            return _device_input(self.session, pixels, table), options
+        x, _ = prepare_image(image, spec, self.decoder.task["normalization"])
         return x, options
+
+    def _limit(self, options):
+        """Records to request from the GPU decoder: the validated max_results."""
+        return self.decoder.check_options(**{k: v for k, v in options.items() if k != "geometry"})
 
     def detect(self, image, **options):
         t0 = time.perf_counter_ns()
         x, options = self._prepare(image, options)
         t1 = time.perf_counter_ns()
-        outputs = self.session.run(x)
-        t2 = time.perf_counter_ns()
-        result = self.decoder.decode(outputs, **options)
+        if self.device_decode:
+            records = self.session.detect_batch(x, self._limit(options))[0]
+            t2 = time.perf_counter_ns()
+            result = self.decoder.finish(records, **options)
+        else:
+            outputs = self.session.run(x)
+            t2 = time.perf_counter_ns()
+            result = self.decoder.decode(outputs, **options)
         self.last_timings = _timings(t0, t1, t2, time.perf_counter_ns())
         return result
 
@@ -201,9 +241,15 @@ class ObjectDetector:
         t0 = time.perf_counter_ns()
         prepared = [self._prepare(image, options) for image in images]
         t1 = time.perf_counter_ns()
-        outputs = self.session.run_batch(np.concatenate([x for x, _ in prepared]))
-        t2 = time.perf_counter_ns()
-        result = [self.decoder.decode(out, **opts) for out, (_, opts) in zip(outputs, prepared)]
+        x = np.concatenate([x for x, _ in prepared])
+        if self.device_decode:
+            records = self.session.detect_batch(x, self._limit(prepared[0][1]) if prepared else 1)
+            t2 = time.perf_counter_ns()
+            result = [self.decoder.finish(rec, **opts) for rec, (_, opts) in zip(records, prepared)]
+        else:
+            outputs = self.session.run_batch(x)
+            t2 = time.perf_counter_ns()
+            result = [self.decoder.decode(out, **opts) for out, (_, opts) in zip(outputs, prepared)]
         self.last_timings = _timings(t0, t1, t2, time.perf_counter_ns())
         return result
 
@@ -220,7 +266,7 @@ class ObjectDetector:
 class ImageClassifier:
     """Classifier with bundled preprocessing, or explicit mean/std when the bundle has none."""
 
-    def __init__(self, model, *, mean=None, std=None, labels=(), library=None, pipeline="rpc"):
+    def __init__(self, model, *, mean=None, std=None, labels=(), library=None, pipeline="rpc", on_device=True):
         model = resolve(model)
         task = model.metadata.get("task", {})
         self.profile = task.get("preprocessing") if task.get("kind") == "image_classification" else None
@@ -241,14 +287,22 @@ class ImageClassifier:
         self.labels = list(labels)
         self.normalization = {"mean": mean, "std": std}
         self.output_spec = outputs[0]
+        self.on_device = bool(on_device)
         self.session = Session(model, library=library, pipeline=pipeline)
         self.last_timings = {}
 
     def _prepare(self, image):
+        spec = self.session.metadata["input"]
         if self.profile:
-            from .modern import prepare_profile
-            return prepare_profile(image, self.session.metadata["input"], self.profile)[0]
-        return prepare_image(image, self.session.metadata["input"], self.normalization)[0]
+            from .modern import prepare_profile, profile_pixels
+            if self.on_device:
+                pixels, table, _ = profile_pixels(image, spec, self.profile)
+                return _device_input(self.session, pixels, table)
+            return prepare_profile(image, spec, self.profile)[0]
+        if self.on_device:
+            pixels, table, _ = image_pixels(image, spec, self.normalization)
+            return _device_input(self.session, pixels, table)
+        return prepare_image(image, spec, self.normalization)[0]
 
     def _top(self, raw, top_k):
         if self.output_spec.get("dequantize"):
