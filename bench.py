@@ -13,6 +13,8 @@ value  -- images/sec with inputs already in HBM: W untimed steps, then exactly K
           a barrier + device sync on both sides, CUDA-event timed, max over ranks.
 e2e    -- the same images/sec through the public batch call ug_infer_batch with pinned host
           buffers: per step the input H2D copy, the graph and the output D2H copy.
+detect_e2e (YOLO) -- the detector's path through ug_detect_batch: uint8 pixels H2D, the byte
+          table, the network and the top-k decode on the GPU, 20 records per image D2H.
 --impl reference -- the reference's own C runtime (oracle/_ref/libug_ref.so, built from the
           reference sources) on all host cores; rank 0 only.
 """
@@ -287,7 +289,44 @@ KERNEL_NAMES = {14: "conv", 15: "depthwise", 16: "pool", 17: "softmax_table", 18
 
 
 # --------------------------------------------------------------------------- one model
-def bench_model(lib, dist, name, global_batch, steps, warmup, peaks, want_roofline):
+def detect_leg(lib, handle, model, h_in, per_gpu, global_batch, steps, dist, k=20):
+    """The detector's own end-to-end path (ug_detect_batch): uint8 pixels from pinned host memory,
+    the bundle's byte table and the one-to-one YOLO top-k on the GPU, k records per image back."""
+    from unoq_dsp.modern import YOLODecoder, profile_lookup
+    from unoq_dsp.native import RECORD_DTYPE
+    md = model.metadata
+    decoder = YOLODecoder(md["task"], md["outputs"], md["input"]["shape"])
+    config = decoder.device_config()
+    prof, q = md["task"]["preprocessing"], md["input"]["quantization"]
+    table = np.ascontiguousarray(profile_lookup(tuple(float(v) for v in prof["mean"]),
+                                                tuple(float(v) for v in prof["std"]), q["scale"], q["zero_point"], "|i1"))
+    if lib.ug_set_yolo_decode(handle, C.byref(config)) or lib.ug_set_input_table(handle, table.ctypes.data, 3):
+        raise RuntimeError(f"decoder set-up: {lib.ug_last_error()}")
+    h_rec = lib.ug_host_alloc(RECORD_DTYPE.itemsize * k * per_gpu)
+    try:
+        for _ in range(2):
+            lib.ug_detect_batch(handle, h_in, per_gpu, k, h_rec)
+        dist.barrier()
+        total = 0.0
+        for _ in range(steps):
+            rc = lib.ug_detect_batch(handle, h_in, per_gpu, k, h_rec)
+            if rc:
+                raise RuntimeError(f"detect rc={rc}: {lib.ug_last_error()}")
+            total += lib.ug_last_infer_ms(handle)
+        dist.barrier()
+        t = dist.max(total / 1e3)
+    finally:
+        lib.ug_set_input_table(handle, None, 0)
+        lib.ug_set_yolo_decode(handle, None)
+        lib.ug_host_free(h_rec)
+    ni = int(np.prod(md["input"]["shape"]))
+    return {"value": round(global_batch * steps / t, 2), "unit": "images/s", "h2d_bytes_per_step": ni * global_batch,
+            "d2h_bytes_per_step": RECORD_DTYPE.itemsize * k * global_batch, "records_per_image": k,
+            "ms_per_step": round(t / steps * 1e3, 4),
+            "path": "ug_detect_batch: uint8 pixels -> byte table -> network -> top-k decode on the GPU -> records"}
+
+
+def bench_model(lib, dist, name, global_batch, steps, warmup, peaks, want_roofline, detect=False):
     from unoq_dsp.bundle import load
     spec = MODELS[name]
     model = load(ROOT / "models" / f"{name}.uqmodel")
@@ -346,13 +385,14 @@ def bench_model(lib, dist, name, global_batch, steps, warmup, peaks, want_roofli
         roof = breakdown = None
         if want_roofline:
             roof, breakdown = roofline(lib, handle, plan, per_gpu, max(1, min(steps, 3)), peaks, KERNEL_NAMES)
+        detected = detect_leg(lib, handle, model, h_in, per_gpu, global_batch, steps, dist) if detect else None
         lib.ug_host_free(h_in)
         lib.ug_host_free(h_out)
         return {
             "value": value, "ms_per_step": t_dev / steps * 1e3, "per_gpu_batch": per_gpu, "kernels_per_step": kernels,
             "e2e": {"value": global_batch * steps / t_e2e, "unit": "images/s", "h2d_bytes_per_step": ni * global_batch,
                     "d2h_bytes_per_step": no * global_batch, "ms_per_step": t_e2e / steps * 1e3},
-            "clocks": clocks.summary(), "roofline": roof, "breakdown": breakdown,
+            "clocks": clocks.summary(), "roofline": roof, "breakdown": breakdown, "detect_e2e": detected,
         }
     finally:
         lib.ug_close(handle)
@@ -444,7 +484,7 @@ def main():
     res = bench_model(lib, dist, "mobilenetv4-small", args.global_batch, args.steps, args.warmup, peaks, True)
     yolo = None
     if not args.no_yolo:
-        yolo = bench_model(lib, dist, "yolo26n-320", args.yolo_batch, args.steps, args.warmup, peaks, True)
+        yolo = bench_model(lib, dist, "yolo26n-320", args.yolo_batch, args.steps, args.warmup, peaks, True, detect=True)
     cpu = None
     if pool is not None:
         # bounded sample: about 20 s of CPU work in total, spread over every host core
@@ -479,7 +519,8 @@ def main():
     if yolo is not None:
         line[MODELS["yolo26n-320"]["key"]] = {
             "value": round(yolo["value"], 2), "unit": "images/s", "global_batch": args.yolo_batch,
-            "ms_per_step": round(yolo["ms_per_step"], 4), "e2e": yolo["e2e"], "roofline": yolo["roofline"],
+            "ms_per_step": round(yolo["ms_per_step"], 4), "e2e": yolo["e2e"], "detect_e2e": yolo["detect_e2e"],
+            "roofline": yolo["roofline"],
             "kernels_per_step": yolo["kernels_per_step"], "kernel_breakdown": yolo["breakdown"], "clocks": yolo["clocks"]}
     print(json.dumps(line))
 
