@@ -272,6 +272,12 @@ def all_cases(scale=1):
         ("conv_5x5_dil2_valid", lambda r: conv_case(r, (1, 12 * s, 11, 8), 4, (5, 5), (1, 1), dilation=(2, 2),
                                                     padding=(1, 0, 2, 3), act="relu6")),
         ("conv_rgb_band", lambda r: conv_case(r, (1, 10 * s, 16, 3), 16, (3, 3), (2, 2), xq=(0.02, 9))),
+        # few input channels (the stems' row-GEMM path): padding on every side, stride 1, ic 1 and 4,
+        # a post table, several column groups
+        ("conv_rows_rgb_s2", lambda r: conv_case(r, (1, 9 * s, 32, 3), 32, (3, 3), (2, 2), xq=(0.02, -7))),
+        ("conv_rows_rgb_s1", lambda r: conv_case(r, (1, 6 * s, 16, 3), 16, (3, 3), (1, 1), xq=(0.02, 4))),
+        ("conv_rows_ic4_post", lambda r: conv_post_case(r, (1, 7 * s, 20, 4), 16, (3, 3), (2, 2))),
+        ("conv_rows_ic1", lambda r: conv_case(r, (1, 5 * s, 48, 1), 32, (3, 3), (2, 2), act="relu6")),
         ("conv_ic8_band", lambda r: conv_case(r, (1, 6 * s, 10, 8), 24, (3, 3), (1, 1))),
         ("conv_rgb_odd_width", lambda r: conv_case(r, (1, 9 * s, 13, 3), 16, (3, 3), (2, 2), xq=(0.02, -5))),
         ("conv_ic8_small", lambda r: conv_case(r, (1, 9 * s, 11, 8), 16, (3, 3), (1, 1))),

@@ -98,3 +98,21 @@ def test_fused_residual_add_matches_unfused(name, native, oracle, monkeypatch):
         separate = s.run(xs, 6)
     np.testing.assert_array_equal(fused, expect)
     np.testing.assert_array_equal(separate, expect)
+
+
+@pytest.mark.parametrize("x_shape,oc,stride", [((1, 300, 48, 3), 16, (2, 2)), ((1, 131, 64, 3), 32, (1, 1)),
+                                               ((1, 224, 224, 3), 32, (2, 2))])
+def test_row_gemm_conv_tiles_and_edges(native, oracle, monkeypatch, x_shape, oc, stride):
+    """The few-channel row-GEMM conv over more than one 128-row tile per image and a partial last
+    column group, against the oracle and against the same plan with that path switched off."""
+    from unoq_dsp import synth
+    rng = np.random.default_rng(sum(x_shape) + oc)
+    plan, xs, _ = synth.single_conv_plan(rng, x_shape, oc, (3, 3), stride, xq=(0.02, -9))
+    images = 3
+    x = rng.integers(-128, 128, size=(images,) + xs[1:], dtype=np.int64).astype(np.int8)
+    expect = oracle.run(plan, x, images)
+    with NativeSession(native, plan) as s:
+        np.testing.assert_array_equal(s.run(x, images), expect)
+    monkeypatch.setenv("UNOQ_CONV_ROWS", "0")
+    with NativeSession(native, plan) as s:
+        np.testing.assert_array_equal(s.run(x, images), expect)

@@ -1,0 +1,522 @@
+// conv_rows.cu -- convolutions over few input channels (the RGB stems) as row GEMMs on the
+// 5th-generation tensor cores (tcgen05 kind::i8).
+//
+// Plan code 14 (runtime/qnn.c:1101-1227) for kh x kw kernels (kh, kw <= 3) over ic <= 4 channels
+// with stride s in both directions. For G adjacent output columns ox0..ox0+G-1 of output row oy,
+// every tap of kernel row ky reads input row iy = s*oy - pt + ky, and all their bytes lie in one
+// window of that row: bytes [X, X + s*ic*(G-1) + kw*ic) with X = (s*ox0 - pl)*ic. Hence
+//
+//     Y[oy][ox0 + j][oc] = sum_ky sum_b  In[iy][A + b] * W_ky[j*OC + oc][b]      (0 <= b < 128)
+//
+// with A = X rounded down to 16 bytes and W_ky[j*OC + oc][b] = w[oc][ky][kx][c] where
+// b = (X - A) + s*ic*j + kx*ic + c (zero elsewhere). That is a GEMM with M = output rows of one
+// image (128 per tile), N = G*OC (G output pixels x OC channels, <= 256) and K = 128 window bytes
+// per kernel row. The A operand of each (tile, ky) is a plain box of the input tensor, loaded by
+// TMA straight into the UMMA SWIZZLE_128B layout from a 3-D tensor map {row bytes, every s-th row,
+// images} whose out-of-range rows and columns read as zero: no im2col assembly at all. The banded
+// B matrix is built once at load time and stays resident in shared memory.
+//
+// Zero fill stands where the reference reads the input zero point (qnn.c:1166-1168): an output
+// whose taps leave the image gets xzp * (sum of those taps' weights) added to its accumulator,
+// from a table indexed by which kernel rows and columns are outside. The u8 / s8 difference of
+// the reference's columns is folded into the per-channel constants as in conv_tc.cu.
+//
+// Roles: warp 0 issues the TMA loads, warp 1 the MMAs (M=128, N=G*OC, K=32 per instruction) into
+// two TMEM accumulators, warps 2.. requantise (tcgen05.ld, exact scale, clamp, post table) into
+// per-warp staging buffers and write them with 3-D TMA tensor stores, which clip the rows past
+// the image. Every wait is bounded (about 2 s); on expiry the kernel records a site code, waits
+// for its copies and MMAs, frees its TMEM and exits.
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+#include <type_traits>
+#include <vector>
+
+#include "conv_rows.cuh"
+#include "plan.hpp"
+#include "tc_common.cuh"
+
+namespace uq {
+
+namespace {
+
+constexpr int kRowsMaxSmem = 227 * 1024;
+
+struct RowsParams {
+    CUtensorMap xmap[2];   // input views: rows v, v + s, v + 2s, ... of every image (v = 0, 1)
+    CUtensorMap ymap;      // output {ow*oc, oh, n}, box {box, 32, 1}, swizzled like the staging
+    const int8_t *w;       // [kh][bn x 128] UMMA SWIZZLE_128B K-major
+    const EpiChan *epi;    // [oc]
+    const uint8_t *post;   // 256 bytes or null
+    const int32_t *corr;   // [(rowmask << kw) | colmask][oc]: xzp * weights of the taps outside
+    int n, ih, iw, ic, oh, ow, oc;
+    int kh, kw, s, pt, pl;
+    int G, bn;             // output pixels per column group; bn = G * oc
+    int groups, row_tiles, tiles;
+    int ksteps;            // 32-byte K steps of a kernel row's window
+    int x0;                // window start (bytes, 16-aligned, may be negative) of group 0; group g adds g * gstep
+    int gstep;
+    int view[3], dy[3];    // per kernel row: input view and row offset (view row = oy + dy)
+    int stages, lo, hi, box, swz, out_bytes, tmem_cols;
+};
+
+struct RowsLayout {
+    size_t a, b, out, epi, lut, bars, total;
+    __host__ __device__ RowsLayout(int stages, int kh, int bn, int oc, int out_bytes) {
+        size_t o = 0;
+        a = o;
+        o += (size_t)stages * kStageBytes;
+        b = o;
+        o += (size_t)kh * bn * kBK;
+        out = o;
+        o += (size_t)out_bytes;
+        epi = (o + 31) & ~(size_t)31;
+        o = epi + (size_t)oc * sizeof(EpiChan);
+        lut = o;
+        o += 256;
+        bars = (o + 7) & ~(size_t)7;
+        o = bars + (size_t)(2 * stages + 5) * 8 + 16;
+        total = o + 1024;  // base alignment slack
+    }
+};
+
+__host__ __device__ inline size_t rows_warp_stage(int box) { return ((size_t)32 * box + 1023) & ~(size_t)1023; }
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, int x, int y, int z, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+        : "memory");
+}
+
+template <int EPI, int EW>
+__global__ void __launch_bounds__((2 + EW) * 32, 1) conv_rows_kernel(const __grid_constant__ RowsParams p) {
+    constexpr int kParts = EW / 4;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const int S = p.stages;
+    const RowsLayout L(S, p.kh, p.bn, p.oc, p.out_bytes);
+    uint8_t *sA = smem + L.a;
+    uint8_t *sB = smem + L.b;
+    uint8_t *sOut = smem + L.out;
+    long long *sK = reinterpret_cast<long long *>(smem + L.epi);
+    int *sI = reinterpret_cast<int *>(sK + p.oc);
+    const EpiSoA E{sK, sI, sI + p.oc, sI + 2 * p.oc, sI + 3 * p.oc, sI + 4 * p.oc, sI + 5 * p.oc};
+    uint8_t *sLut = smem + L.lut;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
+    uint64_t *full = bars, *empty = bars + S;
+    uint64_t *tfull = bars + 2 * S, *tempty = bars + 2 * S + 2, *drain = bars + 2 * S + 4;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 5);
+    volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(smem_u32(full + s), 1);
+            mbar_init(smem_u32(empty + s), 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(smem_u32(tfull + a), 1);
+            mbar_init(smem_u32(tempty + a), EW);
+        }
+        mbar_init(smem_u32(drain), 1);
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    for (int i = threadIdx.x; i < p.oc; i += blockDim.x) {
+        const EpiChan c = p.epi[i];
+        sK[i] = c.k;
+        sI[i] = c.m;
+        sI[p.oc + i] = c.cut;
+        sI[2 * p.oc + i] = c.sh;
+        sI[3 * p.oc + i] = c.ls;
+        sI[4 * p.oc + i] = c.bs;
+        sI[5 * p.oc + i] = c.zadd;
+    }
+    if (p.post)
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) sLut[i] = p.post[i];
+    {
+        // the banded weights, resident for the whole kernel (read by the tensor core: async proxy)
+        const size_t bbytes = (size_t)p.kh * p.bn * kBK;
+        const uint4 *src = reinterpret_cast<const uint4 *>(p.w);
+        for (size_t i = threadIdx.x; i < bbytes / 16; i += blockDim.x) st_shared16(smem_u32(sB) + (uint32_t)(i * 16), __ldg(src + i));
+        fence_proxy_async();
+    }
+    if (warp == 1) {  // the MMA warp owns the TMEM allocation
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(p.tmem_cols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int per_image = p.row_tiles * p.groups;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            long long it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+                const int img = t / per_image, rem = t - img * per_image;
+                const int rt = rem / p.groups, g = rem - rt * p.groups;
+                const int x = p.x0 + g * p.gstep, oy0 = rt * kBM;
+                for (int ky = 0; ky < p.kh; ky++, it++) {
+                    const int s = (int)(it % S);
+                    if (!mbar_wait(smem_u32(empty + s), (uint32_t)(((it / S) & 1) ^ 1), abort, 201)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(smem_u32(full + s), (uint32_t)kStageBytes);
+                    tma_load_3d(smem_u32(sA + (size_t)s * kStageBytes), &p.xmap[p.view[ky]], x, oy0 + p.dy[ky], img,
+                                smem_u32(full + s));
+                }
+            }
+            // every load issued has landed before the CTA may exit (bounded)
+            for (long long q = it - (it < S ? it : S); q < it; q++) {
+                const long long start = clock64();
+                while (!mbar_try_wait(smem_u32(full + (int)(q % S)), (uint32_t)((q / S) & 1), 200000) &&
+                       clock64() - start < kTimeoutCycles) {
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = instr_desc(p.bn);
+            const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
+            long long it = 0;
+            bool ok = true;
+            int lt = 0;
+            for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, lt++) {
+                const int acc = lt & 1;
+                if (!mbar_wait(smem_u32(tempty + acc), (uint32_t)(((lt >> 1) & 1) ^ 1), abort, 202)) break;
+                tc_fence_after();
+                const uint32_t tmem_d = tmem_base + (uint32_t)(acc * p.bn);
+                for (int ky = 0; ky < p.kh; ky++, it++) {
+                    const int s = (int)(it % S);
+                    if (!mbar_wait(smem_u32(full + s), (uint32_t)((it / S) & 1), abort, 203)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    for (int kk = 0; kk < p.ksteps; kk++) {
+                        const uint64_t ad = smem_desc(a0 + (uint32_t)(s * kStageBytes + kk * 32));
+                        const uint64_t bd = smem_desc(b0 + (uint32_t)(ky * p.bn * kBK + kk * 32));
+                        mma_i8(tmem_d, ad, bd, idesc, (ky | kk) ? 1u : 0u);
+                    }
+                    mma_commit(smem_u32(empty + s));
+                }
+                if (!ok) break;
+                mma_commit(smem_u32(tfull + acc));
+            }
+            // every MMA issued has completed before TMEM is freed, on the abort path too
+            mma_commit(smem_u32(drain));
+            const long long start = clock64();
+            while (!mbar_try_wait(smem_u32(drain), 0, 200000) && clock64() - start < kTimeoutCycles) {
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------------ epilogue
+        const int e = warp - 2;
+        const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31 (warp id % 4 rule)
+        const int part = e >> 2;       // column part [part * box, part * box + box) of the tile
+        const int c0 = part * p.box;
+        const int chunks = p.box / 16;
+        const uint8_t *lut = p.post ? sLut : nullptr;
+        const int swz_row = p.swz == 3 ? (lane & 7) : p.swz == 2 ? ((lane >> 1) & 3) : p.swz == 1 ? ((lane >> 2) & 1) : 0;
+        const size_t wsb = rows_warp_stage(p.box);
+        uint8_t *wstage0 = sOut + (size_t)e * 2 * wsb;
+        int lt = 0;
+        for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, lt++) {
+            const int img = t / per_image, rem = t - img * per_image;
+            const int rt = rem / p.groups, g = rem - rt * p.groups;
+            const int oy0 = rt * kBM, ox0 = g * p.G;
+            const int acc = lt & 1;
+            if (!mbar_wait(smem_u32(tfull + acc), (uint32_t)((lt >> 1) & 1), abort, 204)) break;
+            tc_fence_after();
+            const int r0 = oy0 + quarter * 32;  // first output row of this warp
+            const bool live = r0 < p.oh;
+            uint8_t *stage = wstage0 + (size_t)(lt & 1) * wsb;
+            // this buffer's previous store (two tiles back) must have been read out
+            if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+            __syncwarp();
+            if (live) {
+                const int oy = r0 + lane;
+                // kernel rows of this output row that fall outside the image
+                int rmask = 0;
+                for (int ky = 0; ky < p.kh; ky++) {
+                    const int iy = p.s * oy - p.pt + ky;
+                    rmask |= (iy < 0 || iy >= p.ih) ? 1 << ky : 0;
+                }
+                const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.bn + c0);
+                uint32_t ra[16], rb[16];
+                tmem_ld16_nowait(taddr, ra);
+                tmem_wait_ld(ra);
+                for (int ci = 0; ci < chunks; ci++) {
+                    const bool more = ci + 1 < chunks;
+                    if (more) tmem_ld16_nowait(taddr + (ci + 1) * 16, rb);
+                    const int c = c0 + ci * 16, j = c / p.oc, oc0 = c - j * p.oc;
+                    const int ox = ox0 + j;
+                    int cmask = 0;
+                    for (int kx = 0; kx < p.kw; kx++) {
+                        const int ix = p.s * ox - p.pl + kx;
+                        cmask |= (ix < 0 || ix >= p.iw) ? 1 << kx : 0;
+                    }
+                    if ((rmask | cmask) && oy < p.oh && ox < p.ow) {
+                        const int32_t *cr = p.corr + (size_t)((rmask << p.kw) | cmask) * p.oc + oc0;
+#pragma unroll
+                        for (int i = 0; i < 16; i++) ra[i] = (uint32_t)((int32_t)ra[i] + __ldg(cr + i));
+                    }
+                    const uint4 v = epilogue_chunk<EPI>(ra, E, lut, oc0, p.lo, p.hi);
+                    st_shared16(smem_u32(stage + (size_t)lane * p.box + ((ci ^ swz_row) << 4)), v);
+                    if (more) tmem_wait_ld(rb);
+#pragma unroll
+                    for (int q = 0; q < 16; q++) ra[q] = rb[q];
+                }
+            }
+            tc_fence_before();
+            fence_proxy_async();  // staged bytes visible to the TMA (async proxy)
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(smem_u32(tempty + acc));  // accumulator free for reuse
+                if (live)
+                    asm volatile(
+                        "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                            reinterpret_cast<uint64_t>(&p.ymap)),
+                        "r"(smem_u32(stage)), "r"(ox0 * p.oc + c0), "r"(r0), "r"(img)
+                        : "memory");
+                asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+            }
+        }
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(p.tmem_cols));
+    }
+}
+
+int g_rows_sm_count = 0;
+
+}  // namespace
+
+struct ConvRows {
+    RowsParams p{};
+    size_t smem = 0;
+    int epi_mode = kGeneral;
+    int epilogue_warps = 16;
+};
+
+int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *post_dev, const ConvGeom &g,
+                      const std::function<void *(size_t)> &alloc, ConvRows **out) {
+    *out = nullptr;
+    const char *env = std::getenv("UNOQ_CONV_ROWS");
+    if (env && env[0] == '0') return 0;
+    const int s = g.sh;
+    if (g.ic < 1 || g.ic > 4 || g.kh < 1 || g.kh > 3 || g.kw < 1 || g.kw > 3 || g.dh != 1 || g.dw != 1) return 0;
+    if (g.sw != s || (s != 1 && s != 2)) return 0;
+    if (g.oc % 16 != 0 || g.oc > 256) return 0;
+    if (g.pt < 0 || g.pt >= g.kh || g.pl < 0 || g.pl >= g.kw) return 0;
+    const long long row_bytes = (long long)g.iw * g.ic;
+    if (row_bytes % 16 != 0) return 0;  // tensor-map strides are whole 16-byte units
+    if ((long long)g.ih * row_bytes >= (1ll << 31) || (long long)g.oh * g.ow * g.oc >= (1ll << 31)) return 0;
+    // window offset of every group (constant because a group advances by whole 16-byte units)
+    const int o = (((-g.pl * g.ic) % 16) + 16) % 16;
+    int G = 0;
+    for (int c = 256 / g.oc; c >= 1; c /= 2) {
+        if ((s * g.ic * c) % 16 != 0) continue;
+        if (o + s * g.ic * (c - 1) + g.kw * g.ic > kBK) continue;
+        G = c;
+        break;
+    }
+    if (!G) return 0;
+    const int bn = G * g.oc;
+    const int ew = bn % 64 == 0 ? 16 : 8;
+    const int parts = ew / 4;
+    if (bn % (16 * parts) != 0) return 0;
+    const int box = bn / parts;
+    if (box != 16 && box != 32 && box != 64 && box != 128) return 0;  // staging swizzle spans
+    const int span = o + s * g.ic * (G - 1) + g.kw * g.ic;
+    const int ksteps = (span + 31) / 32;
+    const int out_bytes = (int)(2 * ew * rows_warp_stage(box));
+    int stages = 4;
+    while (stages > 2 && RowsLayout(stages, g.kh, bn, g.oc, out_bytes).total > (size_t)kRowsMaxSmem) stages--;
+    const RowsLayout L(stages, g.kh, bn, g.oc, out_bytes);
+    if (L.total > (size_t)kRowsMaxSmem) return 0;
+
+    // Weights: reference packed layout (gemm.h:9), reduction index t = (ky*kw + kx)*ic + c
+    // (tflite.py:155), into the banded B matrix, one SW128 K-major stage per kernel row.
+    const int kp = q[18], oc = g.oc, K = g.kh * g.kw * g.ic;
+    auto wref = [&](int j, int t) -> int { return w_packed[(j / 4) * kp * 4 + (t / 8) * 32 + (j % 4) * 8 + t % 8]; };
+    std::vector<uint8_t> wt((size_t)g.kh * bn * kBK, 0);
+    for (int ky = 0; ky < g.kh; ky++)
+        for (int n = 0; n < bn; n++) {
+            const int j = n / oc, ch = n % oc;
+            for (int kx = 0; kx < g.kw; kx++)
+                for (int c = 0; c < g.ic; c++) {
+                    const int b = o + s * g.ic * j + kx * g.ic + c;
+                    const int chunk = b / 16;
+                    const size_t off = ((size_t)ky * bn + (n / 8) * 8) * kBK + (n % 8) * kBK + ((chunk ^ (n % 8)) * 16) + b % 16;
+                    wt[off] = (uint8_t)(int8_t)wref(ch, (ky * g.kw + kx) * g.ic + c);
+                }
+        }
+    const int32_t *cbias = q + kHead, *mult = cbias + oc, *shift = mult + oc;
+    const int xzp = q[12], yzp = q[13];
+    std::vector<EpiChan> epi(oc);
+    for (int j = 0; j < oc; j++) {
+        long long sum_all = 0, sum_pad = 0;
+        for (int t = 0; t < kp; t++) {
+            const int v = wref(j, t);
+            sum_all += v;
+            if (t >= K) sum_pad += v;
+        }
+        epi[j] = make_epilogue((long long)cbias[j] + 128ll * sum_all + (long long)xzp * sum_pad, mult[j], shift[j], yzp);
+    }
+    bool fast = true;
+    for (int j = 0; j < oc; j++) fast &= shift[j] <= -1 && shift[j] >= -15;
+    const int epi_mode = !fast ? kGeneral : (q[14] >= yzp ? kRelu : kTies);
+    if (epi_mode != kGeneral)
+        for (auto &e : epi) e.sh = e.sh >= 32 ? e.sh - 32 : 0;  // shift of the high word
+    // xzp * sum of the weights of the taps outside the image, per (rows outside, columns outside)
+    std::vector<int32_t> corr((size_t)(1 << g.kh) * (1 << g.kw) * oc, 0);
+    for (int rm = 0; rm < (1 << g.kh); rm++)
+        for (int cm = 0; cm < (1 << g.kw); cm++)
+            for (int j = 0; j < oc; j++) {
+                long long sum = 0;
+                for (int ky = 0; ky < g.kh; ky++)
+                    for (int kx = 0; kx < g.kw; kx++)
+                        if ((rm >> ky & 1) || (cm >> kx & 1))
+                            for (int c = 0; c < g.ic; c++) sum += wref(j, (ky * g.kw + kx) * g.ic + c);
+                corr[((size_t)(rm << g.kw) | cm) * oc + j] = (int32_t)((long long)xzp * sum);
+            }
+    void *dw = alloc(wt.size());
+    void *de = alloc(epi.size() * sizeof(EpiChan));
+    void *dc = alloc(corr.size() * sizeof(int32_t));
+    if (!dw || !de || !dc) return 2001;
+    if (cudaMemcpy(dw, wt.data(), wt.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(de, epi.data(), epi.size() * sizeof(EpiChan), cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(dc, corr.data(), corr.size() * sizeof(int32_t), cudaMemcpyHostToDevice) != cudaSuccess)
+        return 2001;
+    if (!g_rows_sm_count) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_rows_sm_count, cudaDevAttrMultiProcessorCount, dev);
+        if (g_rows_sm_count <= 0) g_rows_sm_count = 148;
+    }
+    static bool attr_set = false;
+    if (!attr_set) {
+        auto allow = [](auto fn) {
+            return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsMaxSmem) == cudaSuccess;
+        };
+        if (!allow(conv_rows_kernel<kRelu, 16>) || !allow(conv_rows_kernel<kTies, 16>) ||
+            !allow(conv_rows_kernel<kGeneral, 16>) || !allow(conv_rows_kernel<kRelu, 8>) ||
+            !allow(conv_rows_kernel<kTies, 8>) || !allow(conv_rows_kernel<kGeneral, 8>))
+            return 2001;
+        attr_set = true;
+    }
+    ConvRows *c = new ConvRows();
+    RowsParams &p = c->p;
+    p.w = static_cast<const int8_t *>(dw);
+    p.epi = static_cast<const EpiChan *>(de);
+    p.corr = static_cast<const int32_t *>(dc);
+    p.post = post_dev;
+    p.ih = g.ih, p.iw = g.iw, p.ic = g.ic, p.oh = g.oh, p.ow = g.ow, p.oc = g.oc;
+    p.kh = g.kh, p.kw = g.kw, p.s = s, p.pt = g.pt, p.pl = g.pl;
+    p.G = G;
+    p.bn = bn;
+    p.groups = (g.ow + G - 1) / G;
+    p.row_tiles = (g.oh + kBM - 1) / kBM;
+    p.ksteps = ksteps;
+    p.x0 = -g.pl * g.ic - o;  // = (s*0 - pl)*ic rounded down to 16 bytes
+    p.gstep = s * g.ic * G;
+    for (int ky = 0; ky < g.kh; ky++) {
+        const int r = ky - g.pt;  // input row = s*oy + r
+        const int v = ((r % s) + s) % s;
+        p.view[ky] = v;
+        p.dy[ky] = (r - v) / s;
+    }
+    p.stages = stages;
+    p.lo = q[14], p.hi = q[15];
+    p.box = box;
+    p.swz = box == 128 ? 3 : box == 64 ? 2 : box == 32 ? 1 : 0;
+    p.out_bytes = out_bytes;
+    int cols = 32;
+    while (cols < 2 * bn) cols *= 2;
+    p.tmem_cols = cols;
+    c->smem = L.total;
+    c->epi_mode = epi_mode;
+    c->epilogue_warps = ew;
+    *out = c;
+    return 0;
+}
+
+int conv_rows_launch(const ConvRows &c, const int8_t *x, int8_t *y, const ConvGeom &g, cudaStream_t s) {
+    RowsParams p = c.p;
+    p.n = g.n;
+    p.tiles = g.n * p.row_tiles * p.groups;
+    if ((long long)g.n * p.row_tiles * p.groups >= (1ll << 31)) return 2001;
+    EncodeTiled enc = encoder();
+    if (!enc) return 2001;
+    const cuuint64_t row_bytes = (cuuint64_t)g.iw * g.ic, img_bytes = row_bytes * (cuuint64_t)g.ih;
+    for (int v = 0; v < p.s; v++) {
+        // view v: input rows v, v + s, ... of every image
+        const cuuint64_t dims[3] = {row_bytes, (cuuint64_t)((g.ih - v + p.s - 1) / p.s), (cuuint64_t)g.n};
+        const cuuint64_t strides[2] = {row_bytes * (cuuint64_t)p.s, img_bytes};
+        const cuuint32_t box[3] = {(cuuint32_t)kBK, (cuuint32_t)kBM, 1};
+        const cuuint32_t estr[3] = {1, 1, 1};
+        if (enc(&p.xmap[v], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t *>(x) + (size_t)v * row_bytes, dims, strides,
+                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return 2001;
+    }
+    {
+        const cuuint64_t dims[3] = {(cuuint64_t)g.ow * g.oc, (cuuint64_t)g.oh, (cuuint64_t)g.n};
+        const cuuint64_t strides[2] = {(cuuint64_t)g.ow * g.oc, (cuuint64_t)g.oh * g.ow * g.oc};
+        const cuuint32_t box[3] = {(cuuint32_t)p.box, 32, 1};
+        const cuuint32_t estr[3] = {1, 1, 1};
+        const CUtensorMapSwizzle sw = p.swz == 3   ? CU_TENSOR_MAP_SWIZZLE_128B
+                                      : p.swz == 2 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                      : p.swz == 1 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                                   : CU_TENSOR_MAP_SWIZZLE_NONE;
+        if (enc(&p.ymap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return 2001;
+    }
+    const int grid = std::min(g_rows_sm_count, p.tiles);
+    auto go = [&](auto ew) {
+        constexpr int EWv = decltype(ew)::value;
+        constexpr int T = (2 + EWv) * 32;
+        if (c.epi_mode == kRelu) conv_rows_kernel<kRelu, EWv><<<grid, T, c.smem, s>>>(p);
+        else if (c.epi_mode == kTies) conv_rows_kernel<kTies, EWv><<<grid, T, c.smem, s>>>(p);
+        else conv_rows_kernel<kGeneral, EWv><<<grid, T, c.smem, s>>>(p);
+    };
+    if (c.epilogue_warps == 16) go(std::integral_constant<int, 16>{});
+    else go(std::integral_constant<int, 8>{});
+    return 0;
+}
+
+void conv_rows_free(ConvRows *c) { delete c; }
+
+int conv_rows_error(bool reset) {
+    int v = 0;
+    cudaMemcpyFromSymbol(&v, g_tc_error, sizeof(int));
+    if (reset && v) {
+        int z = 0;
+        cudaMemcpyToSymbol(g_tc_error, &z, sizeof(int));
+    }
+    return v;
+}
+
+}  // namespace uq

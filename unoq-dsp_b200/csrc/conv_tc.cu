@@ -29,7 +29,7 @@
 // the host folds into the epilogue constants, so results are bit-identical.
 //
 // Every wait (mbarrier phases, including the ones that stand in for sub-CTA barriers) is bounded
-// by about 2 s of SM clock; on expiry the kernel records a site code in g_conv_tc_error, drains its
+// by about 2 s of SM clock; on expiry the kernel records a site code in g_tc_error, drains its
 // MMAs, frees its TMEM and exits.
 #include <cstdio>
 #include <cstdlib>
@@ -43,16 +43,12 @@
 #include "conv_tc.cuh"
 #include "plan.hpp"
 #include "requant.cuh"
+#include "tc_common.cuh"
 
 namespace uq {
 
-__device__ int g_conv_tc_error = 0;
-
 namespace {
 
-constexpr int kBM = 128;              // pixels per tile = TMEM lanes
-constexpr int kBK = 128;              // reduction bytes per stage (one 128-byte swizzle row)
-constexpr int kStageBytes = kBM * kBK;
 // Warp roles by index: producers [0, PW), epilogue [PW, PW + EW), MMA issuer PW + EW.
 // PW = 4 for pointwise convs (light copies; fewer warps leave more registers), 8 for band / gather
 // convs (assembly-heavy). EW = 8 or 16 epilogue warps: EW / 4 warps per TMEM lane quarter, each
@@ -119,8 +115,7 @@ struct Params {
     const int8_t *res;         // residual tensor [M][oc] (the add's other operand)
     const int32_t *add_tab;    // the add's q block on the device: tables at +8 (input a), +264 (input b)
     int res_side;              // 0: this conv is the add's input a (table at +8), 1: input b
-    EpiChan add_epi;           // the add's scale as requant.cuh constants (bias 0)
-    int add_lo, add_hi;
+    AddEpi add;                // the add's scale as requant.cuh constants (bias 0) and clamp
     int swz;                   // staging swizzle: 0 none (16 B rows), 1 = 32 B, 2 = 64 B, 3 = 128 B span
 };
 
@@ -158,233 +153,9 @@ struct Layout {
     }
 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar) : "memory");
-}
-
-// Test a phase; while it is incomplete the thread may be suspended for up to `hint_ns`, and it
-// resumes as soon as the phase completes. Without a hint the hardware's default limit is short
-// and waiting warps would spin, taking issue slots from the warps doing the work.
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity, uint32_t hint_ns = 0) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity), "r"(hint_ns)
-        : "memory");
-    return ok != 0;
-}
-
-// Wait bound: 4e9 SM cycles (about 2 s at the B200's 1.9-2 GHz boost clock).
-constexpr long long kTimeoutCycles = 4000000000ll;
-
-// Bounded wait: returns false (and records `code`) if the phase does not complete in time or
-// another role of this CTA already gave up.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort, int code) {
-    constexpr uint32_t kHintNs = 200000;  // one suspension of at most 0.2 ms per poll
-    if (mbar_try_wait(bar, parity, kHintNs)) return true;
-    const long long start = clock64();
-    while (true) {
-        if (mbar_try_wait(bar, parity, kHintNs)) return true;
-        if (*abort) return false;
-        if (clock64() - start > kTimeoutCycles) {
-            *abort = 1;
-            atomicCAS(&g_conv_tc_error, 0, code);
-            return false;
-        }
-    }
-}
-
-// A barrier among the warps of one role, built on an mbarrier so that it is bounded: each warp
-// arrives once per round (lane 0, after the warp has converged) and every lane waits for the
-// round's phase. One arrival per warp keeps the shared-memory atomics on the barrier word few.
-__device__ __forceinline__ bool role_sync(uint32_t bar, unsigned &round, volatile int *abort, int code) {
-    __syncwarp();
-    if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
-    const bool ok = mbar_wait(bar, round & 1u, abort, code);
-    round++;
-    return ok;
-}
-
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-// cp.async.wait_group with a run-time depth (the instruction takes an immediate).
-__device__ __forceinline__ void cp_async_wait_dyn(int n) {
-    switch (n) {
-        case 0: cp_async_wait<0>(); break;
-        case 1: cp_async_wait<1>(); break;
-        case 2: cp_async_wait<2>(); break;
-        default: cp_async_wait<3>(); break;
-    }
-}
-__device__ __forceinline__ void fence_proxy_async() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-__device__ __forceinline__ void st_shared16(uint32_t dst, uint4 v) {
-    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-                 : "memory");
-}
-
-__device__ __forceinline__ uint4 ld_shared16(uint32_t src) {
-    uint4 v;
-    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(src));
-    return v;
-}
-// Four bytes at any shared-memory address: two aligned words joined by a funnel shift.
-__device__ __forceinline__ uint32_t ld_shared_u32_unaligned(uint32_t addr) {
-    const uint32_t base = addr & ~3u;
-    uint32_t lo, hi;
-    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(lo) : "r"(base));
-    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(hi) : "r"(base + 4));
-    return __funnelshift_r(lo, hi, (addr & 3u) * 8);
-}
-
-// UMMA shared-memory descriptor: K-major, SWIZZLE_128B, 8-row atoms 1024 bytes apart.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
-    return (uint64_t)((addr >> 4) & 0x3FFF) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
-}
-
-// Instruction descriptor for kind::i8: s32 accumulate, signed A and B, both K-major.
-__device__ __forceinline__ uint32_t instr_desc(int bn) {
-    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
-}
-
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-}
-
-// Wait for this thread's outstanding tcgen05.ld; the registers are tied in as read-write
-// operands so no use of them can be scheduled before the wait.
-__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[16]) {
-    asm volatile("tcgen05.wait::ld.sync.aligned;"
-                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
-                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
-                 :
-                 : "memory");
-}
-
 }  // namespace
 
 namespace {
-
-// Epilogue requantisation modes, chosen per layer on the host (all exact, see make_epilogue):
-//   kRelu    every channel has -15 <= shift <= -1 and the clamp floor lo >= yzp, so the tie
-//            correction for negative high products can never survive the clamp:
-//            y = clamp((hi32(acc*m + k)) >> (sh - 32));
-//   kTies    same shifts, lo < yzp: subtract 2^31 first when acc <= cut;
-//   kGeneral any channel with a pre-shift (shift >= 0) or shift < -15: full form.
-enum EpiMode { kRelu = 0, kTies = 1, kGeneral = 2 };
-
-// Per-channel constants in shared memory as structure-of-arrays so 16 columns load as
-// 128-bit broadcast vectors.
-struct EpiSoA {
-    const long long *k;
-    const int *m, *cut, *sh, *ls, *bs, *zadd;
-};
-
-// Saturating pack of four int32 values into int8 lanes (byte i = v_i): two cvt.pack.sat, each
-// putting sat(a) in byte 1 and sat(b) in byte 0 above c's low half shifted up by 16.
-__device__ __forceinline__ uint32_t pack_sat_s8x4(int32_t v0, int32_t v1, int32_t v2, int32_t v3) {
-    uint32_t hi, d;
-    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(hi) : "r"(v3), "r"(v2), "r"(0));
-    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(v1), "r"(v0), "r"(hi));
-    return d;
-}
-
-// Requantise 16 accumulators (columns c0..c0+15 of one row), clamp to [lo, hi] and pack them as
-// int8 (the clamp is two integer min/max per value; byte-SIMD min/max would be emulated).
-template <int EPI>
-__device__ __forceinline__ uint4 epilogue_chunk(const uint32_t (&r)[16], const EpiSoA &E, const uint8_t *lut, int c0,
-                                                int lo, int hi, const Params *fp = nullptr, const int32_t *tabs = nullptr,
-                                                uint4 res = make_uint4(0, 0, 0, 0)) {
-    const uint32_t resw[4] = {res.x, res.y, res.z, res.w};
-    uint32_t packed[4];
-    const longlong2 *K2 = reinterpret_cast<const longlong2 *>(E.k + c0);
-    const int4 *M4 = reinterpret_cast<const int4 *>(E.m + c0);
-    const int4 *S4 = reinterpret_cast<const int4 *>(E.sh + c0);
-    const int4 *C4 = reinterpret_cast<const int4 *>(E.cut + c0);
-    const int4 *L4 = reinterpret_cast<const int4 *>(E.ls + c0);
-    const int4 *B4 = reinterpret_cast<const int4 *>(E.bs + c0);
-    const int4 *Z4 = reinterpret_cast<const int4 *>(E.zadd + c0);
-#pragma unroll
-    for (int g = 0; g < 4; g++) {
-        const int4 mv = M4[g], sv = S4[g];
-        const longlong2 ka = K2[2 * g], kb = K2[2 * g + 1];
-        int4 cv = make_int4(0, 0, 0, 0), lv = cv, bv = cv, zv = cv;
-        if (EPI >= kTies) cv = C4[g];
-        if (EPI == kGeneral) {
-            lv = L4[g];
-            bv = B4[g];
-            zv = Z4[g];
-        }
-        const int mm[4] = {mv.x, mv.y, mv.z, mv.w}, ss[4] = {sv.x, sv.y, sv.z, sv.w};
-        const int cc[4] = {cv.x, cv.y, cv.z, cv.w}, ll[4] = {lv.x, lv.y, lv.z, lv.w};
-        const int bb[4] = {bv.x, bv.y, bv.z, bv.w}, zz[4] = {zv.x, zv.y, zv.z, zv.w};
-        const long long kk[4] = {ka.x, ka.y, kb.x, kb.y};
-        int32_t v[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int32_t acc = (int32_t)r[g * 4 + i];
-            if (EPI == kGeneral) {
-                const int32_t a = (int32_t)(((uint32_t)acc << ll[i]) + (uint32_t)bb[i]);
-                long long p = (long long)a * mm[i] + kk[i];
-                p -= (long long)(acc <= cc[i]) << 31;
-                v[i] = (int32_t)(p >> ss[i]) + zz[i];
-            } else {
-                long long p = (long long)acc * mm[i] + kk[i];
-                if (EPI == kTies) p -= (long long)(acc <= cc[i]) << 31;
-                v[i] = ((int32_t)(p >> 32)) >> ss[i];
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            v[i] = min(max(v[i], lo), hi);
-            if (lut) v[i] = (int8_t)lut[v[i] + 128];
-            if (fp) {  // fused residual add: the add's two tables, then its scale and clamp
-                const int rv = (int)(int8_t)(resw[g] >> (8 * i));
-                const int32_t sum = (int32_t)((uint32_t)tabs[v[i] + 128] + (uint32_t)tabs[256 + rv + 128]);
-                v[i] = epilogue_one(sum, fp->add_epi, fp->add_lo, fp->add_hi);
-            }
-        }
-        packed[g] = pack_sat_s8x4(v[0], v[1], v[2], v[3]);
-    }
-    return make_uint4(packed[0], packed[1], packed[2], packed[3]);
-}
 
 // A fused residual add (qnn.c:175-183) runs inside epilogue_chunk on the requantised int32 values:
 // y = clamp(scale(T_conv[v + 128] + T_res[r + 128]) + zp) with the add's scale as requant.cuh
@@ -802,7 +573,7 @@ __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(con
                         uint4 rr = make_uint4(0, 0, 0, 0);  // rows past M read no residual (never stored)
                         if (row < p.M)
                             rr = __ldg(reinterpret_cast<const uint4 *>(p.res + (size_t)row * p.oc + n0 + c0 + ci * 16));
-                        v = epilogue_chunk<EPI>(ra, E, lut, c0 + ci * 16, p.lo, p.hi, &p, sAdd, rr);
+                        v = epilogue_chunk<EPI>(ra, E, lut, c0 + ci * 16, p.lo, p.hi, &p.add, sAdd, rr);
                     } else {
                         v = epilogue_chunk<EPI>(ra, E, lut, c0 + ci * 16, p.lo, p.hi);
                     }
@@ -1108,9 +879,9 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
     if (add) {
         p.add_tab = add->q_dev;
         p.res_side = add->conv_is_b ? 1 : 0;
-        p.add_epi = make_epilogue(0, add->q_host[0], add->q_host[1], add->q_host[2]);
-        p.add_lo = add->q_host[3];
-        p.add_hi = add->q_host[4];
+        p.add.epi = make_epilogue(0, add->q_host[0], add->q_host[1], add->q_host[2]);
+        p.add.lo = add->q_host[3];
+        p.add.hi = add->q_host[4];
         c->fused = true;
     }
     p.box = box;
@@ -1133,22 +904,6 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
     c->smem = layout().total;
     *out = c;
     return 0;
-}
-
-using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiled encoder() {
-    static EncodeTiled fn = nullptr;
-    if (!fn) {
-        void *ptr = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiled>(ptr);
-    }
-    return fn;
 }
 
 int conv_tc_launch(const ConvTc &c, const int8_t *x, int8_t *y, const ConvGeom &g, cudaStream_t s,
@@ -1199,10 +954,10 @@ void conv_tc_free(ConvTc *c) { delete c; }
 
 int conv_tc_error(bool reset) {
     int v = 0;
-    cudaMemcpyFromSymbol(&v, g_conv_tc_error, sizeof(int));
+    cudaMemcpyFromSymbol(&v, g_tc_error, sizeof(int));
     if (reset && v) {
         int z = 0;
-        cudaMemcpyToSymbol(g_conv_tc_error, &z, sizeof(int));
+        cudaMemcpyToSymbol(g_tc_error, &z, sizeof(int));
     }
     return v;
 }

@@ -7,6 +7,7 @@
 #include <mutex>
 #include <numeric>
 
+#include "conv_rows.cuh"
 #include "conv_small.cuh"
 #include "conv_tc.cuh"
 #include "dw.cuh"
@@ -166,8 +167,21 @@ int Engine::prepare() {
                 Requant r{dq + kHead, dq + kHead + g.oc, dq + kHead + 2 * g.oc,
                           o.p[1] ? dconst(o.p[1] - 1) : nullptr, q[13], q[14], q[15]};
                 const uint32_t ta = o.a, tz = o.out;
+                ConvRows *cr = nullptr;
+                int rc = conv_rows_prepare(P.s8(o.b), q, r.post, g, [this](size_t n) { return prep_alloc(n); }, &cr);
+                if (rc) return rc;
+                if (cr) {
+                    std::shared_ptr<ConvRows> keep(cr, conv_rows_free);
+                    st.run = [keep, g, ta, tz](const BatchCtx &B, cudaStream_t s) -> int {
+                        ConvGeom gb = g;
+                        gb.n = g.n * (int)B.images;
+                        return conv_rows_launch(*keep, reinterpret_cast<const int8_t *>(B.ptr[ta]),
+                                                reinterpret_cast<int8_t *>(B.ptr[tz]), gb, s);
+                    };
+                    break;
+                }
                 ConvSmall *sm = nullptr;
-                int rc = conv_small_prepare(P.s8(o.b), q, r.post, g, [this](size_t n) { return prep_alloc(n); }, &sm);
+                rc = conv_small_prepare(P.s8(o.b), q, r.post, g, [this](size_t n) { return prep_alloc(n); }, &sm);
                 if (rc) return rc;
                 if (sm) {
                     std::shared_ptr<ConvSmall> keep(sm, conv_small_free);
@@ -830,7 +844,8 @@ int Engine::run_static(const void *in, void *out) {
 // A device-side wait that gave up (bounded mbarrier waits in the tensor-core kernels) leaves a
 // code in device memory; report it as 2003 and clear it.
 int Engine::device_status() {
-    const int code = conv_tc_error(true);
+    int code = conv_tc_error(true);
+    if (!code) code = conv_rows_error(true);
     if (code) {
         set_error("device wait timed out in the tensor-core conv (site " + std::to_string(code) + ")");
         return 2003;
