@@ -94,9 +94,12 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map
         : "memory");
 }
 
-template <int EPI, int EW>
-__global__ void __launch_bounds__((2 + EW) * 32, 1) conv_rows_kernel(const __grid_constant__ RowsParams p) {
-    constexpr int kParts = EW / 4;
+// 16 epilogue warps (4 per TMEM lane quarter), each owning CHUNKS 16-column chunks of a tile.
+constexpr int kRowsEW = 16;
+
+template <int EPI, int CHUNKS>
+__global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const __grid_constant__ RowsParams p) {
+    constexpr int EW = kRowsEW;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int S = p.stages;
@@ -229,12 +232,21 @@ __global__ void __launch_bounds__((2 + EW) * 32, 1) conv_rows_kernel(const __gri
         const int e = warp - 2;
         const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31 (warp id % 4 rule)
         const int part = e >> 2;       // column part [part * box, part * box + box) of the tile
-        const int c0 = part * p.box;
-        const int chunks = p.box / 16;
+        constexpr int kBox = CHUNKS * 16;
+        const int c0 = part * kBox;
         const uint8_t *lut = p.post ? sLut : nullptr;
-        const int swz_row = p.swz == 3 ? (lane & 7) : p.swz == 2 ? ((lane >> 1) & 3) : p.swz == 1 ? ((lane >> 2) & 1) : 0;
-        const size_t wsb = rows_warp_stage(p.box);
+        const int swz_row = kBox == 128 ? (lane & 7) : kBox == 64 ? ((lane >> 1) & 3) : kBox == 32 ? ((lane >> 2) & 1) : 0;
+        const size_t wsb = rows_warp_stage(kBox);
         uint8_t *wstage0 = sOut + (size_t)e * 2 * wsb;
+        // output pixel (within the group) and first channel of each chunk: fixed for the kernel
+        int jj[CHUNKS], oo[CHUNKS];
+#pragma unroll
+        for (int ci = 0; ci < CHUNKS; ci++) {
+            jj[ci] = (c0 + ci * 16) / p.oc;
+            oo[ci] = c0 + ci * 16 - jj[ci] * p.oc;
+        }
+        // output columns whose taps all lie inside the image: [ox_lo, ox_hi]
+        const int ox_lo = (p.pl + p.s - 1) / p.s, ox_hi = (p.iw - p.kw + p.pl) / p.s;
         int lt = 0;
         for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, lt++) {
             const int img = t / per_image, rem = t - img * per_image;
@@ -257,30 +269,42 @@ __global__ void __launch_bounds__((2 + EW) * 32, 1) conv_rows_kernel(const __gri
                     const int iy = p.s * oy - p.pt + ky;
                     rmask |= (iy < 0 || iy >= p.ih) ? 1 << ky : 0;
                 }
+                if (oy >= p.oh) rmask = 0;  // past the image: never stored
+                const bool edge_cols = ox0 < ox_lo || ox0 + p.G - 1 > ox_hi;
+                auto chunk = [&](const uint32_t(&rr)[16], int ci) {
+                    uint32_t a[16];
+#pragma unroll
+                    for (int i = 0; i < 16; i++) a[i] = rr[i];
+                    if (rmask | (edge_cols ? 1 : 0)) {
+                        const int ox = ox0 + jj[ci];
+                        int cmask = 0;
+                        for (int kx = 0; kx < p.kw; kx++) {
+                            const int ix = p.s * ox - p.pl + kx;
+                            cmask |= (ix < 0 || ix >= p.iw) ? 1 << kx : 0;
+                        }
+                        if ((rmask | cmask) && ox < p.ow) {
+                            const int32_t *cr = p.corr + (size_t)((rmask << p.kw) | cmask) * p.oc + oo[ci];
+#pragma unroll
+                            for (int i = 0; i < 16; i++) a[i] = (uint32_t)((int32_t)a[i] + __ldg(cr + i));
+                        }
+                    }
+                    const uint4 v = epilogue_chunk<EPI>(a, E, lut, oo[ci], p.lo, p.hi);
+                    st_shared16(smem_u32(stage + (size_t)lane * kBox + ((ci ^ swz_row) << 4)), v);
+                };
                 const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.bn + c0);
                 uint32_t ra[16], rb[16];
                 tmem_ld16_nowait(taddr, ra);
                 tmem_wait_ld(ra);
-                for (int ci = 0; ci < chunks; ci++) {
-                    const bool more = ci + 1 < chunks;
-                    if (more) tmem_ld16_nowait(taddr + (ci + 1) * 16, rb);
-                    const int c = c0 + ci * 16, j = c / p.oc, oc0 = c - j * p.oc;
-                    const int ox = ox0 + j;
-                    int cmask = 0;
-                    for (int kx = 0; kx < p.kw; kx++) {
-                        const int ix = p.s * ox - p.pl + kx;
-                        cmask |= (ix < 0 || ix >= p.iw) ? 1 << kx : 0;
-                    }
-                    if ((rmask | cmask) && oy < p.oh && ox < p.ow) {
-                        const int32_t *cr = p.corr + (size_t)((rmask << p.kw) | cmask) * p.oc + oc0;
 #pragma unroll
-                        for (int i = 0; i < 16; i++) ra[i] = (uint32_t)((int32_t)ra[i] + __ldg(cr + i));
+                for (int ci = 0; ci < CHUNKS; ci += 2) {
+                    if (ci + 1 < CHUNKS) tmem_ld16_nowait(taddr + (ci + 1) * 16, rb);
+                    chunk(ra, ci);
+                    if (ci + 1 < CHUNKS) {
+                        tmem_wait_ld(rb);
+                        if (ci + 2 < CHUNKS) tmem_ld16_nowait(taddr + (ci + 2) * 16, ra);
+                        chunk(rb, ci + 1);
+                        if (ci + 2 < CHUNKS) tmem_wait_ld(ra);
                     }
-                    const uint4 v = epilogue_chunk<EPI>(ra, E, lut, oc0, p.lo, p.hi);
-                    st_shared16(smem_u32(stage + (size_t)lane * p.box + ((ci ^ swz_row) << 4)), v);
-                    if (more) tmem_wait_ld(rb);
-#pragma unroll
-                    for (int q = 0; q < 16; q++) ra[q] = rb[q];
                 }
             }
             tc_fence_before();
@@ -316,7 +340,7 @@ struct ConvRows {
     RowsParams p{};
     size_t smem = 0;
     int epi_mode = kGeneral;
-    int epilogue_warps = 16;
+    int chunks = 4;  // 16-column chunks per epilogue warp
 };
 
 int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *post_dev, const ConvGeom &g,
@@ -343,11 +367,9 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
     }
     if (!G) return 0;
     const int bn = G * g.oc;
-    const int ew = bn % 64 == 0 ? 16 : 8;
-    const int parts = ew / 4;
-    if (bn % (16 * parts) != 0) return 0;
-    const int box = bn / parts;
-    if (box != 16 && box != 32 && box != 64 && box != 128) return 0;  // staging swizzle spans
+    const int ew = kRowsEW;
+    const int box = bn / (ew / 4);  // columns per epilogue warp: 16, 32 or 64
+    if (box != 16 && box != 32 && box != 64) return 0;
     const int span = o + s * g.ic * (G - 1) + g.kw * g.ic;
     const int ksteps = (span + 31) / 32;
     const int out_bytes = (int)(2 * ew * rows_warp_stage(box));
@@ -420,9 +442,11 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
         auto allow = [](auto fn) {
             return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsMaxSmem) == cudaSuccess;
         };
-        if (!allow(conv_rows_kernel<kRelu, 16>) || !allow(conv_rows_kernel<kTies, 16>) ||
-            !allow(conv_rows_kernel<kGeneral, 16>) || !allow(conv_rows_kernel<kRelu, 8>) ||
-            !allow(conv_rows_kernel<kTies, 8>) || !allow(conv_rows_kernel<kGeneral, 8>))
+        if (!allow(conv_rows_kernel<kRelu, 1>) || !allow(conv_rows_kernel<kTies, 1>) ||
+            !allow(conv_rows_kernel<kGeneral, 1>) || !allow(conv_rows_kernel<kRelu, 2>) ||
+            !allow(conv_rows_kernel<kTies, 2>) || !allow(conv_rows_kernel<kGeneral, 2>) ||
+            !allow(conv_rows_kernel<kRelu, 4>) || !allow(conv_rows_kernel<kTies, 4>) ||
+            !allow(conv_rows_kernel<kGeneral, 4>))
             return 2001;
         attr_set = true;
     }
@@ -457,7 +481,7 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
     p.tmem_cols = cols;
     c->smem = L.total;
     c->epi_mode = epi_mode;
-    c->epilogue_warps = ew;
+    c->chunks = box / 16;
     *out = c;
     return 0;
 }
@@ -495,15 +519,16 @@ int conv_rows_launch(const ConvRows &c, const int8_t *x, int8_t *y, const ConvGe
             return 2001;
     }
     const int grid = std::min(g_rows_sm_count, p.tiles);
-    auto go = [&](auto ew) {
-        constexpr int EWv = decltype(ew)::value;
-        constexpr int T = (2 + EWv) * 32;
-        if (c.epi_mode == kRelu) conv_rows_kernel<kRelu, EWv><<<grid, T, c.smem, s>>>(p);
-        else if (c.epi_mode == kTies) conv_rows_kernel<kTies, EWv><<<grid, T, c.smem, s>>>(p);
-        else conv_rows_kernel<kGeneral, EWv><<<grid, T, c.smem, s>>>(p);
+    constexpr int T = (2 + kRowsEW) * 32;
+    auto go = [&](auto chunks) {
+        constexpr int CH = decltype(chunks)::value;
+        if (c.epi_mode == kRelu) conv_rows_kernel<kRelu, CH><<<grid, T, c.smem, s>>>(p);
+        else if (c.epi_mode == kTies) conv_rows_kernel<kTies, CH><<<grid, T, c.smem, s>>>(p);
+        else conv_rows_kernel<kGeneral, CH><<<grid, T, c.smem, s>>>(p);
     };
-    if (c.epilogue_warps == 16) go(std::integral_constant<int, 16>{});
-    else go(std::integral_constant<int, 8>{});
+    if (c.chunks == 4) go(std::integral_constant<int, 4>{});
+    else if (c.chunks == 2) go(std::integral_constant<int, 2>{});
+    else go(std::integral_constant<int, 1>{});
     return 0;
 }
 

@@ -193,66 +193,79 @@ struct AddEpi {
     int lo, hi;
 };
 
-// Requantise 16 accumulators (columns c0..c0+15 of one row), clamp to [lo, hi] and pack them as
-// int8 (the clamp is two integer min/max per value; byte-SIMD min/max would be emulated). With
-// `fp`, the residual add follows: y = clamp(scale(tabs[v + 128] + tabs[256 + r + 128])) with r
-// the residual bytes in `res`.
+// Requantise accumulators r[4g..4g+3] (columns c0+4g.. of one row) and pack them as int8: exact
+// scale, clamp to [lo, hi], then the post table (LUT 1: always, 2: when `lut` is set) and the
+// residual add (ADD). HI = false leaves the upper clamp to the saturating pack (hi == 127 without
+// a lookup after it).
+template <int EPI, int LUT, bool ADD, bool HI>
+__device__ __forceinline__ uint32_t epilogue_group(const uint32_t (&r)[16], int g, const EpiSoA &E, const uint8_t *lut,
+                                                   int c0, int lo, int hi, const AddEpi *fp, const int32_t *tabs,
+                                                   uint32_t resw) {
+    const int4 mv = reinterpret_cast<const int4 *>(E.m + c0)[g], sv = reinterpret_cast<const int4 *>(E.sh + c0)[g];
+    const longlong2 ka = reinterpret_cast<const longlong2 *>(E.k + c0)[2 * g];
+    const longlong2 kb = reinterpret_cast<const longlong2 *>(E.k + c0)[2 * g + 1];
+    int4 cv = make_int4(0, 0, 0, 0), lv = cv, bv = cv, zv = cv;
+    if (EPI >= kTies) cv = reinterpret_cast<const int4 *>(E.cut + c0)[g];
+    if (EPI == kGeneral) {
+        lv = reinterpret_cast<const int4 *>(E.ls + c0)[g];
+        bv = reinterpret_cast<const int4 *>(E.bs + c0)[g];
+        zv = reinterpret_cast<const int4 *>(E.zadd + c0)[g];
+    }
+    const int mm[4] = {mv.x, mv.y, mv.z, mv.w}, ss[4] = {sv.x, sv.y, sv.z, sv.w};
+    const int cc[4] = {cv.x, cv.y, cv.z, cv.w}, ll[4] = {lv.x, lv.y, lv.z, lv.w};
+    const int bb[4] = {bv.x, bv.y, bv.z, bv.w}, zz[4] = {zv.x, zv.y, zv.z, zv.w};
+    const long long kk[4] = {ka.x, ka.y, kb.x, kb.y};
+    int32_t v[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int32_t acc = (int32_t)r[g * 4 + i];
+        if (EPI == kGeneral) {
+            const int32_t a = (int32_t)(((uint32_t)acc << ll[i]) + (uint32_t)bb[i]);
+            long long p = (long long)a * mm[i] + kk[i];
+            p -= (long long)(acc <= cc[i]) << 31;
+            v[i] = (int32_t)(p >> ss[i]) + zz[i];
+        } else {
+            long long p = (long long)acc * mm[i] + kk[i];
+            if (EPI == kTies) p -= (long long)(acc <= cc[i]) << 31;
+            v[i] = ((int32_t)(p >> 32)) >> ss[i];
+        }
+        v[i] = max(v[i], lo);
+        if (HI || LUT || ADD) v[i] = min(v[i], hi);
+        if (LUT == 1 || (LUT == 2 && lut)) v[i] = (int8_t)lut[v[i] + 128];
+        if (ADD) {  // fused residual add: the add's two tables, then its scale and clamp
+            const int rv = (int)(int8_t)(resw >> (8 * i));
+            const int32_t sum = (int32_t)((uint32_t)tabs[v[i] + 128] + (uint32_t)tabs[256 + rv + 128]);
+            v[i] = epilogue_one(sum, fp->epi, fp->lo, fp->hi);
+        }
+    }
+    return pack_sat_s8x4(v[0], v[1], v[2], v[3]);
+}
+
+// Requantise 16 accumulators (columns c0..c0+15 of one row) and pack them as int8. With `fp`, the
+// residual add follows: y = clamp(scale(tabs[v + 128] + tabs[256 + r + 128])) with r the residual
+// bytes in `res`. The layer's variant (table, add, upper clamp) is chosen once per chunk -- the
+// conditions are launch parameters, uniform over the kernel -- so each value runs only the steps
+// its layer needs.
 template <int EPI>
 __device__ __forceinline__ uint4 epilogue_chunk(const uint32_t (&r)[16], const EpiSoA &E, const uint8_t *lut, int c0,
                                                 int lo, int hi, const AddEpi *fp = nullptr, const int32_t *tabs = nullptr,
                                                 uint4 res = make_uint4(0, 0, 0, 0)) {
     const uint32_t resw[4] = {res.x, res.y, res.z, res.w};
-    uint32_t packed[4];
-    const longlong2 *K2 = reinterpret_cast<const longlong2 *>(E.k + c0);
-    const int4 *M4 = reinterpret_cast<const int4 *>(E.m + c0);
-    const int4 *S4 = reinterpret_cast<const int4 *>(E.sh + c0);
-    const int4 *C4 = reinterpret_cast<const int4 *>(E.cut + c0);
-    const int4 *L4 = reinterpret_cast<const int4 *>(E.ls + c0);
-    const int4 *B4 = reinterpret_cast<const int4 *>(E.bs + c0);
-    const int4 *Z4 = reinterpret_cast<const int4 *>(E.zadd + c0);
-#pragma unroll
-    for (int g = 0; g < 4; g++) {
-        const int4 mv = M4[g], sv = S4[g];
-        const longlong2 ka = K2[2 * g], kb = K2[2 * g + 1];
-        int4 cv = make_int4(0, 0, 0, 0), lv = cv, bv = cv, zv = cv;
-        if (EPI >= kTies) cv = C4[g];
-        if (EPI == kGeneral) {
-            lv = L4[g];
-            bv = B4[g];
-            zv = Z4[g];
-        }
-        const int mm[4] = {mv.x, mv.y, mv.z, mv.w}, ss[4] = {sv.x, sv.y, sv.z, sv.w};
-        const int cc[4] = {cv.x, cv.y, cv.z, cv.w}, ll[4] = {lv.x, lv.y, lv.z, lv.w};
-        const int bb[4] = {bv.x, bv.y, bv.z, bv.w}, zz[4] = {zv.x, zv.y, zv.z, zv.w};
-        const long long kk[4] = {ka.x, ka.y, kb.x, kb.y};
-        int32_t v[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int32_t acc = (int32_t)r[g * 4 + i];
-            if (EPI == kGeneral) {
-                const int32_t a = (int32_t)(((uint32_t)acc << ll[i]) + (uint32_t)bb[i]);
-                long long p = (long long)a * mm[i] + kk[i];
-                p -= (long long)(acc <= cc[i]) << 31;
-                v[i] = (int32_t)(p >> ss[i]) + zz[i];
-            } else {
-                long long p = (long long)acc * mm[i] + kk[i];
-                if (EPI == kTies) p -= (long long)(acc <= cc[i]) << 31;
-                v[i] = ((int32_t)(p >> 32)) >> ss[i];
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            v[i] = min(max(v[i], lo), hi);
-            if (lut) v[i] = (int8_t)lut[v[i] + 128];
-            if (fp) {  // fused residual add: the add's two tables, then its scale and clamp
-                const int rv = (int)(int8_t)(resw[g] >> (8 * i));
-                const int32_t sum = (int32_t)((uint32_t)tabs[v[i] + 128] + (uint32_t)tabs[256 + rv + 128]);
-                v[i] = epilogue_one(sum, fp->epi, fp->lo, fp->hi);
-            }
-        }
-        packed[g] = pack_sat_s8x4(v[0], v[1], v[2], v[3]);
+    uint32_t o[4];
+#define UQ_EPI_GROUPS(L, A, H)                                                                       \
+    _Pragma("unroll") for (int g = 0; g < 4; g++) o[g] =                                             \
+        epilogue_group<EPI, L, A, H>(r, g, E, lut, c0, lo, hi, fp, tabs, resw[g])
+    if (fp) {
+        UQ_EPI_GROUPS(2, true, true);
+    } else if (lut) {
+        UQ_EPI_GROUPS(1, false, true);
+    } else if (hi < 127) {
+        UQ_EPI_GROUPS(0, false, true);
+    } else {
+        UQ_EPI_GROUPS(0, false, false);
     }
-    return make_uint4(packed[0], packed[1], packed[2], packed[3]);
+#undef UQ_EPI_GROUPS
+    return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
