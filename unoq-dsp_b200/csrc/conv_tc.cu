@@ -107,8 +107,10 @@ struct Params {
     int tab_bytes;             // size of the band table
     int epi_mode;              // EpiMode
     int n_acc;                 // TMEM accumulators in rotation (2 or 4)
+    int fold;                  // tiles in flight per epilogue warp group: EW/4 warps per lane quarter split
+                               // into column parts (bn / box) x fold tile phases (TMA-store path)
     int store_tma;             // 1: staged tile leaves by TMA tensor store; 0: cooperative stores
-    int box;                   // TMA store box: columns of one epilogue warp (max(16, bn / 2)) x 32 rows
+    int box;                   // TMA store box: columns of one epilogue warp x 32 rows
     int out_bytes;             // output staging: per-warp double buffers (TMA) or two whole tiles
     // Fused residual add (plan code 18 consuming this conv's output; 0 / null when not fused):
     // y = clamp(scale(T_conv[v + 128] + T_res[r + 128]) + zp) with the add's two 256-entry tables.
@@ -206,7 +208,7 @@ __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(con
         }
         for (int a = 0; a < 4; a++) {
             mbar_init(smem_u32(tfull + a), 1);
-            mbar_init(smem_u32(tempty + a), kEpilogueWarps);
+            mbar_init(smem_u32(tempty + a), kEpilogueWarps / p.fold);
         }
         mbar_init(smem_u32(bfull), kProducerWarps);
         mbar_init(smem_u32(drain), 1);
@@ -542,19 +544,24 @@ __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(con
         unsigned round = 0;
         int lt = 0;
         if (p.store_tma) {
-            // Each warp owns rows 32*quarter.. and the column half [half*box, half*box + box) of every
-            // tile: it stages them in its own double buffer (swizzled like the box) and stores them
-            // with its own TMA store, so no epilogue warp ever waits for another.
-            const int c0 = half * p.box;
+            // Each warp owns rows 32*quarter.. and one column part [c0, c0 + box) of every fold-th
+            // tile (phase ph): it stages them in its own double buffer (swizzled like the box) and
+            // stores them with its own TMA store, so no epilogue warp ever waits for another. When a
+            // tile has fewer column parts than warps per lane quarter (narrow N tiles), the spare
+            // warps take the following tiles of the accumulator ring instead of idling.
+            const int nparts = kParts / p.fold;
+            const int c0 = (half % nparts) * p.box, ph = half / nparts;
             const int my_chunks = c0 < cols ? (min(p.box, cols - c0) + 15) / 16 : 0;
             const int swz_row = p.swz == 3 ? (lane & 7) : p.swz == 2 ? ((lane >> 1) & 3) : p.swz == 1 ? ((lane >> 2) & 1) : 0;
             const size_t wsb = warp_stage_bytes(p.box);
             uint8_t *wstage0 = sOut + (size_t)e * 2 * wsb;
-            for (int mt = blockIdx.x; mt < m_tiles; mt += gridDim.x, lt++) {
+            int k = 0;  // tiles this warp has staged
+            lt = ph;
+            for (int mt = blockIdx.x + ph * gridDim.x; mt < m_tiles; mt += p.fold * gridDim.x, lt += p.fold, k++) {
                 const int acc = lt % p.n_acc;
                 if (!mbar_wait(smem_u32(tfull + acc), (uint32_t)((lt / p.n_acc) & 1), abort, 105)) break;
                 tc_fence_after();
-                uint8_t *stage = wstage0 + (size_t)(lt & 1) * wsb;
+                uint8_t *stage = wstage0 + (size_t)(k & 1) * wsb;
                 // this buffer's previous store (two tiles back) must have been read out
                 if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
                 __syncwarp();
@@ -734,7 +741,9 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
     // epilogue warps: 16 for pointwise convs (4 producer warps leave room; more warps hide the
     // epilogue's latency), 8 for the other modes (8 producer warps)
     const int ew = mode == kPointwise ? 16 : 8;
-    const int box = std::max(16, bn / (ew / 4));
+    // columns per epilogue warp: up to 64 (a 64-byte TMA box), fewer warps per tile for narrow N
+    // tiles (the spare ones take other tiles, see fold), so fewer per-warp, per-tile fixed costs
+    const int box = std::max(std::min(bn, 64), bn / (ew / 4));
     const int out_bytes = store_tma ? (int)(2 * ew * warp_stage_bytes(box)) : (int)(2 * out_stride(bn));
     auto layout = [&]() {
         return Layout(stages, kc, bn, mode == kBand ? (int)bg.bytes() : 0, nbands, mode == kBand ? bg.fill_bytes : 0,
@@ -885,6 +894,8 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
         c->fused = true;
     }
     p.box = box;
+    // narrow N tiles: spare epilogue warps of each lane quarter take alternate tiles (divides n_acc)
+    p.fold = store_tma ? (ew / 4) / ((bn + box - 1) / box) : 1;
     p.out_bytes = out_bytes;
     p.swz = p.box == 128 ? 3 : p.box == 64 ? 2 : p.box == 32 ? 1 : 0;
     p.mode = mode;
