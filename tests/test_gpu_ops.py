@@ -116,3 +116,16 @@ def test_row_gemm_conv_tiles_and_edges(native, oracle, monkeypatch, x_shape, oc,
     monkeypatch.setenv("UNOQ_CONV_ROWS", "0")
     with NativeSession(native, plan) as s:
         np.testing.assert_array_equal(s.run(x, images), expect)
+
+
+@pytest.mark.parametrize("padding", ["same", (2, 0, 1, 3)])
+def test_gather_mode_conv_wide_rows(native, oracle, padding):
+    """Input rows too wide for the band path (32 KB each) take the tensor-core conv's per-tap
+    gather, whose taps outside the image are written as the zero point directly."""
+    from unoq_dsp import synth
+    rng = np.random.default_rng(77)
+    plan, xs, _ = synth.single_conv_plan(rng, (1, 9, 512, 64), 32, (3, 3), (1, 1), xq=(0.02, 21), padding=padding)
+    images = 2
+    x = rng.integers(-128, 128, size=(images,) + xs[1:], dtype=np.int64).astype(np.int8)
+    with NativeSession(native, plan) as s:
+        np.testing.assert_array_equal(s.run(x, images), oracle.run(plan, x, images))

@@ -10,8 +10,8 @@
 //   * A (warps 0-3): the im2col rows of a tile, 128 reduction bytes per pipeline stage, built
 //     straight into the swizzled layout.
 //       - 16-byte channel blocks (ic % 16 == 0): cp.async per (pixel, 16 channels); taps outside
-//         the image copy 16 bytes of the input zero point from a tiny global fill row -- the
-//         value the reference feeds its dot product there (qnn.c:1166-1168) -- so no border
+//         the image get 16 bytes of the input zero point by a plain shared store -- the value
+//         the reference feeds its dot product there (qnn.c:1166-1168) -- so no border
 //         correction is needed. A warp signals a stage a few stages after issuing it, once its
 //         copies have landed, so several stages of copies stay in flight per thread.
 //       - other channel counts (the 3-channel RGB stem, ic = 8): the input rows a tile touches
@@ -82,7 +82,6 @@ struct Params {
     const EpiChan *epi;        // [n_tiles * BN]
     const uint8_t *post;       // 256 bytes or null
     const int *tab;            // band mode: chunk taps (ic % 16 == 0) or word sources (else), see conv_tc_prepare
-    const int8_t *fill;        // 16 bytes of the input zero point
     long long x_bytes;         // bytes of the whole (batched) input tensor
     int M;                     // total output pixels
     FastDiv f_ow, f_img;       // division by ow and by oh*ow (pixel index -> n, oy, ox)
@@ -265,6 +264,8 @@ __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(con
         if (p.mode != kBand) {
             const int j = t & 7;    // 16-byte chunk of the 128-byte stage row
             const int r0 = t >> 3;  // rows r0 + kRowStep i
+            const uint32_t fillw = 0x01010101u * (uint32_t)(uint8_t)p.xzp;
+            const uint4 fill16 = make_uint4(fillw, fillw, fillw, fillw);
             // Each stage's copies are tracked per thread with cp.async groups; a warp signals
             // stage `it - lag` once all its lanes have seen that group land (one barrier arrival
             // per warp). The lag keeps up to lag + 1 stages of copies in flight per thread.
@@ -317,9 +318,13 @@ __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(con
                                 const uint32_t dst = stage + (r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4);
                                 if (!rvalid[i]) continue;
                                 const int iy = ry[i] + dy, ix = rx[i] + dx;
-                                const bool in = iy >= 0 && ix >= 0 && iy < p.ih && ix < p.iw;
-                                cp_async16(dst, in ? (const void *)(rbase[i] + ((size_t)iy * p.iw + ix) * p.ic + c)
-                                                   : (const void *)p.fill);
+                                // taps outside the image hold the zero point, stored directly: a
+                                // shared global source would put every CTA's border copies on one
+                                // L2 slice
+                                if (iy >= 0 && ix >= 0 && iy < p.ih && ix < p.iw)
+                                    cp_async16(dst, rbase[i] + ((size_t)iy * p.iw + ix) * p.ic + c);
+                                else
+                                    st_shared16(dst, fill16);
                             }
                         }
                     }
@@ -834,17 +839,13 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
             }
         }
     }
-    int8_t fill[16];
-    std::memset(fill, xzp, sizeof(fill));
     void *dw = alloc(wt.size());
     void *de = alloc(epi.size() * sizeof(EpiChan));
     void *dt = alloc(tab.size() * sizeof(int));
-    void *df = alloc(sizeof(fill));
-    if (!dw || !de || !dt || !df) return 2001;
+    if (!dw || !de || !dt) return 2001;
     if (cudaMemcpy(dw, wt.data(), wt.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMemcpy(de, epi.data(), epi.size() * sizeof(EpiChan), cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemcpy(dt, tab.data(), tab.size() * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemcpy(df, fill, sizeof(fill), cudaMemcpyHostToDevice) != cudaSuccess)
+        cudaMemcpy(dt, tab.data(), tab.size() * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess)
         return 2001;
     if (!g_sm_count) {
         int dev = 0;
@@ -871,7 +872,6 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
     p.epi = static_cast<const EpiChan *>(de);
     p.post = post_dev;
     p.tab = static_cast<const int *>(dt);
-    p.fill = static_cast<const int8_t *>(df);
     p.ih = g.ih, p.iw = g.iw, p.ic = g.ic, p.oh = g.oh, p.ow = g.ow, p.oc = g.oc;
     p.f_ow = FastDiv(g.ow);
     p.f_img = FastDiv(g.oh * g.ow);
