@@ -398,13 +398,25 @@ def bench_model(lib, dist, name, global_batch, steps, warmup, peaks, want_roofli
         lib.ug_close(handle)
 
 
-def conv_traffic_per_image():
-    """DRAM bytes per image of the conv launches of one MobileNetV4 step, from the committed ncu
-    launch-list summary (profiles/mnv4_b512_launches.md); None when absent."""
+TRAFFIC_PROFILES = {"mobilenetv4-small": "mnv4_b512_launches.md", "yolo26n-320": "yolo26n_b128_launches.md"}
+
+
+def conv_traffic_per_image(model="mobilenetv4-small"):
+    """DRAM bytes per image of the conv launches of one step of `model`, from the committed ncu
+    launch-list summary under profiles/; None when absent."""
     import re
-    p = ROOT / "profiles" / "mnv4_b512_launches.md"
+    p = ROOT / "profiles" / TRAFFIC_PROFILES[model]
     m = re.search(r"conv_dram_bytes_per_image = (\d+)", p.read_text()) if p.is_file() else None
     return int(m.group(1)) if m else None
+
+
+def attach_traffic(roof, model, images):
+    """Fill roofline.traffic of the conv family from the model's committed launch list."""
+    per_image = conv_traffic_per_image(model)
+    if roof is not None and per_image and roof.get("kernel") == "conv":
+        roof["traffic"] = per_image * images
+        roof["traffic_source"] = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of the conv launches of one step "
+                                  f"(profiles/{TRAFFIC_PROFILES[model]}), scaled by images")
 
 
 def load_peaks():
@@ -425,6 +437,8 @@ def main():
     ap.add_argument("--yolo-batch", type=int, default=MODELS["yolo26n-320"]["batch"])
     ap.add_argument("--no-yolo", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--yolo-only", action="store_true",
+                    help="profiling aid: run only the YOLO26n section and print its fields")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -481,15 +495,22 @@ def main():
     if lib.ug_set_device(dist.local) != 0:
         raise SystemExit(f"cannot select CUDA device {dist.local}")
     peaks = load_peaks()
+    if args.yolo_only:
+        yolo = bench_model(lib, dist, "yolo26n-320", args.yolo_batch, args.steps, args.warmup, peaks, True, detect=True)
+        dist.close()
+        if rank == 0:
+            print(json.dumps({"model": "yolo26n-320", **{k: yolo[k] for k in ("value", "ms_per_step", "e2e", "detect_e2e",
+                                                                              "roofline", "kernels_per_step")}}))
+        return
     res = bench_model(lib, dist, "mobilenetv4-small", args.global_batch, args.steps, args.warmup, peaks, True)
     yolo = None
     if not args.no_yolo:
         yolo = bench_model(lib, dist, "yolo26n-320", args.yolo_batch, args.steps, args.warmup, peaks, True, detect=True)
     cpu = None
     if pool is not None:
-        # bounded sample: about 20 s of CPU work in total, spread over every host core
+        # bounded sample: about 25 s of CPU work in total, spread over every host core
         _, _, t1 = reference_throughput(MODELS["mobilenetv4-small"]["shape"], 1, cores, pool)
-        per_proc = max(1, min(16, int(20.0 / (cores * max(t1, 1e-3)))))
+        per_proc = max(1, min(32, int(25.0 / (cores * max(t1, 1e-3)))))
         value, wall, _ = reference_throughput(MODELS["mobilenetv4-small"]["shape"], per_proc, cores, pool)
         pool.close()
         cpu = {"value": round(value, 3), "unit": "images/s", "cores": cores, "kind": "reference",
@@ -502,11 +523,10 @@ def main():
     roof = res["roofline"]
     if roof is not None:
         roof["peak_source"] = peaks["source"]
-        per_image = conv_traffic_per_image()
-        if per_image and roof.get("kernel") == "conv":
-            roof["traffic"] = per_image * res["per_gpu_batch"]
-            roof["traffic_source"] = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of the conv launches of one "
-                                      "step at batch 512 (profiles/mnv4_b512_launches.md), scaled by images")
+        attach_traffic(roof, "mobilenetv4-small", res["per_gpu_batch"])
+    if yolo is not None and yolo["roofline"] is not None:
+        yolo["roofline"]["peak_source"] = peaks["source"]
+        attach_traffic(yolo["roofline"], "yolo26n-320", yolo["per_gpu_batch"])
     line = {
         "metric": METRIC, "value": round(res["value"], 2), "unit": "images/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(res["ms_per_step"], 4), "higher_is_better": True,
