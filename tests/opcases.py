@@ -278,6 +278,12 @@ def all_cases(scale=1):
         ("conv_rows_rgb_s1", lambda r: conv_case(r, (1, 6 * s, 16, 3), 16, (3, 3), (1, 1), xq=(0.02, 4))),
         ("conv_rows_ic4_post", lambda r: conv_post_case(r, (1, 7 * s, 20, 4), 16, (3, 3), (2, 2))),
         ("conv_rows_ic1", lambda r: conv_case(r, (1, 5 * s, 48, 1), 32, (3, 3), (2, 2), act="relu6")),
+        # input channels a multiple of 32 (the per-tap TMA path): dilation, 32 / 64 / 128-byte
+        # channel chunks, several N tiles, a 2 x 3 kernel with a post table
+        ("conv_taps_ic64_dil2", lambda r: conv_case(r, (1, 9 * s, 11, 64), 32, (3, 3), (1, 1), dilation=(2, 2))),
+        ("conv_taps_ic96_s2", lambda r: conv_case(r, (1, 11 * s, 9, 96), 48, (3, 3), (2, 2), xq=(0.03, -40))),
+        ("conv_taps_ic128_oc320", lambda r: conv_case(r, (1, 5 * s, 6, 128), 320, (3, 3), (1, 1), act="none")),
+        ("conv_taps_2x3_post", lambda r: conv_post_case(r, (1, 7 * s, 8, 32), 16, (2, 3), (1, 1))),
         ("conv_ic8_band", lambda r: conv_case(r, (1, 6 * s, 10, 8), 24, (3, 3), (1, 1))),
         ("conv_rgb_odd_width", lambda r: conv_case(r, (1, 9 * s, 13, 3), 16, (3, 3), (2, 2), xq=(0.02, -5))),
         ("conv_ic8_small", lambda r: conv_case(r, (1, 9 * s, 11, 8), 16, (3, 3), (1, 1))),

@@ -129,3 +129,18 @@ def test_gather_mode_conv_wide_rows(native, oracle, padding):
     x = rng.integers(-128, 128, size=(images,) + xs[1:], dtype=np.int64).astype(np.int8)
     with NativeSession(native, plan) as s:
         np.testing.assert_array_equal(s.run(x, images), oracle.run(plan, x, images))
+
+
+TAP_CASES = [n for n in NAMES if n.startswith("conv_taps") or n in ("conv_3x3_s1", "conv_3x3_s2", "conv_wide_k",
+                                                                      "conv_post_lut")]
+
+
+@pytest.mark.parametrize("name", TAP_CASES)
+def test_tap_tma_conv_on_every_eligible_case(name, native, golden_ops, monkeypatch):
+    """The per-tap TMA conv (taken by default only for 128-byte channel chunks) on every op case
+    with ic % 32 == 0: 32 / 64 / 128-byte chunks, dilation, odd sizes, post table."""
+    monkeypatch.setenv("UNOQ_CONV_TAPS", "all")
+    plan = golden_ops[f"{name}/plan"].tobytes()
+    x = golden_ops[f"{name}/x"]
+    with NativeSession(native, plan) as s:
+        np.testing.assert_array_equal(s.run(x), golden_ops[f"{name}/y"])

@@ -8,6 +8,7 @@
 #include <numeric>
 
 #include "conv_rows.cuh"
+#include "conv_taps.cuh"
 #include "conv_small.cuh"
 #include "conv_tc.cuh"
 #include "dw.cuh"
@@ -222,6 +223,19 @@ int Engine::prepare() {
                             break;
                         }
                     }
+                }
+                ConvTaps *ct = nullptr;
+                rc = conv_taps_prepare(P.s8(o.b), q, r.post, g, [this](size_t n) { return prep_alloc(n); }, &ct);
+                if (rc) return rc;
+                if (ct) {
+                    std::shared_ptr<ConvTaps> keep(ct, conv_taps_free);
+                    st.run = [keep, g, ta, tz](const BatchCtx &B, cudaStream_t s) -> int {
+                        ConvGeom gb = g;
+                        gb.n = g.n * (int)B.images;
+                        return conv_taps_launch(*keep, reinterpret_cast<const int8_t *>(B.ptr[ta]),
+                                                reinterpret_cast<int8_t *>(B.ptr[tz]), gb, s);
+                    };
+                    break;
                 }
                 rc = conv_tc_prepare(P.s8(o.b), q, r.post, g, [this](size_t n) { return prep_alloc(n); }, &tc);
                 if (rc) return rc;
@@ -846,6 +860,7 @@ int Engine::run_static(const void *in, void *out) {
 int Engine::device_status() {
     int code = conv_tc_error(true);
     if (!code) code = conv_rows_error(true);
+    if (!code) code = conv_taps_error(true);
     if (code) {
         set_error("device wait timed out in the tensor-core conv (site " + std::to_string(code) + ")");
         return 2003;
