@@ -238,7 +238,9 @@ int dw_prepare(const int8_t *w, const int32_t *q, const uint8_t *post_dev, const
         for (auto &e : epi) e.sh = e.sh >= 32 ? e.sh - 32 : 0;
     // Tile: 8 columns; the whole image height when it is at most 32 rows, else 16 rows.
     const int rg = g.oh <= 32 ? (g.oh + kR - 1) / kR : 8;
-    int cb = 64;
+    // channels per block: 32 for stride 1 (smaller blocks, more of them resident: 7-10% faster on
+    // the 14x14 and 28x28 layers), 64 for stride 2 (wider halo reuse; 32 was up to 45% slower)
+    int cb = S == 1 ? 32 : 64;
     while (cb > 16 && (C % cb != 0 || cb * rg > 512)) cb /= 2;
     if (C % cb != 0 || cb * rg > 512) return 0;
     DwFast *d = new DwFast();
