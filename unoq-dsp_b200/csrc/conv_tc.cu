@@ -538,7 +538,7 @@ __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(con
         // ------------------------------------------------------------------ epilogue
         const int e = warp - kProducerWarps;
         const int et = threadIdx.x - kProducers;  // 0..kEpilogues-1
-        const int quarter = e & 3;                // TMEM lanes 32*quarter .. +31 (warp id % 4 rule)
+        const int quarter = warp & 3;             // TMEM lanes 32*quarter .. +31 (warp id % 4 rule)
         const int half = e >> 2;                  // which column part of the tile this warp takes
         const int row = quarter * 32 + lane;
         const uint8_t *lut = p.post ? sLut : nullptr;
