@@ -142,6 +142,29 @@ def concat_case(rng, shape_a, shape_b, axis):
     return pw.build(x, z), _rand_input(rng, shape_a)
 
 
+def c2f_bytes_case(rng, hw, c):
+    """YOLO's C2f byte ops: a tensor split in two by innermost-axis slices, each half through a
+    table, then a chain of innermost-axis concats, concat(concat(concat(t0, t1), x), s1), where
+    s1 also feeds its table (so that slice stays a copy)."""
+    shape, half = (1, hw, hw, c), (1, hw, hw, c // 2)
+    pw = PlanWriter()
+    x = pw.tensor(shape)
+    tables = [pw.tensor((256,), "u1", rng.integers(0, 256, size=256).astype(np.uint8)) for _ in range(2)]
+    s0, s1 = pw.tensor(half), pw.tensor(half)
+    pw.op(26, x, x, s0, (0, 0, 0, 0))
+    pw.op(26, x, x, s1, (0, 0, 0, c // 2))
+    t0, t1 = pw.tensor(half), pw.tensor(half)
+    pw.op(22, s0, tables[0], t0)
+    pw.op(22, s1, tables[1], t1)
+    c1 = pw.tensor((1, hw, hw, c))
+    pw.op(20, t0, t1, c1, (3, 0, 0, 0))
+    c2 = pw.tensor((1, hw, hw, 2 * c))
+    pw.op(20, c1, x, c2, (3, 0, 0, 0))
+    z = pw.tensor((1, hw, hw, 2 * c + c // 2))
+    pw.op(20, c2, s1, z, (3, 0, 0, 0))
+    return pw.build(x, z), _rand_input(rng, shape)
+
+
 def slice_case(rng, shape, begin, size):
     pw = PlanWriter()
     x = pw.tensor(shape)
@@ -312,6 +335,8 @@ def all_cases(scale=1):
         ("lut_u8", lambda r: lut_case(r, (1, 3 * s, 3, 16), out_dtype="u1")),
         ("mean", lambda r: mean_case(r, (1, 7, 7, 40 * s))),
         ("concat_c", lambda r: concat_case(r, (1, 4 * s, 5, 16), (1, 4 * s, 5, 8), 3)),
+        ("c2f_bytes", lambda r: c2f_bytes_case(r, 5 * s, 32)),
+        ("c2f_bytes_odd", lambda r: c2f_bytes_case(r, 3 * s, 24)),
         ("concat_h", lambda r: concat_case(r, (1, 4 * s, 5, 16), (1, 2, 5, 16), 1)),
         ("slice", lambda r: slice_case(r, (1, 6 * s, 7, 16), (0, 1, 2, 4), (1, 3, 4, 8))),
         ("transpose_nchw", lambda r: transpose_case(r, (1, 5 * s, 6, 12), (0, 3, 1, 2))),

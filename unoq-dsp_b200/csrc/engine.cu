@@ -139,9 +139,15 @@ int Engine::prepare() {
     std::iota(alias_.begin(), alias_.end(), 0);
     steps_.clear();
     birth_ = P.birth;
+    death_ = P.death;
     fused_.assign(P.h.no, 0);
     const char *fuse_env = std::getenv("UNOQ_FUSE_ADD");
     fuse_adds_ = !(fuse_env && fuse_env[0] == '0');
+    skip_.assign(P.h.no, 0);
+    concat_in_.assign(P.h.no, {});
+    lut_src_.assign(P.h.no, LutSrc{});
+    const char *bytes_env = std::getenv("UNOQ_FUSE_BYTES");
+    if (!(bytes_env && bytes_env[0] == '0')) fuse_byte_ops();
     for (uint32_t i = 0; i < P.h.no; i++) {
         const Op o = P.ops[i];
         const Tensor a = P.ts[o.a], b = P.ts[o.b], z = P.ts[o.out];
@@ -197,7 +203,7 @@ int Engine::prepare() {
                 // Residual add fused into the epilogue when the next op is an add whose one input is
                 // this conv's output and nothing else reads that output.
                 ConvTc *tc = nullptr;
-                if (i + 1 < P.h.no && P.ops[i + 1].code == 18 && o.out != P.h.output && P.death[o.out] == (int)i + 1 &&
+                if (i + 1 < P.h.no && P.ops[i + 1].code == 18 && o.out != P.h.output && death_[o.out] == (int)i + 1 &&
                     fuse_adds_) {
                     const Op &n = P.ops[i + 1];
                     const bool is_a = n.a == o.out, is_b = n.b == o.out;
@@ -346,6 +352,10 @@ int Engine::prepare() {
                 break;
             }
             case 26: {
+                if (skip_[i]) {  // read in place by the table op that consumes it
+                    st.run = nullptr;
+                    break;
+                }
                 Shape5 in{}, out{};
                 in.rank = out.rank = (int)a.rank + 1;
                 in.d[0] = out.d[0] = 1;
@@ -406,6 +416,16 @@ int Engine::prepare() {
             case 22: {
                 const uint8_t *table = dconst(o.b);
                 const unsigned flip = a.type == 3 ? 128u : 0u;
+                if (lut_src_[i].tensor >= 0) {  // slice of the innermost axis + table in one pass
+                    const LutSrc ls = lut_src_[i];
+                    const uint32_t tz = o.out;
+                    st.run = [=](const BatchCtx &B, cudaStream_t s) -> int {
+                        launch_lut_rows(B.ptr[ls.tensor], B.ptr[tz], (size_t)ls.rows * B.images, ls.in_w, ls.off, ls.out_w,
+                                        table, flip, s);
+                        return 0;
+                    };
+                    break;
+                }
                 const uint32_t ta = o.a, tz = o.out, ab = a.bytes;
                 st.run = [=](const BatchCtx &B, cudaStream_t s) -> int {
                     launch_lut(B.ptr[ta], B.ptr[tz], (size_t)ab * B.images, table, flip, s);
@@ -425,6 +445,29 @@ int Engine::prepare() {
                 break;
             }
             case 20: {
+                if (skip_[i]) {  // collapsed into the concat that consumes it
+                    st.run = nullptr;
+                    break;
+                }
+                if (!concat_in_[i].empty()) {
+                    const std::vector<uint32_t> ins = concat_in_[i];
+                    size_t rows = 1;
+                    for (unsigned d = 0; d + 1 < a.rank; d++) rows *= a.d[d];
+                    std::vector<uint32_t> widths;
+                    for (uint32_t t : ins) widths.push_back((uint32_t)(P.ts[t].bytes / rows));
+                    const uint32_t tz = o.out;
+                    st.run = [=](const BatchCtx &B, cudaStream_t s) -> int {
+                        ConcatInputs ci{};
+                        ci.count = (int)ins.size();
+                        for (size_t k = 0; k < ins.size(); k++) {
+                            ci.src[k] = B.ptr[ins[k]];
+                            ci.width[k] = widths[k];
+                        }
+                        launch_concat_multi(ci, B.ptr[tz], rows * B.images, s);
+                        return 0;
+                    };
+                    break;
+                }
                 const unsigned axis = o.p[0];
                 size_t outer = 1, inner = 1;
                 for (unsigned d = 0; d < axis; d++) outer *= a.d[d];
@@ -509,6 +552,75 @@ int Engine::prepare() {
 // Batched arena: storage groups (copy aliases share one group) placed by lifetime. A group
 // lives from its first producer to its last reader; groups whose lifetimes intersect never
 // share bytes. Constants read as activations are replicated per image once, up front.
+// Byte-op fusion at load time (no change to any result):
+//  * a concat (code 20) along the innermost axis whose first input is another such concat, read by
+//    nothing else, absorbs it: one pass writes all the inputs (YOLO's C2f concat chains);
+//  * a table (code 22) whose input is a slice (code 26) of the innermost axis, read by nothing
+//    else, reads the slice's source in place.
+// The skipped op's inputs are then read later than the plan says, so their lifetimes (death_) are
+// extended for the arena planner.
+void Engine::fuse_byte_ops() {
+    const Plan &P = P_;
+    const uint32_t nt = P.h.nt, no = P.h.no;
+    std::vector<int> prod(nt, -1), uses(nt, 0);
+    for (uint32_t i = 0; i < no; i++) {
+        const Op &o = P.ops[i];
+        prod[o.out] = (int)i;
+        uses[o.a]++;
+        if (o.code == 18 || o.code == 20 || o.code == 25 || o.code == 27) uses[o.b]++;
+        if (o.code == 19) {
+            const uint32_t *list = reinterpret_cast<const uint32_t *>(P.bytes(o.b));
+            for (uint32_t j = 0; j < P.ts[o.b].bytes / 4; j++) uses[list[j]]++;
+        }
+    }
+    uses[P.h.output]++;
+    auto rows_of = [&](const Tensor &t) {
+        size_t r = 1;
+        for (uint32_t d = 0; d + 1 < t.rank; d++) r *= t.d[d];
+        return r;
+    };
+    for (uint32_t i = 0; i < no; i++) {
+        const Op &o = P.ops[i];
+        const Tensor &a = P.ts[o.a];
+        const int j = prod[o.a];
+        if (j < 0 || uses[o.a] != 1 || o.a == P.h.output || P.ts[o.a].flags) continue;
+        const Op &pj = P.ops[j];
+        if (o.code == 20 && a.rank >= 1 && o.p[0] + 1 == a.rank && pj.code == 20 && pj.p[0] + 1 == a.rank &&
+            P.ts[pj.a].rank == a.rank) {
+            std::vector<uint32_t> list = concat_in_[j].empty() ? std::vector<uint32_t>{pj.a, pj.b} : concat_in_[j];
+            list.push_back(o.b);
+            const size_t rows = rows_of(a);
+            bool ok = list.size() <= 8 && rows > 0;
+            for (uint32_t t : list) ok = ok && rows_of(P.ts[t]) == rows && P.ts[t].bytes % rows == 0;
+            if (!ok) continue;
+            skip_[j] = 1;
+            concat_in_[j].clear();
+            concat_in_[i] = list;
+            for (uint32_t t : list) death_[t] = std::max(death_[t], (int)i);
+        } else if (o.code == 22 && pj.code == 26) {
+            const Tensor &src = P.ts[pj.a], &sl = P.ts[pj.out];
+            if (src.rank != sl.rank || src.rank < 1 || src.rank > 4 || src.type != sl.type) continue;
+            bool inner = true;
+            for (uint32_t d = 0; d + 1 < src.rank; d++) inner = inner && pj.p[d] == 0 && sl.d[d] == src.d[d];
+            const size_t rows = rows_of(src);
+            if (!inner || rows == 0 || src.bytes % rows || sl.bytes % rows) continue;
+            const uint32_t in_w = (uint32_t)(src.bytes / rows), out_w = (uint32_t)(sl.bytes / rows);
+            const uint32_t esize = in_w / src.d[src.rank - 1];
+            if (esize * src.d[src.rank - 1] != in_w) continue;
+            LutSrc ls;
+            ls.tensor = (int)pj.a;
+            ls.rows = (uint32_t)rows;
+            ls.in_w = in_w;
+            ls.off = pj.p[src.rank - 1] * esize;
+            ls.out_w = out_w;
+            if (ls.off + out_w > in_w) continue;
+            lut_src_[i] = ls;
+            skip_[j] = 1;
+            death_[pj.a] = std::max(death_[pj.a], (int)i);
+        }
+    }
+}
+
 int Engine::plan_arena(BatchCtx &B) {
     std::vector<size_t> offset;
     std::vector<uint32_t> replicated;
@@ -572,12 +684,12 @@ void Engine::layout(uint32_t images, std::vector<size_t> &offset, std::vector<ui
         if (gid[r] < 0) {
             gid[r] = (int)groups.size();
             groups.push_back({r, align_up((size_t)P.ts[r].bytes * images, kAlign), is_const ? -1 : birth_[r],
-                              is_const ? (int)P.h.no : P.death[r], 0});
+                              is_const ? (int)P.h.no : death_[r], 0});
         }
         Group &g = groups[gid[r]];
         if (!is_const) {
             g.birth = std::min(g.birth, birth_[t]);
-            g.death = std::max(g.death, P.death[t]);
+            g.death = std::max(g.death, death_[t]);
         }
         gid[t] = gid[r];
     }

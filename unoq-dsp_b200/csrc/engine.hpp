@@ -127,6 +127,17 @@ class Engine {
     std::vector<Step> steps_;
     std::vector<int> alias_;             // tensor -> storage root (copy ops alias their source)
     std::vector<int> birth_;             // tensor birth op, moved earlier for fused outputs
+    std::vector<int> death_;             // tensor last-read op, moved later for fused byte ops
+    // Byte-op fusion (fuse_byte_ops): ops computed by a later op, concat chains collapsed into their
+    // last concat, and tables that read a slice's source directly.
+    struct LutSrc {
+        int tensor = -1;                 // the slice's source tensor (-1: not fused)
+        uint32_t rows = 0, in_w = 0, off = 0, out_w = 0;
+    };
+    std::vector<char> skip_;
+    std::vector<std::vector<uint32_t>> concat_in_;
+    std::vector<LutSrc> lut_src_;
+    void fuse_byte_ops();
     std::vector<char> fused_;            // op computed inside the previous op's kernel
     bool fuse_adds_ = true;              // UNOQ_FUSE_ADD=0 keeps every add separate
     std::map<uint64_t, std::unique_ptr<BatchCtx>> batches_;  // key: slot << 32 | images

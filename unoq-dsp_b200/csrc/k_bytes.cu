@@ -101,6 +101,49 @@ __global__ void concat_kernel(const uint8_t *__restrict__ a, const uint8_t *__re
     }
 }
 
+// Concat chain: up to 8 inputs along the innermost axis; the inputs' row widths are staged in
+// shared memory so the input lookup indexes no kernel parameter dynamically.
+template <int V>
+__global__ void concat_multi_kernel(const ConcatInputs in, uint8_t *__restrict__ z, uint64_t rows, uint32_t row_units) {
+    using T = typename Unit<V>::T;
+    __shared__ const T *src[8];
+    __shared__ uint32_t units[8];
+    if (threadIdx.x < 8) {
+        src[threadIdx.x] = threadIdx.x < (unsigned)in.count ? reinterpret_cast<const T *>(in.src[threadIdx.x]) : nullptr;
+        units[threadIdx.x] = threadIdx.x < (unsigned)in.count ? in.width[threadIdx.x] / V : 0u;
+    }
+    __syncthreads();
+    const uint64_t total = rows * row_units;
+    for (uint64_t u = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; u < total; u += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t r = u / row_units;
+        uint32_t c = (uint32_t)(u - r * row_units);
+        int i = 0;
+        while (c >= units[i]) c -= units[i++];
+        reinterpret_cast<T *>(z)[u] = src[i][r * units[i] + c];
+    }
+}
+
+// Slice of the innermost axis followed by a byte table, in one pass.
+template <int V>
+__global__ void lut_rows_kernel(const uint8_t *__restrict__ x, uint8_t *__restrict__ y, uint64_t rows, uint32_t in_w,
+                                uint32_t off, uint32_t out_w, const uint8_t *__restrict__ table, unsigned flip) {
+    using T = typename Unit<V>::T;
+    __shared__ uint8_t t[256];
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) t[i] = table[i];
+    __syncthreads();
+    const uint32_t per_row = out_w / V;
+    const uint64_t total = rows * per_row;
+    for (uint64_t u = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; u < total; u += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t r = u / per_row;
+        const uint32_t c = (uint32_t)(u - r * per_row) * V;
+        T v = *reinterpret_cast<const T *>(x + r * in_w + off + c);
+        uint8_t *b = reinterpret_cast<uint8_t *>(&v);
+#pragma unroll
+        for (int k = 0; k < V; k++) b[k] = t[b[k] ^ flip];
+        *reinterpret_cast<T *>(y + r * out_w + c) = v;
+    }
+}
+
 // ---------------------------------------------------------------- transpose (code 10) --------
 // Batched 2-D transpose of elements of `E` bytes: z[b][c][r] = a[b][r][c].
 template <int E>
@@ -464,6 +507,28 @@ void launch_resize(const uint8_t *a, uint8_t *z, int n, int ih, int iw, int c, i
     if (v == 16) resize_kernel<16><<<grid_for(units, kT), kT, 0, s>>>(a, z, pixels, oh, ow, (uint32_t)c, img, offsets);
     else if (v == 4) resize_kernel<4><<<grid_for(units, kT), kT, 0, s>>>(a, z, pixels, oh, ow, (uint32_t)c, img, offsets);
     else resize_kernel<1><<<grid_for(units, kT), kT, 0, s>>>(a, z, pixels, oh, ow, (uint32_t)c, img, offsets);
+}
+
+void launch_concat_multi(const ConcatInputs &in, uint8_t *z, size_t rows, cudaStream_t s) {
+    uint64_t m = reinterpret_cast<uintptr_t>(z), row = 0;
+    for (int i = 0; i < in.count; i++) {
+        m |= in.width[i] | reinterpret_cast<uintptr_t>(in.src[i]);
+        row += in.width[i];
+    }
+    const int v = unit_for(m);
+    const uint64_t units = rows * (row / v);
+    if (v == 16) concat_multi_kernel<16><<<grid_for(units, kT), kT, 0, s>>>(in, z, rows, (uint32_t)(row / 16));
+    else if (v == 4) concat_multi_kernel<4><<<grid_for(units, kT), kT, 0, s>>>(in, z, rows, (uint32_t)(row / 4));
+    else concat_multi_kernel<1><<<grid_for(units, kT), kT, 0, s>>>(in, z, rows, (uint32_t)row);
+}
+
+void launch_lut_rows(const uint8_t *x, uint8_t *y, size_t rows, uint32_t in_w, uint32_t off, uint32_t out_w,
+                     const uint8_t *table, unsigned flip, cudaStream_t s) {
+    const int v = unit_for((uint64_t)in_w | off | out_w | reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y));
+    const uint64_t units = (uint64_t)rows * (out_w / v);
+    if (v == 16) lut_rows_kernel<16><<<grid_for(units, kT), kT, 0, s>>>(x, y, rows, in_w, off, out_w, table, flip);
+    else if (v == 4) lut_rows_kernel<4><<<grid_for(units, kT), kT, 0, s>>>(x, y, rows, in_w, off, out_w, table, flip);
+    else lut_rows_kernel<1><<<grid_for(units, kT), kT, 0, s>>>(x, y, rows, in_w, off, out_w, table, flip);
 }
 
 void launch_pack(const Segments &segs, uint8_t *z, uint32_t z_bytes, int images, cudaStream_t s) {

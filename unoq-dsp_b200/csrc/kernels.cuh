@@ -74,6 +74,18 @@ struct Segments {
     uint32_t dst_offset[32];
 };
 void launch_pack(const Segments &segs, uint8_t *z, uint32_t z_bytes, int images, cudaStream_t s);
+// Code 20 chains fused: z row r = row r of each input in turn (concatenation along the innermost
+// axis of up to 8 inputs; widths in bytes per row).
+struct ConcatInputs {
+    int count;
+    const uint8_t *src[8];
+    uint32_t width[8];
+};
+void launch_concat_multi(const ConcatInputs &in, uint8_t *z, size_t rows, cudaStream_t s);
+// Code 26 (innermost axis) followed by code 22, in one pass: y[r][c] = table[x[r][off + c] ^ flip]
+// for c < out_w, x rows of in_w bytes.
+void launch_lut_rows(const uint8_t *x, uint8_t *y, size_t rows, uint32_t in_w, uint32_t off, uint32_t out_w,
+                     const uint8_t *table, unsigned flip, cudaStream_t s);
 void launch_copy(const void *src, void *dst, size_t bytes, cudaStream_t s);
 
 }  // namespace uq
