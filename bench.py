@@ -289,6 +289,30 @@ KERNEL_NAMES = {14: "conv", 15: "depthwise", 16: "pool", 17: "softmax_table", 18
 
 
 # --------------------------------------------------------------------------- one model
+def pcie_h2d_gbs(nbytes, device):
+    """Host-to-device bandwidth of one plain pinned copy of `nbytes` (the step's input), timed with
+    CUDA events: the ceiling of the e2e leg, which moves those bytes every step."""
+    try:
+        import torch
+        src = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+        dst = torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{device}")
+        s = torch.cuda.Stream(device=device)
+        with torch.cuda.stream(s):
+            dst.copy_(src, non_blocking=True)
+            s.synchronize()
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0.record(s)
+            for _ in range(3):
+                dst.copy_(src, non_blocking=True)
+            t1.record(s)
+        t1.synchronize()
+        gbs = 3 * nbytes / (t0.elapsed_time(t1) / 1e3) / 1e9
+        del src, dst
+        return round(gbs, 2)
+    except Exception:  # torch absent or no pinned memory: the figure is context only
+        return None
+
+
 def detect_leg(lib, handle, model, h_in, per_gpu, global_batch, steps, dist, k=20):
     """The detector's own end-to-end path (ug_detect_batch): uint8 pixels from pinned host memory,
     the bundle's byte table and the one-to-one YOLO top-k on the GPU, k records per image back."""
@@ -382,6 +406,7 @@ def bench_model(lib, dist, name, global_batch, steps, warmup, peaks, want_roofli
             e2e_ms += lib.ug_last_infer_ms(handle)
         dist.barrier()
         t_e2e = dist.max(e2e_ms / 1e3)
+        h2d_gbs = pcie_h2d_gbs(ni * per_gpu, dist.local)
         roof = breakdown = None
         if want_roofline:
             roof, breakdown = roofline(lib, handle, plan, per_gpu, max(1, min(steps, 3)), peaks, KERNEL_NAMES)
@@ -391,7 +416,9 @@ def bench_model(lib, dist, name, global_batch, steps, warmup, peaks, want_roofli
         return {
             "value": value, "ms_per_step": t_dev / steps * 1e3, "per_gpu_batch": per_gpu, "kernels_per_step": kernels,
             "e2e": {"value": global_batch * steps / t_e2e, "unit": "images/s", "h2d_bytes_per_step": ni * global_batch,
-                    "d2h_bytes_per_step": no * global_batch, "ms_per_step": t_e2e / steps * 1e3},
+                    "d2h_bytes_per_step": no * global_batch, "ms_per_step": t_e2e / steps * 1e3,
+                    "pcie_h2d_gbs": h2d_gbs,
+                    "h2d_bound_images_per_s": round(h2d_gbs * 1e9 / ni * dist.world, 1) if h2d_gbs else None},
             "clocks": clocks.summary(), "roofline": roof, "breakdown": breakdown, "detect_e2e": detected,
         }
     finally:
