@@ -69,6 +69,11 @@ void Engine::release() {
     if (ev0_) cudaEventDestroy(ev0_);
     if (ev1_) cudaEventDestroy(ev1_);
     ev0_ = ev1_ = nullptr;
+    for (auto &e : pipe_t_) {
+        if (e) cudaEventDestroy(e);
+        e = nullptr;
+    }
+    pipe_growth_ = 1.25;
     for (auto &row : pipe_ev_)
         for (auto &e : row) {
             if (e) cudaEventDestroy(e);
@@ -114,6 +119,7 @@ int Engine::load(const void *plan, uint32_t bytes, int device) {
     UQ_CUDA(cudaStreamCreateWithFlags(&d2h_, cudaStreamNonBlocking));
     UQ_CUDA(cudaEventCreate(&ev0_));
     UQ_CUDA(cudaEventCreate(&ev1_));
+    for (auto &e : pipe_t_) UQ_CUDA(cudaEventCreate(&e));
     for (auto &row : pipe_ev_)
         for (auto &e : row) UQ_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     UQ_CUDA(cudaMalloc(&d_const_, P_.h.arena_bytes));
@@ -822,13 +828,9 @@ int Engine::run_host(const void *in, void *out, uint32_t images) { return run_ba
 int Engine::run_batch_host(const void *in, void *out, uint32_t images, uint32_t k) {
     if (!ready_ || !in || !out) return 22;
     if (k && !yolo_.levels) return 22;
-    // Large batches overlap their copies with compute, in pieces of about 512 images (2 to 16):
-    // small enough that the first copy and the last read-back are short, large enough that the
-    // graph runs as efficiently as on the whole batch.
-    if (!profiling_ && images >= 512) {
-        const uint32_t pieces = std::min<uint32_t>(16, std::max<uint32_t>(2, (images + 256) / 512));
-        return run_pipelined(static_cast<const uint8_t *>(in), static_cast<uint8_t *>(out), images, pieces, k);
-    }
+    // Large batches overlap their copies with compute, in pieces (run_pipelined).
+    if (!profiling_ && images >= 512)
+        return run_pipelined(static_cast<const uint8_t *>(in), static_cast<uint8_t *>(out), images, k);
     BatchCtx *B = nullptr;
     int rc = batch(images, &B);
     if (!rc) rc = stage_buffers(*B, k != 0);
@@ -866,17 +868,42 @@ int Engine::run_batch_host(const void *in, void *out, uint32_t images, uint32_t 
     return device_status();
 }
 
-int Engine::run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint32_t chunks, uint32_t k) {
-    const uint32_t c = (images + chunks - 1) / chunks;  // images per piece; the last may be smaller
-    chunks = (images + c - 1) / c;
-    const uint32_t rem = images - (chunks - 1) * c;
+int Engine::run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint32_t k) {
+    // Piece sizes grow geometrically: the first is small (1/16 of the batch, 64 to 256 images), so
+    // compute starts after a short upload, and each next piece is `growth` times the previous, so
+    // that its upload still fits inside the previous piece's compute while the later, larger pieces
+    // run at close to whole-batch efficiency (a 512-image MobileNetV4 graph runs about 17% slower
+    // per image than a 4096-image one: tail waves and launch gaps). The growth is the ratio of
+    // compute to upload time per image measured on the previous call's last piece (1.25 at first;
+    // about 1.2 for MobileNetV4, 2.7 for YOLO26n). At most kMaxPieces; a small remainder joins the
+    // last piece. UNOQ_PIPE_GROWTH fixes the factor.
+    constexpr size_t kMaxPieces = 16;
+    static const double fixed_growth = [] {
+        const char *env = std::getenv("UNOQ_PIPE_GROWTH");
+        const double g = env ? std::atof(env) : 0.0;
+        return g >= 1.0 && g <= 4.0 ? g : 0.0;
+    }();
+    const double growth = fixed_growth > 0 ? fixed_growth : pipe_growth_;
+    std::vector<uint32_t> sizes;
+    {
+        uint32_t left = images;
+        double cur = std::min(256.0, std::max(64.0, images / 16.0));
+        while (left) {
+            uint32_t n = std::min<uint32_t>(left, (uint32_t)cur);
+            if (left - n < (uint32_t)(cur * 0.5) || sizes.size() + 1 == kMaxPieces) n = left;
+            sizes.push_back(n);
+            left -= n;
+            cur *= growth;
+        }
+    }
     const size_t ni = input_bytes(), no = k ? sizeof(UgDetectionRecord) * k : output_bytes();
-    BatchCtx *slot[2] = {nullptr, nullptr}, *last = nullptr;
-    int rc = batch(c, &slot[0], 1);
-    if (!rc) rc = batch(c, &slot[1], 2);
-    if (!rc && rem != c) rc = batch(rem, &last, 3);
-    for (BatchCtx *b : {slot[0], slot[1], last})
-        if (!rc && b) rc = stage_buffers(*b, k != 0);
+    // one batch context per piece (slot p + 1): no arena is refilled within a call
+    std::vector<BatchCtx *> ctx(sizes.size(), nullptr);
+    int rc = 0;
+    for (size_t p = 0; p < sizes.size() && !rc; p++) {
+        rc = batch(sizes[p], &ctx[p], (uint32_t)p + 1);
+        if (!rc) rc = stage_buffers(*ctx[p], k != 0);
+    }
     if (rc) return rc;
     UQ_CUDA(cudaSetDevice(device_));
     const bool gathering = !k && gather_ && gather_->active();
@@ -886,20 +913,24 @@ int Engine::run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint
     UQ_CUDA(cudaEventRecord(ev0_, stream_));
     UQ_CUDA(cudaStreamWaitEvent(h2d_, ev0_, 0));
     UQ_CUDA(cudaStreamWaitEvent(d2h_, ev0_, 0));
-    for (uint32_t piece = 0; piece < chunks; piece++) {
+    size_t off = 0;
+    for (size_t piece = 0; piece < sizes.size(); piece++) {
         const int s = (int)(piece & 1);
-        BatchCtx *B = (piece == chunks - 1 && last) ? last : slot[s];
-        const size_t n = piece == chunks - 1 ? rem : c, off = (size_t)piece * c;
-        // the slot's previous piece must be computed and read out before its arena is refilled
-        if (piece >= 2) UQ_CUDA(cudaStreamWaitEvent(h2d_, pipe_ev_[2][s], 0));
+        BatchCtx *B = ctx[piece];
+        const size_t n = sizes[piece];
+        const bool timed = piece + 1 == sizes.size() && sizes.size() > 1;
+        if (timed) UQ_CUDA(cudaEventRecord(pipe_t_[0], h2d_));
         UQ_CUDA(cudaMemcpyAsync(landing(*B), in + off * ni, n * ni, cudaMemcpyHostToDevice, h2d_));
         UQ_CUDA(cudaEventRecord(pipe_ev_[0][s], h2d_));
+        if (timed) UQ_CUDA(cudaEventRecord(pipe_t_[1], h2d_));
         UQ_CUDA(cudaStreamWaitEvent(stream_, pipe_ev_[0][s], 0));
+        if (timed) UQ_CUDA(cudaEventRecord(pipe_t_[2], stream_));
         if ((rc = stage_in(*B, stream_))) return rc;
         if (cudaGraphLaunch(B->exec, stream_) != cudaSuccess) {
             set_error("graph launch failed");
             return 2001;
         }
+        if (timed) UQ_CUDA(cudaEventRecord(pipe_t_[3], stream_));
         if (k && (rc = stage_out(*B, k, stream_))) return rc;
         if (gathering && (rc = gather_->enqueue(B->ptr[P_.h.output], n * no, no * images, off * no, stream_)))
             return rc;
@@ -916,12 +947,19 @@ int Engine::run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint
             }
         }
         UQ_CUDA(cudaEventRecord(pipe_ev_[2][s], d2h_));
+        off += n;
     }
     UQ_CUDA(cudaEventRecord(ev1_, d2h_));
     UQ_CUDA(cudaStreamWaitEvent(stream_, ev1_, 0));
     if ((rc = finish(ev1_))) return rc;
     UQ_CUDA(cudaEventElapsedTime(&last_ms_, ev0_, ev1_));
     last_images_ = images;
+    if (sizes.size() > 1) {
+        float up = 0.f, comp = 0.f;
+        if (cudaEventElapsedTime(&up, pipe_t_[0], pipe_t_[1]) == cudaSuccess &&
+            cudaEventElapsedTime(&comp, pipe_t_[2], pipe_t_[3]) == cudaSuccess && up > 0.f && comp > 0.f)
+            pipe_growth_ = std::min(3.0, std::max(1.15, 1.1 * comp / up));
+    }
     return device_status();
 }
 

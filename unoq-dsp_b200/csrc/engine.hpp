@@ -100,10 +100,10 @@ class Engine {
     // Batch context for `images`; slot > 0 gives further contexts of the same size (own arena and
     // graph) for the copy/compute pipeline.
     int batch(uint32_t images, BatchCtx **out, uint32_t slot = 0);
-    // Host batch in `chunks` pieces: H2D of piece k+1, compute of piece k and D2H of piece k-1
-    // run concurrently on three streams, two arena slots alternating.
+    // Host batch in pieces of growing size: H2D of piece p+1, compute of piece p and D2H of piece
+    // p-1 run concurrently on three streams, each piece in its own batch context.
     // k > 0: the output is k decoder records per image instead of the output tensor.
-    int run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint32_t chunks, uint32_t k = 0);
+    int run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint32_t k = 0);
     int run_batch_host(const void *in, void *out, uint32_t images, uint32_t k);
     int stage_buffers(BatchCtx &b, bool records);
     uint8_t *landing(const BatchCtx &b) const { return table_channels_ ? b.pixels : b.ptr[P_.h.input]; }
@@ -144,6 +144,8 @@ class Engine {
     cudaStream_t h2d_ = nullptr, d2h_ = nullptr;             // copy streams of the pipeline
     cudaEvent_t pipe_ev_[3][2] = {};                         // per slot: input landed, computed, output read
     cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
+    cudaEvent_t pipe_t_[4] = {};         // timing of the last piece: upload start / end, graph start / end
+    double pipe_growth_ = 1.25;          // piece growth: compute / upload time per image, from the last call
     float last_ms_ = 0.f;
     uint32_t last_images_ = 0;
     bool profiling_ = false;
