@@ -81,8 +81,9 @@ UG_API int ug_set_device(int device);
 /* Run `images` independent images (inputs back to back, outputs back to back), host
  * buffers. Pinned buffers from ug_host_alloc give full-bandwidth copies. The first call
  * for a batch size prepares and captures a CUDA graph for it. From 512 images the batch runs
- * in pieces of about 512 images (2 to 16) whose host-to-device copy, graph and device-to-host
- * copy overlap on three streams. */
+ * in up to 16 pieces whose host-to-device copy, graph and device-to-host copy overlap on three
+ * streams; pieces grow geometrically from a small first one, by the compute/upload time ratio
+ * measured on the previous call (UNOQ_PIPE_GROWTH fixes it). */
 UG_API int ug_infer_batch(void *session, const void *input, uint32_t images, void *output);
 /* Device-resident variant: `device_input`/`device_output` are this session's device
  * buffers from ug_batch_buffers; nothing crosses PCIe. Asynchronous on the session stream. */
