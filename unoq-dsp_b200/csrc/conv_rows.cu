@@ -1,8 +1,8 @@
 // conv_rows.cu -- convolutions over few input channels (the RGB stems) as row GEMMs on the
 // 5th-generation tensor cores (tcgen05 kind::i8).
 //
-// Plan code 14 (runtime/qnn.c:1101-1227) for kh x kw kernels (kh, kw <= 3) over ic <= 4 channels
-// with stride s in both directions. For G adjacent output columns ox0..ox0+G-1 of output row oy,
+// Plan code 14 (runtime/qnn.c:1101-1227) for kh x kw kernels (kh, kw <= 3) over ic <= 16 channels
+// with stride s in both directions (the RGB stems, and the 8 / 16-channel layers of YOLO26n). For G adjacent output columns ox0..ox0+G-1 of output row oy,
 // every tap of kernel row ky reads input row iy = s*oy - pt + ky, and all their bytes lie in one
 // window of that row: bytes [X, X + s*ic*(G-1) + kw*ic) with X = (s*ox0 - pl)*ic. Hence
 //
@@ -349,7 +349,9 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
     const char *env = std::getenv("UNOQ_CONV_ROWS");
     if (env && env[0] == '0') return 0;
     const int s = g.sh;
-    if (g.ic < 1 || g.ic > 4 || g.kh < 1 || g.kh > 3 || g.kw < 1 || g.kw > 3 || g.dh != 1 || g.dw != 1) return 0;
+    const char *env_ic = std::getenv("UNOQ_CONV_ROWS_IC");  // widest input taken (default 16)
+    const int max_ic = env_ic ? std::atoi(env_ic) : 16;
+    if (g.ic < 1 || g.ic > max_ic || g.kh < 1 || g.kh > 3 || g.kw < 1 || g.kw > 3 || g.dh != 1 || g.dw != 1) return 0;
     if (g.sw != s || (s != 1 && s != 2)) return 0;
     if (g.oc % 16 != 0 || g.oc > 256) return 0;
     if (g.pt < 0 || g.pt >= g.kh || g.pl < 0 || g.pl >= g.kw) return 0;

@@ -12,7 +12,7 @@ namespace uq {
 
 struct ConvRows;  // prepared banded weights, epilogue constants and border corrections
 
-// Take the conv if it has ic <= 4, a kh x kw <= 3 x 3 kernel with dilation 1, equal strides 1 or 2,
+// Take the conv if it has ic <= 16 (UNOQ_CONV_ROWS_IC lowers the bound), a kh x kw <= 3 x 3 kernel with dilation 1, equal strides 1 or 2,
 // oc a multiple of 16 (<= 256) and 16-byte input rows; prepare its device data with `alloc`.
 // *out = nullptr when another path should run. Returns 0 or 2001.
 int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *post_dev, const ConvGeom &g,
