@@ -341,12 +341,20 @@ def all_cases(scale=1):
         ("slice", lambda r: slice_case(r, (1, 6 * s, 7, 16), (0, 1, 2, 4), (1, 3, 4, 8))),
         ("transpose_nchw", lambda r: transpose_case(r, (1, 5 * s, 6, 12), (0, 3, 1, 2))),
         ("transpose_3d", lambda r: transpose_case(r, (2, 7 * s, 9), (0, 2, 1))),
+        # rows and columns multiples of 4 (the word transpose): one matrix per block, and many
+        # small matrices per block with a partial last chunk
+        ("transpose_words", lambda r: transpose_case(r, (2, 10, 10, 64 * s), (0, 3, 1, 2))),
+        ("transpose_words_many", lambda r: transpose_case(r, (13, 3, 12, 20 * s), (0, 1, 3, 2))),
         ("resize2x", lambda r: resize_case(r, (1, 5 * s, 6, 8), (10 * s, 12))),
         ("pad", lambda r: pad_case(r, (1, 4 * s, 5, 6), [0, 0, 1, 2, 2, 1, 0, 0])),
         ("pad_channels", lambda r: pad_case(r, (1, 3, 4 * s, 5), [0, 1, 0, 0, 1, 0, 2, 3])),
         ("pack", lambda r: pack_case(r, (1, 4 * s, 3, 6))),
         ("bmm", lambda r: bmm_case(r, 2, 10 * s, 16, 12)),
         ("bmm_adj", lambda r: bmm_case(r, 2, 9, 20, 7 * s, adj_x=1, adj_y=1)),
+        # attention shapes (q^T k and v attn^T), K not a multiple of 4, one operand transposed
+        ("bmm_attn_qk", lambda r: bmm_case(r, 2, 100, 32, 25 * s)),
+        ("bmm_attn_v", lambda r: bmm_case(r, 2, 16 * s, 100, 100, adj_y=1)),
+        ("bmm_odd_k", lambda r: bmm_case(r, 3, 7 * s, 13, 9, adj_x=1)),
         ("softmax_exact", lambda r: softmax_exact_case(r, 10 * s, 100)),
         ("softmax_table", lambda r: softmax_table_case(r, 6 * s, 33)),
         ("block", lambda r: block_case(r, hw=7 * s)),

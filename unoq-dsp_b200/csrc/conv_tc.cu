@@ -432,14 +432,19 @@ __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(con
                         const int e = sTab[kc * 8 + j];
                         if (e >= 0) {
                             const int dy = e >> 20, off = e & 0xFFFFF;
+                            // all loads first: each store waits only for its own load, not in turn
+                            uint4 v[kRowIters];
 #pragma unroll
                             for (int i = 0; i < kRowIters; i++) {
-                                const int r = r0 + kRowStep * i, iy = y0[i] + dy;
-                                const uint32_t src = (iy >= 0 && iy < p.ih)
-                                                         ? bandb + (uint32_t)((rb[i] + iy) * pitch + cb[i] + off)
-                                                         : fillrow + (uint32_t)off;
-                                st_shared16(stage + (r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4),
-                                            ld_shared16(src));
+                                const int iy = y0[i] + dy;
+                                v[i] = ld_shared16((iy >= 0 && iy < p.ih)
+                                                       ? bandb + (uint32_t)((rb[i] + iy) * pitch + cb[i] + off)
+                                                       : fillrow + (uint32_t)off);
+                            }
+#pragma unroll
+                            for (int i = 0; i < kRowIters; i++) {
+                                const int r = r0 + kRowStep * i;
+                                st_shared16(stage + (r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4), v[i]);
                             }
                         }
                         fence_proxy_async();

@@ -173,6 +173,46 @@ __global__ void transpose2d_kernel(const uint8_t *__restrict__ a, uint8_t *__res
     }
 }
 
+// Byte transpose for rows % 4 == 0 and cols % 4 == 0 with 4-byte aligned buffers. A block stages
+// `per` whole matrices (contiguous in memory) in shared memory with an odd word stride per row,
+// then each thread transposes a 4 x 4 byte block in registers with byte permutes and writes one
+// word into each of four output rows; consecutive lanes take consecutive 4-byte runs of an output
+// row, so both the global loads and the global stores are contiguous across a warp.
+constexpr int kTrSmem = 40 * 1024;
+
+__global__ void transpose_b4_kernel(const uint32_t *__restrict__ a, uint32_t *__restrict__ z, uint32_t batches,
+                                    uint32_t rows, uint32_t cols, uint32_t per, FastDiv div_cw, FastDiv div_blocks,
+                                    FastDiv div_rb) {
+    extern __shared__ uint32_t tsm[];
+    const uint32_t cw = cols / 4, cs = cw | 1, rb = rows / 4;
+    const uint32_t mat_words = rows * cw, blocks_per = rb * cw;
+    const uint32_t chunks = (batches + per - 1) / per;
+    for (uint32_t ch = blockIdx.x; ch < chunks; ch += gridDim.x) {
+        const uint32_t m0 = ch * per, cnt = min(per, batches - m0);
+        const uint32_t *src = a + (size_t)m0 * mat_words;
+        uint32_t *dst = z + (size_t)m0 * mat_words;
+        for (uint32_t g = threadIdx.x; g < cnt * mat_words; g += blockDim.x) {
+            const uint32_t row = (uint32_t)div_cw.div((int)g);
+            tsm[row * cs + (g - row * cw)] = __ldg(src + g);
+        }
+        __syncthreads();
+        for (uint32_t q = threadIdx.x; q < cnt * blocks_per; q += blockDim.x) {
+            const uint32_t mat = (uint32_t)div_blocks.div((int)q), rem = q - mat * blocks_per;
+            const uint32_t cb = (uint32_t)div_rb.div((int)rem), r = rem - cb * rb;
+            const uint32_t *t = tsm + (mat * rows + 4 * r) * cs + cb;
+            const uint32_t v0 = t[0], v1 = t[cs], v2 = t[2 * cs], v3 = t[3 * cs];
+            const uint32_t t0 = __byte_perm(v0, v1, 0x5140), t1 = __byte_perm(v0, v1, 0x7362);
+            const uint32_t t2 = __byte_perm(v2, v3, 0x5140), t3 = __byte_perm(v2, v3, 0x7362);
+            uint32_t *d = dst + (size_t)mat * mat_words + (size_t)(4 * cb) * rb + r;
+            d[0] = __byte_perm(t0, t2, 0x5410);
+            d[rb] = __byte_perm(t0, t2, 0x7632);
+            d[2 * rb] = __byte_perm(t1, t3, 0x5410);
+            d[3 * rb] = __byte_perm(t1, t3, 0x7632);
+        }
+        __syncthreads();
+    }
+}
+
 struct Perm5 {
     int p[5];
 };
@@ -282,63 +322,100 @@ __global__ void maxpool16_kernel(const int8_t *__restrict__ x, int8_t *__restric
 
 // ---------------------------------------------------------------- bmm (code 27) --------------
 // qnn.c:119-153 computes sum (x + 128) w - (xz + 128) sum w - wz sum (x + 128) + k (xz + 128) wz
-// in wrapping int32, which is sum (x - xz)(w - wz). Block = one batch matrix, up to 64 output rows
-// at a time: both operands, zero points subtracted, sit in shared memory as int16 (X rows x K,
-// W K x N, both stored K-major per output index), and each thread accumulates a 4 x 4 register
-// tile of outputs. Matrices too large for the shared-memory budget use the 32 x 32 tiled path.
-constexpr int kBmmRows = 64;       // output rows per block pass
+// in wrapping int32, which is sum (x - xz)(w - wz) = sum x w - wz sum x - xz sum w + k xz wz. The
+// small-matrix kernel takes that last form: block = one batch matrix, up to `rows_cap` output rows
+// at a time, both operands raw int8 in shared memory packed four reduction steps to a word (zero
+// padded, X rows x K, W K x N, both K-major per output index, odd word stride per row), sum x w
+// through __dp4a, the row sums of X and column sums of W once per block. Each thread accumulates a
+// 4 x 4 register tile whose rows and columns lie a quarter of the block's extent apart, so the lanes
+// of a warp read consecutive W rows (distinct banks) and share X rows (broadcast). Matrices too
+// large for the shared-memory budget use the 32 x 32 tiled path.
 constexpr int kBmmSmem = 48 * 1024;
+
+__host__ __device__ inline size_t bmm_small_smem(int n, int k, int rows_cap) {
+    const size_t kp = (size_t)((k + 3) / 4) | 1;
+    return ((size_t)n + rows_cap) * (kp + 1) * sizeof(int32_t);
+}
 
 __global__ void bmm_small_kernel(const int8_t *__restrict__ x, const int8_t *__restrict__ w, int8_t *__restrict__ y,
                                  uint32_t batches, int m, int n, int k, int xz, int wz, int yz, int mult, int s,
-                                 int adj_x, int adj_y) {
-    extern __shared__ int16_t bsm[];
-    const int kpad = k | 1;                        // odd stride: rows fall in distinct banks
-    int16_t *ws = bsm;                             // [n][kpad]  (w[t][c] at ws[c * kpad + t])
-    int16_t *xs = bsm + (size_t)n * kpad;          // [kBmmRows][kpad]
-    const int tiles_r = (n + 3) / 4;               // 4-column groups
-    for (uint32_t job = blockIdx.x; job < batches * (uint32_t)((m + kBmmRows - 1) / kBmmRows); job += gridDim.x) {
-        const uint32_t bt = job / ((m + kBmmRows - 1) / kBmmRows);
-        const int r0 = (int)(job % ((m + kBmmRows - 1) / kBmmRows)) * kBmmRows;
-        const int rows = min(kBmmRows, m - r0);
+                                 int adj_x, int adj_y, int rows_cap) {
+    extern __shared__ int32_t bsm[];
+    const int kw = (k + 3) / 4, kp = kw | 1;
+    int32_t *ws = bsm;                        // [n][kp]: word t4 of column c = w[4 t4 .. 4 t4 + 3][c]
+    int32_t *xs = ws + (size_t)n * kp;        // [rows_cap][kp]
+    int32_t *sw = xs + (size_t)rows_cap * kp; // [n] column sums of W
+    int32_t *sx = sw + n;                     // [rows_cap] row sums of X
+    const uint32_t kzz = (uint32_t)k * (uint32_t)xz * (uint32_t)wz;
+    const uint32_t row_jobs = (uint32_t)((m + rows_cap - 1) / rows_cap);
+    for (uint32_t job = blockIdx.x; job < batches * row_jobs; job += gridDim.x) {
+        const uint32_t bt = job / row_jobs;
+        const int r0 = (int)(job - bt * row_jobs) * rows_cap;
+        const int rows = min(rows_cap, m - r0);
         const int8_t *xb = x + (size_t)bt * m * k, *wb = w + (size_t)bt * k * n;
-        for (int i = threadIdx.x; i < n * k; i += blockDim.x) {
-            const int c = i / k, t = i - c * k;
-            ws[c * kpad + t] = (int16_t)(wb[adj_y ? (size_t)c * k + t : (size_t)t * n + c] - wz);
+        for (int i = threadIdx.x; i < n * kw; i += blockDim.x) {
+            int c, t4;  // the stored layout's contiguous index runs fastest across the threads
+            if (adj_y) t4 = i % kw, c = i / kw;
+            else c = i % n, t4 = i / n;
+            uint32_t v = 0;
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+                const int t = 4 * t4 + b;
+                if (t < k) v |= (uint32_t)(uint8_t)wb[adj_y ? (size_t)c * k + t : (size_t)t * n + c] << (8 * b);
+            }
+            ws[c * kp + t4] = (int32_t)v;
         }
-        for (int i = threadIdx.x; i < rows * k; i += blockDim.x) {
-            const int r = i / k, t = i - r * k;
-            xs[r * kpad + t] = (int16_t)(xb[adj_x ? (size_t)t * m + r0 + r : (size_t)(r0 + r) * k + t] - xz);
+        for (int i = threadIdx.x; i < rows * kw; i += blockDim.x) {
+            int r, t4;
+            if (adj_x) r = i % rows, t4 = i / rows;
+            else t4 = i % kw, r = i / kw;
+            uint32_t v = 0;
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+                const int t = 4 * t4 + b;
+                if (t < k) v |= (uint32_t)(uint8_t)xb[adj_x ? (size_t)t * m + r0 + r : (size_t)(r0 + r) * k + t] << (8 * b);
+            }
+            xs[r * kp + t4] = (int32_t)v;
         }
         __syncthreads();
-        // thread -> 4 rows (rb * 4 ..) x 4 columns (cb * 4 ..)
-        const int groups = ((rows + 3) / 4) * tiles_r;
-        for (int gi = threadIdx.x; gi < groups; gi += blockDim.x) {
-            const int rb = gi / tiles_r, cb = gi - rb * tiles_r;
-            int acc[4][4] = {};
-            for (int t = 0; t < k; t++) {
-                int xv[4], wv[4];
+        for (int i = threadIdx.x; i < n + rows; i += blockDim.x) {
+            const int32_t *src = i < n ? ws + (size_t)i * kp : xs + (size_t)(i - n) * kp;
+            int32_t acc = 0;
+            for (int t4 = 0; t4 < kw; t4++) acc = __dp4a(src[t4], 0x01010101, acc);
+            (i < n ? sw[i] : sx[i - n]) = acc;
+        }
+        __syncthreads();
+        const int rq = (rows + 3) / 4, cq = (n + 3) / 4;
+        for (int gi = threadIdx.x; gi < rq * cq; gi += blockDim.x) {
+            const int rr = gi / cq, cc = gi - rr * cq;
+            const int32_t *xp[4], *wp[4];
 #pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const int r = min(rb * 4 + i, rows - 1), c = min(cb * 4 + i, n - 1);
-                    xv[i] = xs[r * kpad + t];
-                    wv[i] = ws[c * kpad + t];
-                }
+            for (int i = 0; i < 4; i++) {
+                xp[i] = xs + (size_t)min(rr + i * rq, rows - 1) * kp;
+                wp[i] = ws + (size_t)min(cc + i * cq, n - 1) * kp;
+            }
+            int32_t acc[4][4] = {};
+            for (int t4 = 0; t4 < kw; t4++) {
+                int32_t xv[4], wv[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++) xv[i] = xp[i][t4], wv[i] = wp[i][t4];
 #pragma unroll
                 for (int i = 0; i < 4; i++)
 #pragma unroll
-                    for (int j = 0; j < 4; j++) acc[i][j] += xv[i] * wv[j];
+                    for (int j = 0; j < 4; j++) acc[i][j] = __dp4a(xv[i], wv[j], acc[i][j]);
             }
 #pragma unroll
             for (int i = 0; i < 4; i++) {
-                const int r = rb * 4 + i;
+                const int r = rr + i * rq;
                 if (r >= rows) break;
+                const uint32_t rowc = kzz - (uint32_t)wz * (uint32_t)sx[r];
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
-                    const int c = cb * 4 + j;
-                    if (c < n)
-                        y[((size_t)bt * m + r0 + r) * n + c] =
-                            (int8_t)dev_clamp(dev_scale(acc[i][j], mult, s) + yz, -128, 127);
+                    const int c = cc + j * cq;
+                    if (c < n) {
+                        const int32_t v = (int32_t)((uint32_t)acc[i][j] + rowc - (uint32_t)xz * (uint32_t)sw[c]);
+                        y[((size_t)bt * m + r0 + r) * n + c] = (int8_t)dev_clamp(dev_scale(v, mult, s) + yz, -128, 127);
+                    }
                 }
             }
         }
@@ -415,11 +492,12 @@ void launch_pool(const int8_t *x, int8_t *y, const ConvGeom &g, int is_max, int 
 
 void launch_bmm(const int8_t *x, const int8_t *w, int8_t *y, size_t batches, int m, int n, int k, const int32_t q7[7],
                 cudaStream_t s) {
-    const size_t smem = ((size_t)n + kBmmRows) * (size_t)(k | 1) * sizeof(int16_t);
-    if (smem <= (size_t)kBmmSmem) {
-        const uint64_t jobs = (uint64_t)batches * ((m + kBmmRows - 1) / kBmmRows);
+    for (int rows_cap = 128; rows_cap >= 32; rows_cap /= 2) {
+        const size_t smem = bmm_small_smem(n, k, rows_cap);
+        if (smem > (size_t)kBmmSmem || (rows_cap > 32 && rows_cap / 2 >= m)) continue;
+        const uint64_t jobs = (uint64_t)batches * ((m + rows_cap - 1) / rows_cap);
         bmm_small_kernel<<<grid_for(jobs, 1), kT, smem, s>>>(x, w, y, (uint32_t)batches, m, n, k, q7[0], q7[1], q7[2],
-                                                             q7[3], q7[4], q7[5], q7[6]);
+                                                             q7[3], q7[4], q7[5], q7[6], rows_cap);
         return;
     }
     const uint64_t tiles = (uint64_t)batches * ((m + 31) / 32) * ((n + 31) / 32);
@@ -449,6 +527,18 @@ void launch_permute(const uint8_t *a, uint8_t *z, const Shape5 &in, const int pe
     if (t2 && B * R * Cc == count && R < (1u << 31) && Cc < (1u << 31)) {
         const uint64_t tiles = B * ((R + 31) / 32) * ((Cc + 31) / 32);
         const unsigned grid = (unsigned)std::min<uint64_t>(tiles, 148ull * 16);
+        const size_t mat_smem = R * ((Cc / 4) | 1) * sizeof(uint32_t);
+        if (elem_bytes == 1 && R >= 4 && Cc >= 4 && R % 4 == 0 && Cc % 4 == 0 && mat_smem <= (size_t)kTrSmem && B < (1u << 31) &&
+            unit_for(reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(z)) >= 4) {
+            // matrices per block: fill about a quarter of the budget, keeping the word counts < 2^31
+            const uint64_t per = std::max<uint64_t>(1, std::min<uint64_t>(B, (kTrSmem / 4) / mat_smem));
+            const uint64_t chunks = (B + per - 1) / per;
+            const int cw = (int)(Cc / 4);
+            transpose_b4_kernel<<<(unsigned)std::min<uint64_t>(chunks, 148ull * 16), kT, per * mat_smem, s>>>(
+                reinterpret_cast<const uint32_t *>(a), reinterpret_cast<uint32_t *>(z), (uint32_t)B, (uint32_t)R,
+                (uint32_t)Cc, (uint32_t)per, FastDiv(cw), FastDiv((int)(R / 4) * cw), FastDiv((int)(R / 4)));
+            return;
+        }
         if (elem_bytes == 1) transpose2d_kernel<1><<<grid, kT, 0, s>>>(a, z, (uint32_t)B, (uint32_t)R, (uint32_t)Cc);
         else if (elem_bytes == 4) transpose2d_kernel<4><<<grid, kT, 0, s>>>(a, z, (uint32_t)B, (uint32_t)R, (uint32_t)Cc);
         else t2 = false;
