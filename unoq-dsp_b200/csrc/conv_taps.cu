@@ -478,7 +478,10 @@ int conv_taps_launch(const ConvTaps &c, const int8_t *x, int8_t *y, const ConvGe
             CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return 2001;
-    int per_tile = (g_taps_sm_count + c.n_tiles - 1) / c.n_tiles;
+    // CTAs per N tile: floor, so that all n_tiles * per_tile CTAs are resident at once (one per SM).
+    // Rounding up would start the extra CTAs only after a first wave had finished, and the static
+    // tile schedule would make them run a full share of tiles on their own.
+    int per_tile = g_taps_sm_count / c.n_tiles;
     if (per_tile < 1) per_tile = 1;
     if (per_tile > p.tiles) per_tile = p.tiles;
     const dim3 grid(per_tile, c.n_tiles);

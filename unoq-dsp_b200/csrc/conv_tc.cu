@@ -949,7 +949,10 @@ int conv_tc_launch(const ConvTc &c, const int8_t *x, int8_t *y, const ConvGeom &
     }
     p.x_bytes = (long long)g.n * g.ih * g.iw * g.ic;
     const int m_tiles = (p.M + kBM - 1) / kBM;
-    int per_tile = (g_sm_count + c.n_tiles - 1) / c.n_tiles;
+    // CTAs per N tile: floor, so that all n_tiles * per_tile CTAs are resident at once (one per SM).
+    // Rounding up would start the extra CTAs only after a first wave had finished, and the static
+    // tile schedule would make them run a full share of tiles on their own.
+    int per_tile = g_sm_count / c.n_tiles;
     if (per_tile < 1) per_tile = 1;
     if (per_tile > m_tiles) per_tile = m_tiles;
     dim3 grid(per_tile, c.n_tiles);
