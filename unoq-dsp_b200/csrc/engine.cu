@@ -966,7 +966,7 @@ int Engine::run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint
 // Fixed device arena of the allocation-free entry point (ug_run_static): the reference's own
 // arena bound (runtime/graph.h:7). Nothing in it needs to start at zero: every activation is
 // written before it is read, and replicated constants are copied in at every call.
-__device__ __align__(256) uint8_t g_static_arena[kStaticArenaBytes];
+static __device__ __align__(256) uint8_t g_static_arena[kStaticArenaBytes];
 
 int Engine::run_static(const void *in, void *out) {
     if (!ready_ || !in || !out) return 22;
