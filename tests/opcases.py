@@ -289,6 +289,14 @@ def all_cases(scale=1):
     return [
         ("conv_pw_c0", lambda r: conv_case(r, (1, 8 * s, 8 * s, 64), 128, (1, 1), (1, 1))),
         ("conv_pw_ragged", lambda r: conv_case(r, (1, 5 * s, 7, 48), 40, (1, 1), (1, 1), act="none")),
+        # N tiles that are not powers of two: one 192-wide tile in four 48-column parts, three
+        # 192-wide tiles, four 256-wide tiles whose last holds 192 channels, 80 channels in a
+        # 96-wide tile, and a 3x3 conv with 96 channels on the 8-warp epilogue
+        ("conv_pw_oc192", lambda r: conv_case(r, (1, 6 * s, 7, 96), 192, (1, 1), (1, 1))),
+        ("conv_pw_oc576", lambda r: conv_case(r, (1, 3 * s, 7, 96), 576, (1, 1), (1, 1), act="none")),
+        ("conv_pw_oc960", lambda r: conv_case(r, (1, 2 * s, 7, 128), 960, (1, 1), (1, 1))),
+        ("conv_pw_oc80", lambda r: conv_case(r, (1, 5 * s, 9, 32), 80, (1, 1), (1, 1))),
+        ("conv_3x3_oc96", lambda r: conv_case(r, (1, 6 * s, 9, 32), 96, (3, 3), (1, 1))),
         ("conv_3x3_s1", lambda r: conv_case(r, (1, 9 * s, 7, 16), 24, (3, 3), (1, 1))),
         ("conv_3x3_s2", lambda r: conv_case(r, (1, 10 * s, 10, 32), 16, (3, 3), (2, 2), xq=(0.03, 17))),
         ("conv_stem_rgb", lambda r: conv_case(r, (1, 16 * s, 12, 3), 16, (3, 3), (2, 2), xq=(0.02, -13))),

@@ -737,23 +737,34 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
     BandGeom bg;
     if (mode != kPointwise && (g.ic % 16 == 0 || kc == 1) && band_geometry(g, bg)) mode = kBand;
     if (mode == kGather16 && g.ic % 16 != 0) return 0;
-    // N tiling: a power-of-two tile width (16..256, so staged tiles match a TMA swizzle span)
-    // no wider than the channel count needs, whose weights stay resident in shared memory.
-    int bn = 16;
-    while (bn < 256 && bn < g.oc) bn *= 2;
-    while (bn > 16 && (size_t)kc * bn * kBK > (size_t)kWeightBudget) bn /= 2;
-    if ((size_t)kc * bn * kBK > (size_t)kWeightBudget) return 0;
-    const int n_tiles = (g.oc + bn - 1) / bn;
+    // epilogue warps: 16 for pointwise convs (4 producer warps leave room; more warps hide the
+    // epilogue's latency), 8 for the other modes (8 producer warps)
+    const int ew = mode == kPointwise ? 16 : 8;
+    // N tiling: the fewest tiles of equal width (at most 256) that cover oc, each tile's weights
+    // resident in shared memory. The width is a multiple of 16 columns per epilogue part (see
+    // nparts below), so that no part's store box reaches into the next tile: 192 channels are one
+    // 192-wide tile and 576 three, where power-of-two widths would leave a quarter idle.
+    int n_tiles = (g.oc + 255) / 256, bn = 16;
+    for (;; n_tiles++) {
+        bn = std::max(16, ((g.oc + n_tiles - 1) / n_tiles + 15) & ~15);
+        const int align = bn > 128 && ew == 16 ? 64 : bn > 64 ? 32 : 16;
+        bn = (bn + align - 1) / align * align;
+        if ((size_t)kc * bn * kBK <= (size_t)kWeightBudget) break;
+        if (bn == 16) return 0;
+    }
     // Band table: per 16-byte chunk (ic % 16 == 0) one int, else per 4-byte word eight ints.
     const int tab_bytes = mode != kBand ? 16 : g.ic % 16 == 0 ? kc * 8 * 4 : (K32 / 4) * 32;
     int stages = 8, nbands = 0;
     const bool store_tma = (g.oc % 16) == 0;
-    // epilogue warps: 16 for pointwise convs (4 producer warps leave room; more warps hide the
-    // epilogue's latency), 8 for the other modes (8 producer warps)
-    const int ew = mode == kPointwise ? 16 : 8;
-    // columns per epilogue warp: up to 64 (a 64-byte TMA box), fewer warps per tile for narrow N
-    // tiles (the spare ones take other tiles, see fold), so fewer per-warp, per-tile fixed costs
-    const int box = std::max(std::min(bn, 64), bn / (ew / 4));
+    // column parts per tile (1, 2 or ew / 4 warps of each lane quarter): the fewest that keep a part
+    // within 64 columns, so narrow N tiles leave spare warps to take other tiles (see fold) and pay
+    // fewer per-warp, per-tile fixed costs. Parts are equal (bn / nparts, a multiple of 16 by the
+    // choice of bn); a 32 / 64 / 128-byte part is stored swizzled, others unswizzled, whose odd
+    // 16-byte multiples (48, 80, 112) still put the lanes of a 16-byte store in distinct banks.
+    int nparts = 1;
+    while (nparts < ew / 4 && bn / nparts > 64) nparts *= 2;
+    const int box = bn / nparts;
+    if (box % 16 != 0) return 0;
     const int out_bytes = store_tma ? (int)(2 * ew * warp_stage_bytes(box)) : (int)(2 * out_stride(bn));
     auto layout = [&]() {
         return Layout(stages, kc, bn, mode == kBand ? (int)bg.bytes() : 0, nbands, mode == kBand ? bg.fill_bytes : 0,
@@ -888,7 +899,8 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
     p.lo = q[14], p.hi = q[15];
     p.xzp = xzp;
     p.n_acc = bn <= 128 ? 4 : 2;
-    p.tmem_cols = std::max(32, p.n_acc * bn);
+    p.tmem_cols = 32;  // a power of two (tcgen05.alloc)
+    while (p.tmem_cols < p.n_acc * bn) p.tmem_cols *= 2;
     p.store_tma = store_tma;
     if (add) {
         p.add_tab = add->q_dev;
@@ -899,8 +911,9 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
         c->fused = true;
     }
     p.box = box;
-    // narrow N tiles: spare epilogue warps of each lane quarter take alternate tiles (divides n_acc)
-    p.fold = store_tma ? (ew / 4) / ((bn + box - 1) / box) : 1;
+    // narrow N tiles: spare epilogue warps of each lane quarter take alternate tiles; the kernel
+    // splits each quarter's ew / 4 warps into (ew / 4) / fold column parts x fold tile phases
+    p.fold = store_tma ? (ew / 4) / nparts : 1;
     p.out_bytes = out_bytes;
     p.swz = p.box == 128 ? 3 : p.box == 64 ? 2 : p.box == 32 ? 1 : 0;
     p.mode = mode;
