@@ -42,6 +42,9 @@ struct DwParams {
     int cb, th;             // channels per block, output rows per tile
     int tiles_x, tiles_y;
     int ir, pw, plane;      // input rows per tile, words per plane row, words per plane (odd)
+    int cb_shift;           // log2(cb)
+    // multiply-shift division (no run-time divide in the per-unit index arithmetic)
+    FastDiv f_tx, f_ty, f_pw, f_ir;
 };
 
 __device__ __forceinline__ void transpose4(uint32_t x0, uint32_t x1, uint32_t x2, uint32_t x3, uint32_t (&y)[4]) {
@@ -84,11 +87,8 @@ __global__ void __launch_bounds__(512, (K == 3 && S == 1) ? 4 : 3) dw_kernel(con
     uint32_t *sPlane = reinterpret_cast<uint32_t *>(smem + 256);            // [cb][plane words]
     uint8_t *sOut = smem + 256 + (size_t)cb * p.plane * 4;                  // [th][8][cb]
 
-    int tile = blockIdx.x;
-    const int tx = tile % p.tiles_x;
-    tile /= p.tiles_x;
-    const int ty = tile % p.tiles_y;
-    const int n = tile / p.tiles_y;
+    const int t1 = p.f_tx.div((int)blockIdx.x), tx = (int)blockIdx.x - t1 * p.tiles_x;
+    const int n = p.f_ty.div(t1), ty = t1 - n * p.tiles_y;
     const int c0 = blockIdx.y * cb;
     const int iy0 = ty * th * S - p.pt, ix0 = tx * kTW * S - p.pl;
 
@@ -100,8 +100,8 @@ __global__ void __launch_bounds__(512, (K == 3 && S == 1) ? 4 : 3) dw_kernel(con
         const uint4 fill = make_uint4(fillw, fillw, fillw, fillw);
         const int units = (cb / 16) * p.ir * p.pw;
         for (int u = threadIdx.x; u < units; u += blockDim.x) {
-            const int wc = u % p.pw, rest = u / p.pw;
-            const int row = rest % p.ir, chunk = rest / p.ir;
+            const int rest = p.f_pw.div(u), wc = u - rest * p.pw;
+            const int chunk = p.f_ir.div(rest), row = rest - chunk * p.ir;
             const int iy = iy0 + row;
             uint4 px[4];
 #pragma unroll
@@ -126,7 +126,7 @@ __global__ void __launch_bounds__(512, (K == 3 && S == 1) ? 4 : 3) dw_kernel(con
     }
 
     // ---- this thread: channel ch, output rows 2 * rg, 2 * rg + 1 of the tile
-    const int ch = threadIdx.x % cb, rg = threadIdx.x / cb;
+    const int ch = threadIdx.x & (cb - 1), rg = threadIdx.x >> p.cb_shift;
     const int c = c0 + ch;
     uint32_t wa[K], wb[K];
 #pragma unroll
@@ -177,7 +177,7 @@ __global__ void __launch_bounds__(512, (K == 3 && S == 1) ? 4 : 3) dw_kernel(con
     // ---- copy-out: 16 channels of one pixel per store
     const int units = th * kTW * (cb / 16);
     for (int u = threadIdx.x; u < units; u += blockDim.x) {
-        const int chunk = u % (cb / 16), pix = u / (cb / 16);
+        const int chunk = u & ((cb >> 4) - 1), pix = u >> (p.cb_shift - 4);
         const int j = pix % kTW, row = pix / kTW;
         const int oy = ty * th + row, ox = tx * kTW + j;
         if (oy >= p.oh || ox >= p.ow) continue;
@@ -255,6 +255,11 @@ int dw_prepare(const int8_t *w, const int32_t *q, const uint8_t *post_dev, const
     p.tiles_y = (g.oh + p.th - 1) / p.th;
     p.ir = (p.th - 1) * S + K;
     p.pw = ((kTW - 1) * S + K + 3) / 4;
+    p.cb_shift = cb == 16 ? 4 : cb == 32 ? 5 : 6;
+    p.f_tx = FastDiv(p.tiles_x);
+    p.f_ty = FastDiv(p.tiles_y);
+    p.f_pw = FastDiv(p.pw);
+    p.f_ir = FastDiv(p.ir);
     p.plane = p.ir * p.pw;
     if ((p.plane & 1) == 0) p.plane++;  // odd plane stride: lanes (channels) fall in distinct banks
     d->k = K, d->s = S, d->epi = epi_mode, d->threads = cb * rg;
