@@ -76,6 +76,8 @@ enum Mode { kPointwise = 0, kGather16 = 1, kBand = 2 };
 
 struct Params {
     CUtensorMap ymap;          // output [M rows][oc] int8, box {min(bn,128), 128}, swizzled (TMA store)
+    CUtensorMap xmap;          // pointwise input [M rows][ic] int8, box {128, 128}, SWIZZLE_128B (a_tma)
+    int a_tma;                 // pointwise A tiles by TMA (one thread) instead of cp.async
     const int8_t *x;
     int8_t *y;
     const int8_t *w;           // [n_tiles][kc][BN x 128] swizzled
@@ -162,6 +164,18 @@ namespace {
 // y = clamp(scale(T_conv[v + 128] + T_res[r + 128]) + zp) with the add's scale as requant.cuh
 // constants; rows past M (the last tile) read no residual and are never stored.
 
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
 template <int EPI, int PW, int EW>
 __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(const __grid_constant__ Params p) {
     using R = Roles<PW, EW>;
@@ -202,7 +216,7 @@ __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(con
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
-            mbar_init(smem_u32(full + s), kProducerWarps);
+            mbar_init(smem_u32(full + s), p.a_tma ? 1 : kProducerWarps);
             mbar_init(smem_u32(empty + s), 1);
         }
         for (int a = 0; a < 4; a++) {
@@ -261,7 +275,32 @@ __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(con
         if (lane == 0) mbar_arrive(smem_u32(bfull));
 
         long long it = 0;
-        if (p.mode != kBand) {
+        if (p.a_tma) {
+            // Pointwise A tiles by TMA: producer thread 0 loads each stage as one 128 x 128-byte box
+            // of the [M][ic] input, already in the SWIZZLE_128B layout. Columns past ic and rows past
+            // M read as zero (the zero columns meet zero weights; those rows are never stored).
+            if (t == 0) {
+                bool ok = true;
+                for (int mt = blockIdx.x; mt < m_tiles && ok; mt += gridDim.x)
+                    for (int kc = 0; kc < p.kc; kc++, it++) {
+                        const int s = (int)(it % S);
+                        if (!mbar_wait(smem_u32(empty + s), (uint32_t)(((it / S) & 1) ^ 1), abort, 111)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_expect_tx(smem_u32(full + s), (uint32_t)kStageBytes);
+                        tma_load_2d(smem_u32(sA + (size_t)s * kStageBytes), &p.xmap, kc * kBK, mt * kBM,
+                                    smem_u32(full + s));
+                    }
+                // every load issued has landed before the CTA may exit (bounded)
+                for (long long q = it - (it < S ? it : S); q < it; q++) {
+                    const long long start = clock64();
+                    while (!mbar_try_wait(smem_u32(full + (int)(q % S)), (uint32_t)((q / S) & 1), 200000) &&
+                           clock64() - start < kTimeoutCycles) {
+                    }
+                }
+            }
+        } else if (p.mode != kBand) {
             const int j = t & 7;    // 16-byte chunk of the 128-byte stage row
             const int r0 = t >> 3;  // rows r0 + kRowStep i
             const uint32_t fillw = 0x01010101u * (uint32_t)(uint8_t)p.xzp;
@@ -917,6 +956,11 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
     p.out_bytes = out_bytes;
     p.swz = p.box == 128 ? 3 : p.box == 64 ? 2 : p.box == 32 ? 1 : 0;
     p.mode = mode;
+    {
+        // pointwise A tiles by TMA unless switched off (UNOQ_CONV_TC_ATMA=0: per-thread cp.async)
+        const char *ea = std::getenv("UNOQ_CONV_TC_ATMA");
+        p.a_tma = mode == kPointwise && !(ea && ea[0] == '0');
+    }
     p.band_bytes = mode == kBand ? (int)bg.bytes() : 0;
     p.nbands = nbands;
     p.band_rows = bg.rows;
@@ -958,6 +1002,20 @@ int conv_tc_launch(const ConvTc &c, const int8_t *x, int8_t *y, const ConvGeom &
                                                    : CU_TENSOR_MAP_SWIZZLE_NONE;
         if (enc(&p.ymap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                 CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return 2001;
+    }
+    if (p.a_tma) {
+        // Input [M][ic] int8. The box is one A stage: 128 reduction bytes x 128 pixels; its x
+        // coordinate (a multiple of 128) meets the 16-byte rule of tiled TMA loads.
+        EncodeTiled enc = encoder();
+        if (!enc || (reinterpret_cast<uintptr_t>(x) & 15) != 0) return 2001;
+        const cuuint64_t dims[2] = {(cuuint64_t)g.ic, (cuuint64_t)p.M};
+        const cuuint64_t strides[1] = {(cuuint64_t)g.ic};
+        const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kBM};
+        const cuuint32_t estr[2] = {1, 1};
+        if (enc(&p.xmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t *>(x), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return 2001;
     }
     p.x_bytes = (long long)g.n * g.ih * g.iw * g.ic;
