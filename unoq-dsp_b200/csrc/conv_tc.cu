@@ -14,9 +14,9 @@
 //         the reference feeds its dot product there (qnn.c:1166-1168) -- so no border
 //         correction is needed. A warp signals a stage a few stages after issuing it, once its
 //         copies have landed, so several stages of copies stay in flight per thread.
-//       - other channel counts (the 3-channel RGB stem, ic = 8): the input rows a tile touches
-//         (a "band") are copied to shared memory with 16-byte cp.async, double-buffered across
-//         tiles, and each thread then assembles its pixel's K bytes from the band.
+//       - other spatial convs whose input rows fit: the input rows a tile touches (a "band") are
+//         copied to shared memory by a loader warp (one bulk copy per row, 2-3 bands in flight),
+//         and the producers assemble each pixel's K bytes from the band.
 //   * warp 12 (one thread) issues tcgen05.mma.kind::i8 (s8 x s8 -> s32, M=128, N=BN, K=32)
 //     into one of two TMEM accumulators, so the epilogue of tile i overlaps the MMAs of i+1.
 //   * warps 4-11 read the accumulator with tcgen05.ld (thread = pixel row, 16 channels per load,
@@ -60,7 +60,10 @@ struct Roles {
     static constexpr int kEpilogues = EW * 32;
     static constexpr int kParts = EW / 4;
     static constexpr int kMmaWarp = PW + EW;
-    static constexpr int kThreads = (kMmaWarp + 1) * 32;
+    // band / gather configurations (8 producer warps) add one warp that fetches the bands
+    static constexpr bool kLoader = PW == 8;
+    static constexpr int kLoaderWarp = kMmaWarp + 1;
+    static constexpr int kThreads = (kMmaWarp + 1 + (kLoader ? 1 : 0)) * 32;
     static constexpr int kProducers = PW * 32;
     // 16-byte-chunk producers: thread t builds chunk t % 8 of rows t / 8 + kRowStep * i, i < kRowIters.
     static constexpr int kRowStep = kProducers / 8;
@@ -176,6 +179,25 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
         : "memory");
 }
 
+// One contiguous global -> shared bulk copy (no tensor map, no multicast); both addresses 16-byte
+// aligned, `bytes` a multiple of 16. Completes `bytes` of transactions on `bar`.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+// Band of M tile `mt` (band mode): global input rows [g_lo, g_lo + rows), image-major rows being
+// contiguous in memory.
+__device__ __forceinline__ void band_of(const Params &p, int mt, long long &g_lo, int &rows) {
+    const int m0 = mt * kBM, m1 = min(p.M, m0 + kBM) - 1;
+    const int n0 = p.f_img.div(m0), oy0 = p.f_ow.div(m0 - n0 * p.f_img.d);
+    const int n1 = p.f_img.div(m1), oy1 = p.f_ow.div(m1 - n1 * p.f_img.d);
+    g_lo = (long long)n0 * p.ih + max(0, oy0 * p.sh - p.pt);
+    const long long g_hi = (long long)n1 * p.ih + max(-1, min(p.ih - 1, oy1 * p.sh - p.pt + (p.kh - 1) * p.dh));
+    rows = g_hi >= g_lo ? (int)(g_hi - g_lo + 1) : 0;
+}
+
 template <int EPI, int PW, int EW>
 __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(const __grid_constant__ Params p) {
     using R = Roles<PW, EW>;
@@ -227,7 +249,7 @@ __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(con
         mbar_init(smem_u32(drain), 1);
         mbar_init(smem_u32(psync), kProducerWarps);
         for (int b = 0; b < 4; b++) {
-            mbar_init(smem_u32(bandfull + b), kProducers);  // every producer, on completion of its copies
+            mbar_init(smem_u32(bandfull + b), 1);  // the loader's expect_tx; its bulk copies complete the bytes
             mbar_init(smem_u32(bandfree + b), kProducerWarps);
         }
         mbar_init(smem_u32(esync), kEpilogueWarps);
@@ -384,10 +406,10 @@ __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(con
             if (lane == 0)
                 for (long long q = it - pending; q < it; q++) mbar_arrive(smem_u32(full + (int)(q % S)));
         } else {
-            // Band mode: the input rows a tile touches (its "band") are copied to shared memory with
-            // contiguous 16-byte cp.async, each row framed by margins of the input zero point, with
-            // up to nb bands in flight; A rows are then assembled from the band. Rows above or below
-            // the image read a shared row of zero-point bytes instead.
+            // Band mode: the input rows a tile touches (its "band") sit in shared memory, each row
+            // framed by margins of the input zero point, with up to nb bands in flight (fetched by
+            // the loader warp); A rows are assembled from the band. Rows above or below the image
+            // read a shared row of zero-point bytes instead.
             const int pitch = p.pitch, ML = p.ml;
             const uint32_t buf_bytes = (uint32_t)p.band_bytes;
             const uint32_t band0 = smem_u32(sBand), fillrow = band0 + (uint32_t)p.nbands * buf_bytes + 16;
@@ -405,49 +427,19 @@ __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(con
                 for (int q = t; q < (p.fill_bytes >> 4); q += kProducers) st_shared16(fillrow - 16 + q * 16, f);
             }
             unsigned round = 0;
-            const long long row_bytes = (long long)p.iw * p.ic;
-            // band of tile `mt`: global input rows [g_lo, g_lo + rows) (image-major rows are contiguous)
-            auto band_of = [&](int mt, long long &g_lo, int &rows) {
-                const int m0 = mt * kBM, m1 = min(p.M, m0 + kBM) - 1;
-                const int n0 = p.f_img.div(m0), oy0 = p.f_ow.div(m0 - n0 * p.f_img.d);
-                const int n1 = p.f_img.div(m1), oy1 = p.f_ow.div(m1 - n1 * p.f_img.d);
-                g_lo = (long long)n0 * p.ih + max(0, oy0 * p.sh - p.pt);
-                const long long g_hi =
-                    (long long)n1 * p.ih + max(-1, min(p.ih - 1, oy1 * p.sh - p.pt + (p.kh - 1) * p.dh));
-                rows = g_hi >= g_lo ? (int)(g_hi - g_lo + 1) : 0;
-            };
-            // The producers fetch the band of this CTA's tile f into buffer f % nb (warp w copies rows
-            // w, w + 8, ...) once every producer warp has released that buffer's previous band (tile
-            // f - nb); each thread's copies complete onto the buffer's band-full barrier.
+            // The loader warp fetches each tile's band into buffer (tile index) % nb; the producers
+            // wait for it, assemble, and release the buffer.
             const int nb = p.nbands;
-            const int my_tiles = blockIdx.x < m_tiles ? (m_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-            auto prefetch = [&](int f) -> bool {
-                const int b = f % nb;
-                if (f >= nb && !mbar_wait(smem_u32(bandfree + b), (uint32_t)((f / nb - 1) & 1), abort, 106)) return false;
-                long long g_lo;
-                int rows;
-                band_of(blockIdx.x + f * gridDim.x, g_lo, rows);
-                const uint8_t *src = reinterpret_cast<const uint8_t *>(p.x) + g_lo * row_bytes;
-                const uint32_t dst = band0 + (uint32_t)b * buf_bytes + (uint32_t)ML;
-                for (int r = warp; r < rows; r += kProducerWarps)
-                    for (int c = lane; c < p.row16; c += 32)
-                        cp_async16(dst + (uint32_t)(r * pitch + c * 16), src + r * row_bytes + c * 16);
-                asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bandfull + b))
-                             : "memory");
-                return true;
-            };
             // the zero-point margins written above are read by every warp
             bool ok = role_sync(smem_u32(psync), round, abort, 109);
-            for (int f = 0; f < nb - 1 && f < my_tiles && ok; f++) ok = prefetch(f);
             int i_tile = 0;
             for (int mt = blockIdx.x; mt < m_tiles && ok; mt += gridDim.x, i_tile++) {
                 const int bsel = i_tile % nb;
                 const uint32_t bandb = band0 + (uint32_t)bsel * buf_bytes;
-                if (i_tile + nb - 1 < my_tiles && !prefetch(i_tile + nb - 1)) break;
                 if (!mbar_wait(smem_u32(bandfull + bsel), (uint32_t)((i_tile / nb) & 1), abort, 110)) break;
                 long long g_lo;
                 int rows;
-                band_of(mt, g_lo, rows);
+                band_of(p, mt, g_lo, rows);
                 if (p.ic % 16 == 0) {
                     // 16-byte chunks: thread (j = t % 8, r0 = t / 8) builds chunk j of rows r0 + kRowStep i.
                     const int j = t & 7, r0 = t >> 3;
@@ -575,6 +567,40 @@ __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(con
             mma_commit(smem_u32(drain));
             const long long start = clock64();
             while (!mbar_try_wait(smem_u32(drain), 0, 200000) && clock64() - start < kTimeoutCycles) {
+            }
+        }
+        __syncwarp();
+    } else if (R::kLoader && warp == R::kLoaderWarp) {
+        // ------------------------------------------------------------------ band loader
+        // One thread fetches the band of this CTA's tile f into buffer f % nb, one bulk copy per
+        // input row into its slot between the zero-point margins, once the producers have released
+        // that buffer's previous band (tile f - nb). The copies complete their bytes on the buffer's
+        // band-full barrier. A warp of its own, so the assembling producer warps stay in step.
+        if (lane == 0 && p.mode == kBand) {
+            const int nb = p.nbands;
+            const int my_tiles = blockIdx.x < m_tiles ? (m_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+            const long long row_bytes = (long long)p.iw * p.ic;
+            const uint32_t band0 = smem_u32(sBand), buf_bytes = (uint32_t)p.band_bytes;
+            int f = 0;
+            for (; f < my_tiles; f++) {
+                const int b = f % nb;
+                if (f >= nb && !mbar_wait(smem_u32(bandfree + b), (uint32_t)((f / nb - 1) & 1), abort, 106)) break;
+                long long g_lo;
+                int rows;
+                band_of(p, blockIdx.x + f * gridDim.x, g_lo, rows);
+                const uint8_t *src = reinterpret_cast<const uint8_t *>(p.x) + g_lo * row_bytes;
+                const uint32_t dst = band0 + (uint32_t)b * buf_bytes + (uint32_t)p.ml;
+                const uint32_t bar = smem_u32(bandfull + b);
+                mbar_expect_tx(bar, (uint32_t)(rows * row_bytes));
+                for (int r = 0; r < rows; r++)
+                    bulk_load(dst + (uint32_t)(r * p.pitch), src + r * row_bytes, (uint32_t)row_bytes, bar);
+            }
+            // every band issued has landed before the CTA may exit (bounded)
+            for (int q = f - (f < nb ? f : nb); q < f; q++) {
+                const long long start = clock64();
+                while (!mbar_try_wait(smem_u32(bandfull + q % nb), (uint32_t)((q / nb) & 1), 200000) &&
+                       clock64() - start < kTimeoutCycles) {
+                }
             }
         }
         __syncwarp();
