@@ -5,12 +5,12 @@
 // then y = post[clamp(scale(acc, m, s) + yzp)]. Here the +128 is folded into the bias on the
 // host (bias' = bias + 128 * sum w), so the device accumulates signed x * w with dp4a.
 //
-// Block = one output tile (TH rows x 8 columns) of one image for CB channels.
+// Block = one output tile (TH rows x TW = 7 or 8 columns) of one image for CB channels.
 //  * Fill: the input tile plus halo is read with 16-byte loads (4 pixels x 16 channels per
 //    thread, zero point outside the image), transposed in registers with byte permutes, and
 //    stored as byte planes: plane[channel][row][column], 4 columns per 32-bit word. Each input
 //    byte leaves HBM once per tile.
-//  * Compute: a thread owns one channel x 8 adjacent output pixels x 2 output rows. For every
+//  * Compute: a thread owns one channel x TW adjacent output pixels x 2 output rows. For every
 //    input row it loads the row's words once, forms the sliding 4-column windows with funnel
 //    shifts, and adds 4 taps per dp4a against the channel's weight words; the 5th tap of a
 //    5-wide row is byte 3 of the next window, so it costs one dp4a and no shift. Each loaded row
@@ -28,7 +28,6 @@ namespace uq {
 
 namespace {
 
-constexpr int kTW = 8;   // output columns per tile (one thread row)
 constexpr int kR = 2;    // output rows per thread
 
 struct DwParams {
@@ -76,12 +75,14 @@ __device__ __forceinline__ int32_t requant(int32_t acc, const EpiChan &e, int lo
 // than 2), 3 elsewhere (4 spills on the 5x5 and stride-2 shapes). Each block's fill, compute and
 // store run back to back, so resident blocks are what overlaps one block's loads with another's
 // arithmetic.
-template <int K, int S, int EPI>
+// TW = output columns per tile (one thread's row of outputs): 7 or 8, whichever wastes fewer
+// columns of the layer's width (7 for MobileNetV4's 28 / 14 / 7-wide layers).
+template <int K, int S, int EPI, int TW>
 __global__ void __launch_bounds__(512, (K == 3 && S == 1) ? 4 : 3) dw_kernel(const DwParams p) {
     extern __shared__ __align__(16) uint8_t smem[];
-    constexpr int TWIN = (kTW - 1) * S + K;       // input columns per tile
+    constexpr int TWIN = (TW - 1) * S + K;       // input columns per tile
     constexpr int NWORD = (TWIN + 3) / 4;         // words per input row
-    constexpr int NWIN = (kTW - 1) * S + 2;       // window starts 0 .. (7*S + 1)
+    constexpr int NWIN = (TW - 1) * S + 2;        // window starts 0 .. ((TW - 1) * S + 1)
     const int cb = p.cb, th = p.th;
     uint8_t *sLut = smem;                                                   // 256 bytes
     uint32_t *sPlane = reinterpret_cast<uint32_t *>(smem + 256);            // [cb][plane words]
@@ -90,7 +91,7 @@ __global__ void __launch_bounds__(512, (K == 3 && S == 1) ? 4 : 3) dw_kernel(con
     const int t1 = p.f_tx.div((int)blockIdx.x), tx = (int)blockIdx.x - t1 * p.tiles_x;
     const int n = p.f_ty.div(t1), ty = t1 - n * p.tiles_y;
     const int c0 = blockIdx.y * cb;
-    const int iy0 = ty * th * S - p.pt, ix0 = tx * kTW * S - p.pl;
+    const int iy0 = ty * th * S - p.pt, ix0 = tx * TW * S - p.pl;
 
     if (p.post)
         for (int i = threadIdx.x; i < 256; i += blockDim.x) sLut[i] = p.post[i];
@@ -137,11 +138,11 @@ __global__ void __launch_bounds__(512, (K == 3 && S == 1) ? 4 : 3) dw_kernel(con
     const EpiChan e = p.epi[c];
     __syncthreads();
 
-    int acc[kR][kTW];
+    int acc[kR][TW];
 #pragma unroll
     for (int r = 0; r < kR; r++)
 #pragma unroll
-        for (int j = 0; j < kTW; j++) acc[r][j] = 0;
+        for (int j = 0; j < TW; j++) acc[r][j] = 0;
     const uint32_t *plane = sPlane + (size_t)ch * p.plane + (size_t)(rg * kR * S) * p.pw;
     // input rows used by the thread's two output rows: (kR - 1) * S + K
 #pragma unroll
@@ -158,7 +159,7 @@ __global__ void __launch_bounds__(512, (K == 3 && S == 1) ? 4 : 3) dw_kernel(con
             const int ky = ir - r * S;
             if (ky < 0 || ky >= K) continue;
 #pragma unroll
-            for (int j = 0; j < kTW; j++) {
+            for (int j = 0; j < TW; j++) {
                 acc[r][j] = __dp4a((int)win[j * S], (int)wa[ky], acc[r][j]);
                 if (K == 5) acc[r][j] = __dp4a((int)win[j * S + 1], (int)wb[ky], acc[r][j]);
             }
@@ -168,46 +169,57 @@ __global__ void __launch_bounds__(512, (K == 3 && S == 1) ? 4 : 3) dw_kernel(con
 #pragma unroll
     for (int r = 0; r < kR; r++)
 #pragma unroll
-        for (int j = 0; j < kTW; j++) {
+        for (int j = 0; j < TW; j++) {
             int32_t v = requant<EPI>(acc[r][j], e, p.lo, p.hi);
             if (lut) v = (int8_t)lut[v + 128];
-            sOut[((size_t)(rg * kR + r) * kTW + j) * cb + ch] = (uint8_t)v;
+            sOut[((size_t)(rg * kR + r) * TW + j) * cb + ch] = (uint8_t)v;
         }
     __syncthreads();
     // ---- copy-out: 16 channels of one pixel per store
-    const int units = th * kTW * (cb / 16);
+    const int units = th * TW * (cb / 16);
     for (int u = threadIdx.x; u < units; u += blockDim.x) {
         const int chunk = u & ((cb >> 4) - 1), pix = u >> (p.cb_shift - 4);
-        const int j = pix % kTW, row = pix / kTW;
-        const int oy = ty * th + row, ox = tx * kTW + j;
+        const int j = pix % TW, row = pix / TW;
+        const int oy = ty * th + row, ox = tx * TW + j;
         if (oy >= p.oh || ox >= p.ow) continue;
         *reinterpret_cast<uint4 *>(p.y + (((size_t)n * p.oh + oy) * p.ow + ox) * p.c + c0 + chunk * 16) =
             *reinterpret_cast<const uint4 *>(sOut + (size_t)pix * cb + chunk * 16);
     }
 }
 
-template <int K, int S>
+template <int K, int S, int TW>
 void launch_shape(const DwParams &p, int epi, dim3 grid, int threads, size_t smem, cudaStream_t s) {
-    if (epi == 0) dw_kernel<K, S, 0><<<grid, threads, smem, s>>>(p);
-    else if (epi == 1) dw_kernel<K, S, 1><<<grid, threads, smem, s>>>(p);
-    else dw_kernel<K, S, 2><<<grid, threads, smem, s>>>(p);
+    if (epi == 0) dw_kernel<K, S, 0, TW><<<grid, threads, smem, s>>>(p);
+    else if (epi == 1) dw_kernel<K, S, 1, TW><<<grid, threads, smem, s>>>(p);
+    else dw_kernel<K, S, 2, TW><<<grid, threads, smem, s>>>(p);
+}
+
+template <int K, int S, int TW>
+bool allow_smem_tw(size_t bytes) {
+    return cudaFuncSetAttribute(dw_kernel<K, S, 0, TW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) ==
+               cudaSuccess &&
+           cudaFuncSetAttribute(dw_kernel<K, S, 1, TW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) ==
+               cudaSuccess &&
+           cudaFuncSetAttribute(dw_kernel<K, S, 2, TW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) ==
+               cudaSuccess;
 }
 
 template <int K, int S>
 bool allow_smem(size_t bytes) {
-    return cudaFuncSetAttribute(dw_kernel<K, S, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) ==
-               cudaSuccess &&
-           cudaFuncSetAttribute(dw_kernel<K, S, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) ==
-               cudaSuccess &&
-           cudaFuncSetAttribute(dw_kernel<K, S, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) ==
-               cudaSuccess;
+    return allow_smem_tw<K, S, 7>(bytes) && allow_smem_tw<K, S, 8>(bytes);
+}
+
+template <int K, int S>
+void launch_tw(const DwParams &p, int tw, int epi, dim3 grid, int threads, size_t smem, cudaStream_t s) {
+    if (tw == 7) launch_shape<K, S, 7>(p, epi, grid, threads, smem, s);
+    else launch_shape<K, S, 8>(p, epi, grid, threads, smem, s);
 }
 
 }  // namespace
 
 struct DwFast {
     DwParams p{};
-    int k = 3, s = 1, epi = 0, threads = 0;
+    int k = 3, s = 1, epi = 0, threads = 0, tw = 8;
     size_t smem = 0;
 };
 
@@ -240,8 +252,10 @@ int dw_prepare(const int8_t *w, const int32_t *q, const uint8_t *post_dev, const
     const int epi_mode = !fast ? 2 : (q[14] >= yzp ? 0 : 1);
     if (epi_mode != 2)
         for (auto &e : epi) e.sh = e.sh >= 32 ? e.sh - 32 : 0;
-    // Tile: 8 columns; the whole image height when it is at most 32 rows, else 16 rows.
+    // Tile: 7 or 8 columns; the whole image height when it is at most 32 rows, else 16 rows.
     const int rg = g.oh <= 32 ? (g.oh + kR - 1) / kR : 8;
+    // tile width: 7 or 8 output columns, whichever leaves fewer computed columns past the image
+    const int tw = ((g.ow + 6) / 7 * 7 - g.ow) < ((g.ow + 7) / 8 * 8 - g.ow) ? 7 : 8;
     // channels per block: 32 for stride 1 (smaller blocks, more of them resident: 7-10% faster on
     // the 14x14 and 28x28 layers), 64 for stride 2 (wider halo reuse; 32 was up to 45% slower)
     int cb = S == 1 ? 32 : 64;
@@ -251,10 +265,10 @@ int dw_prepare(const int8_t *w, const int32_t *q, const uint8_t *post_dev, const
     DwParams &p = d->p;
     p.cb = cb;
     p.th = rg * kR;
-    p.tiles_x = (g.ow + kTW - 1) / kTW;
+    p.tiles_x = (g.ow + tw - 1) / tw;
     p.tiles_y = (g.oh + p.th - 1) / p.th;
     p.ir = (p.th - 1) * S + K;
-    p.pw = ((kTW - 1) * S + K + 3) / 4;
+    p.pw = ((tw - 1) * S + K + 3) / 4;
     p.cb_shift = cb == 16 ? 4 : cb == 32 ? 5 : 6;
     p.f_tx = FastDiv(p.tiles_x);
     p.f_ty = FastDiv(p.tiles_y);
@@ -262,8 +276,8 @@ int dw_prepare(const int8_t *w, const int32_t *q, const uint8_t *post_dev, const
     p.f_ir = FastDiv(p.ir);
     p.plane = p.ir * p.pw;
     if ((p.plane & 1) == 0) p.plane++;  // odd plane stride: lanes (channels) fall in distinct banks
-    d->k = K, d->s = S, d->epi = epi_mode, d->threads = cb * rg;
-    d->smem = 256 + (size_t)cb * p.plane * 4 + (size_t)p.th * kTW * cb;
+    d->k = K, d->s = S, d->epi = epi_mode, d->threads = cb * rg, d->tw = tw;
+    d->smem = 256 + (size_t)cb * p.plane * 4 + (size_t)p.th * tw * cb;
     if (d->smem > 200 * 1024) {
         delete d;
         return 0;
@@ -298,10 +312,10 @@ int dw_launch(const DwFast &d, const int8_t *x, int8_t *y, const ConvGeom &g, cu
     p.y = y;
     p.n = g.n;
     dim3 grid((unsigned)(p.n * p.tiles_y * p.tiles_x), (unsigned)(p.c / p.cb));
-    if (d.k == 3 && d.s == 1) launch_shape<3, 1>(p, d.epi, grid, d.threads, d.smem, s);
-    else if (d.k == 3) launch_shape<3, 2>(p, d.epi, grid, d.threads, d.smem, s);
-    else if (d.s == 1) launch_shape<5, 1>(p, d.epi, grid, d.threads, d.smem, s);
-    else launch_shape<5, 2>(p, d.epi, grid, d.threads, d.smem, s);
+    if (d.k == 3 && d.s == 1) launch_tw<3, 1>(p, d.tw, d.epi, grid, d.threads, d.smem, s);
+    else if (d.k == 3) launch_tw<3, 2>(p, d.tw, d.epi, grid, d.threads, d.smem, s);
+    else if (d.s == 1) launch_tw<5, 1>(p, d.tw, d.epi, grid, d.threads, d.smem, s);
+    else launch_tw<5, 2>(p, d.tw, d.epi, grid, d.threads, d.smem, s);
     return 0;
 }
 
