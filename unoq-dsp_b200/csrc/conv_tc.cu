@@ -7,22 +7,23 @@
 //   * W: the N tile's weights, prepared on the host in the UMMA K-major SWIZZLE_128B layout
 //     (8-row x 128-byte atoms, 16-byte chunks XOR-swizzled by row), copied to shared memory
 //     once and kept resident.
-//   * A (warps 0-3): the im2col rows of a tile, 128 reduction bytes per pipeline stage, built
-//     straight into the swizzled layout.
-//       - 16-byte channel blocks (ic % 16 == 0): cp.async per (pixel, 16 channels); taps outside
-//         the image get 16 bytes of the input zero point by a plain shared store -- the value
-//         the reference feeds its dot product there (qnn.c:1166-1168) -- so no border
-//         correction is needed. A warp signals a stage a few stages after issuing it, once its
-//         copies have landed, so several stages of copies stay in flight per thread.
+//   * A (producer warps, 4 or 8): the im2col rows of a tile, 128 reduction bytes per pipeline
+//     stage, in the swizzled layout.
+//       - pointwise: one 128 x 128-byte TMA box per stage, issued by one producer thread.
 //       - other spatial convs whose input rows fit: the input rows a tile touches (a "band") are
 //         copied to shared memory by a loader warp (one bulk copy per row, 2-3 bands in flight),
 //         and the producers assemble each pixel's K bytes from the band.
-//   * warp 12 (one thread) issues tcgen05.mma.kind::i8 (s8 x s8 -> s32, M=128, N=BN, K=32)
-//     into one of two TMEM accumulators, so the epilogue of tile i overlaps the MMAs of i+1.
-//   * warps 4-11 read the accumulator with tcgen05.ld (thread = pixel row, 16 channels per load,
-//     two warps per TMEM lane quarter on alternating chunks), requantise with the exact
-//     branch-free form of the reference's `scale` (make_epilogue), apply the optional post
-//     table, stage the int8 tile in shared memory and write it out with coalesced stores.
+//       - the rest (ic % 16 == 0): cp.async per (pixel, 16 channels); taps outside the image get
+//         16 bytes of the input zero point by a plain shared store -- the value the reference
+//         feeds its dot product there (qnn.c:1166-1168) -- so no border correction is needed. A
+//         warp signals a stage a few stages after issuing it, once its copies have landed.
+//   * the MMA warp (one thread) issues tcgen05.mma.kind::i8 (s8 x s8 -> s32, M=128, N=BN, K=32)
+//     into 2-4 TMEM accumulators in rotation, so the epilogue of tile i overlaps later MMAs.
+//   * the epilogue warps (8 or 16) read the accumulator with tcgen05.ld (thread = pixel row, 16
+//     channels per load; each warp owns an equal column part of the tile), requantise with the
+//     exact branch-free form of the reference's `scale` (make_epilogue), apply the optional post
+//     table or fused residual add, stage the int8 part in shared memory and write it out with
+//     their own TMA tensor stores.
 //
 // Reference arithmetic: the reference multiplies u8 columns (x ^ 0x80) by s8 weights and adds a
 // corrected bias; with s8 columns the same sum is  sum x*w + 128*sum(w) + xzp*sum(w_kpad), which
