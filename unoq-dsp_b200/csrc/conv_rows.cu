@@ -53,6 +53,7 @@ struct RowsParams {
     int kh, kw, s, pt, pl;
     int G, bn;             // output pixels per column group; bn = G * oc
     int groups, row_tiles, tiles;
+    int R, ipt;            // M tile = R output rows of each of ipt = 128 / R consecutive images
     int ksteps;            // 32-byte K steps of a kernel row's window
     int x0;                // window start (bytes, 16-aligned, may be negative) of group 0; group g adds g * gstep
     int gstep;
@@ -159,7 +160,7 @@ __global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    const int per_image = p.row_tiles * p.groups;
+    const int per_group = p.row_tiles * p.groups;  // tiles per group of ipt images
 
     if (warp == 0) {
         // ------------------------------------------------------------------ TMA producer
@@ -167,9 +168,9 @@ __global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const 
             long long it = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
-                const int img = t / per_image, rem = t - img * per_image;
+                const int ig = t / per_group, rem = t - ig * per_group;
                 const int rt = rem / p.groups, g = rem - rt * p.groups;
-                const int x = p.x0 + g * p.gstep, oy0 = rt * kBM;
+                const int x = p.x0 + g * p.gstep, oy0 = rt * p.R, img = ig * p.ipt;
                 for (int ky = 0; ky < p.kh; ky++, it++) {
                     const int s = (int)(it % S);
                     if (!mbar_wait(smem_u32(empty + s), (uint32_t)(((it / S) & 1) ^ 1), abort, 201)) {
@@ -249,20 +250,24 @@ __global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const 
         const int ox_lo = (p.pl + p.s - 1) / p.s, ox_hi = (p.iw - p.kw + p.pl) / p.s;
         int lt = 0;
         for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, lt++) {
-            const int img = t / per_image, rem = t - img * per_image;
+            const int ig = t / per_group, rem = t - ig * per_group;
             const int rt = rem / p.groups, g = rem - rt * p.groups;
-            const int oy0 = rt * kBM, ox0 = g * p.G;
+            const int oy0 = rt * p.R, ox0 = g * p.G;
             const int acc = lt & 1;
             if (!mbar_wait(smem_u32(tfull + acc), (uint32_t)((lt >> 1) & 1), abort, 204)) break;
             tc_fence_after();
-            const int r0 = oy0 + quarter * 32;  // first output row of this warp
+            // TMEM lane m = (image ig * ipt + m / R, row oy0 + m % R). A lane quarter covers rows
+            // r0.. of one image when R >= 32, else 32 / R whole images (rows oy0 .. oy0 + R - 1).
+            const int m0 = quarter * 32;
+            const int r0 = oy0 + (p.R >= 32 ? m0 % p.R : 0);  // first output row of this warp
+            const int img = ig * p.ipt + m0 / p.R;            // first image of this warp
             const bool live = r0 < p.oh;
             uint8_t *stage = wstage0 + (size_t)(lt & 1) * wsb;
             // this buffer's previous store (two tiles back) must have been read out
             if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
             __syncwarp();
             if (live) {
-                const int oy = r0 + lane;
+                const int oy = p.R >= 32 ? r0 + lane : oy0 + lane % p.R;
                 // kernel rows of this output row that fall outside the image
                 int rmask = 0;
                 for (int ky = 0; ky < p.kh; ky++) {
@@ -463,7 +468,17 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
     p.G = G;
     p.bn = bn;
     p.groups = (g.ow + G - 1) / G;
-    p.row_tiles = (g.oh + kBM - 1) / kBM;
+    // rows per image in an M tile: the power of two R in [8, 128] that leaves the fewest computed
+    // rows past the image (ties: larger R); the tile then holds R rows of 128 / R images
+    {
+        int best = kBM;
+        auto waste = [&](int r) { return (double)(((g.oh + r - 1) / r) * r - g.oh) / ((g.oh + r - 1) / r * r); };
+        for (int r = kBM / 2; r >= 8; r /= 2)
+            if (waste(r) < waste(best) - 1e-9) best = r;
+        p.R = best;
+        p.ipt = kBM / best;
+    }
+    p.row_tiles = (g.oh + p.R - 1) / p.R;
     p.ksteps = ksteps;
     p.x0 = -g.pl * g.ic - o;  // = (s*0 - pl)*ic rounded down to 16 bytes
     p.gstep = s * g.ic * G;
@@ -491,8 +506,9 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
 int conv_rows_launch(const ConvRows &c, const int8_t *x, int8_t *y, const ConvGeom &g, cudaStream_t s) {
     RowsParams p = c.p;
     p.n = g.n;
-    p.tiles = g.n * p.row_tiles * p.groups;
-    if ((long long)g.n * p.row_tiles * p.groups >= (1ll << 31)) return 2001;
+    const long long igroups = (g.n + p.ipt - 1) / p.ipt;
+    if (igroups * p.row_tiles * p.groups >= (1ll << 31)) return 2001;
+    p.tiles = (int)(igroups * p.row_tiles * p.groups);
     EncodeTiled enc = encoder();
     if (!enc) return 2001;
     const cuuint64_t row_bytes = (cuuint64_t)g.iw * g.ic, img_bytes = row_bytes * (cuuint64_t)g.ih;
@@ -500,7 +516,7 @@ int conv_rows_launch(const ConvRows &c, const int8_t *x, int8_t *y, const ConvGe
         // view v: input rows v, v + s, ... of every image
         const cuuint64_t dims[3] = {row_bytes, (cuuint64_t)((g.ih - v + p.s - 1) / p.s), (cuuint64_t)g.n};
         const cuuint64_t strides[2] = {row_bytes * (cuuint64_t)p.s, img_bytes};
-        const cuuint32_t box[3] = {(cuuint32_t)kBK, (cuuint32_t)kBM, 1};
+        const cuuint32_t box[3] = {(cuuint32_t)kBK, (cuuint32_t)p.R, (cuuint32_t)p.ipt};
         const cuuint32_t estr[3] = {1, 1, 1};
         if (enc(&p.xmap[v], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t *>(x) + (size_t)v * row_bytes, dims, strides,
                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
@@ -510,7 +526,8 @@ int conv_rows_launch(const ConvRows &c, const int8_t *x, int8_t *y, const ConvGe
     {
         const cuuint64_t dims[3] = {(cuuint64_t)g.ow * g.oc, (cuuint64_t)g.oh, (cuuint64_t)g.n};
         const cuuint64_t strides[2] = {(cuuint64_t)g.ow * g.oc, (cuuint64_t)g.oh * g.ow * g.oc};
-        const cuuint32_t box[3] = {(cuuint32_t)p.box, 32, 1};
+        // one lane quarter: 32 rows of one image, or R rows of 32 / R images
+        const cuuint32_t box[3] = {(cuuint32_t)p.box, (cuuint32_t)std::min(p.R, 32), (cuuint32_t)std::max(1, 32 / p.R)};
         const cuuint32_t estr[3] = {1, 1, 1};
         const CUtensorMapSwizzle sw = p.swz == 3   ? CU_TENSOR_MAP_SWIZZLE_128B
                                       : p.swz == 2 ? CU_TENSOR_MAP_SWIZZLE_64B
