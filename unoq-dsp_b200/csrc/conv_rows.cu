@@ -1,19 +1,22 @@
 // conv_rows.cu -- convolutions over few input channels (the RGB stems) as row GEMMs on the
 // 5th-generation tensor cores (tcgen05 kind::i8).
 //
-// Plan code 14 (runtime/qnn.c:1101-1227) for kh x kw kernels (kh, kw <= 3) over ic <= 16 channels
-// with stride s in both directions (the RGB stems, and the 8 / 16-channel layers of YOLO26n). For G adjacent output columns ox0..ox0+G-1 of output row oy,
+// Plan code 14 (runtime/qnn.c:1101-1227) for kh x kw kernels (kh, kw <= 3) over ic <= 32 channels
+// with stride s in both directions (the RGB stems, the 8 / 16-channel layers of YOLO26n, and
+// 24 / 32-channel 3x3 layers). For G adjacent output columns ox0..ox0+G-1 of output row oy,
 // every tap of kernel row ky reads input row iy = s*oy - pt + ky, and all their bytes lie in one
 // window of that row: bytes [X, X + s*ic*(G-1) + kw*ic) with X = (s*ox0 - pl)*ic. Hence
 //
-//     Y[oy][ox0 + j][oc] = sum_ky sum_b  In[iy][A + b] * W_ky[j*OC + oc][b]      (0 <= b < 128)
+//     Y[oy][ox0 + j][oc] = sum_ky sum_b  In[iy][A + b] * W_ky[j*OC + oc][b]      (0 <= b < span)
 //
 // with A = X rounded down to 16 bytes and W_ky[j*OC + oc][b] = w[oc][ky][kx][c] where
 // b = (X - A) + s*ic*j + kx*ic + c (zero elsewhere). That is a GEMM with M = output rows of one
-// image (128 per tile), N = G*OC (G output pixels x OC channels, <= 256) and K = 128 window bytes
-// per kernel row. The A operand of each (tile, ky) is a plain box of the input tensor, loaded by
-// TMA straight into the UMMA SWIZZLE_128B layout from a 3-D tensor map {row bytes, every s-th row,
-// images} whose out-of-range rows and columns read as zero: no im2col assembly at all. The banded
+// image (128 per tile), N = G*OC (G output pixels x OC channels, <= 256) and K = one or two
+// 128-byte blocks ("atoms") of window per kernel row: two when a 17-32-channel input leaves no
+// tile width whose window fits one. The A operand of each (tile, ky, atom) is a plain box of the
+// input tensor, loaded by TMA straight into the UMMA SWIZZLE_128B layout from a 3-D tensor map
+// {row bytes, every s-th row, images} whose out-of-range rows and columns read as zero: no im2col
+// assembly at all. The banded
 // B matrix is built once at load time and stays resident in shared memory.
 //
 // Zero fill stands where the reference reads the input zero point (qnn.c:1166-1168): an output
@@ -54,7 +57,8 @@ struct RowsParams {
     int G, bn;             // output pixels per column group; bn = G * oc
     int groups, row_tiles, tiles;
     int R, ipt;            // M tile = R output rows of each of ipt = 128 / R consecutive images
-    int ksteps;            // 32-byte K steps of a kernel row's window
+    int span;              // bytes of a kernel row's window (from its 16-byte-aligned start)
+    int atoms;             // 128-byte K blocks per kernel row (1 or 2): stages per tile = kh * atoms
     int x0;                // window start (bytes, 16-aligned, may be negative) of group 0; group g adds g * gstep
     int gstep;
     int view[3], dy[3];    // per kernel row: input view and row offset (view row = oy + dy)
@@ -63,12 +67,12 @@ struct RowsParams {
 
 struct RowsLayout {
     size_t a, b, out, epi, lut, bars, total;
-    __host__ __device__ RowsLayout(int stages, int kh, int bn, int oc, int out_bytes) {
+    __host__ __device__ RowsLayout(int stages, int kblocks, int bn, int oc, int out_bytes) {
         size_t o = 0;
         a = o;
         o += (size_t)stages * kStageBytes;
         b = o;
-        o += (size_t)kh * bn * kBK;
+        o += (size_t)kblocks * bn * kBK;
         out = o;
         o += (size_t)out_bytes;
         epi = (o + 31) & ~(size_t)31;
@@ -104,7 +108,7 @@ __global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int S = p.stages;
-    const RowsLayout L(S, p.kh, p.bn, p.oc, p.out_bytes);
+    const RowsLayout L(S, p.kh * p.atoms, p.bn, p.oc, p.out_bytes);
     uint8_t *sA = smem + L.a;
     uint8_t *sB = smem + L.b;
     uint8_t *sOut = smem + L.out;
@@ -146,7 +150,7 @@ __global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const 
         for (int i = threadIdx.x; i < 256; i += blockDim.x) sLut[i] = p.post[i];
     {
         // the banded weights, resident for the whole kernel (read by the tensor core: async proxy)
-        const size_t bbytes = (size_t)p.kh * p.bn * kBK;
+        const size_t bbytes = (size_t)p.kh * p.atoms * p.bn * kBK;
         const uint4 *src = reinterpret_cast<const uint4 *>(p.w);
         for (size_t i = threadIdx.x; i < bbytes / 16; i += blockDim.x) st_shared16(smem_u32(sB) + (uint32_t)(i * 16), __ldg(src + i));
         fence_proxy_async();
@@ -171,15 +175,16 @@ __global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const 
                 const int ig = t / per_group, rem = t - ig * per_group;
                 const int rt = rem / p.groups, g = rem - rt * p.groups;
                 const int x = p.x0 + g * p.gstep, oy0 = rt * p.R, img = ig * p.ipt;
-                for (int ky = 0; ky < p.kh; ky++, it++) {
+                for (int kb = 0; kb < p.kh * p.atoms; kb++, it++) {  // K block kb: kernel row ky, atom a
+                    const int ky = kb / p.atoms, a = kb - ky * p.atoms;
                     const int s = (int)(it % S);
                     if (!mbar_wait(smem_u32(empty + s), (uint32_t)(((it / S) & 1) ^ 1), abort, 201)) {
                         ok = false;
                         break;
                     }
                     mbar_expect_tx(smem_u32(full + s), (uint32_t)kStageBytes);
-                    tma_load_3d(smem_u32(sA + (size_t)s * kStageBytes), &p.xmap[p.view[ky]], x, oy0 + p.dy[ky], img,
-                                smem_u32(full + s));
+                    tma_load_3d(smem_u32(sA + (size_t)s * kStageBytes), &p.xmap[p.view[ky]], x + a * kBK,
+                                oy0 + p.dy[ky], img, smem_u32(full + s));
                 }
             }
             // every load issued has landed before the CTA may exit (bounded)
@@ -204,17 +209,19 @@ __global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const 
                 if (!mbar_wait(smem_u32(tempty + acc), (uint32_t)(((lt >> 1) & 1) ^ 1), abort, 202)) break;
                 tc_fence_after();
                 const uint32_t tmem_d = tmem_base + (uint32_t)(acc * p.bn);
-                for (int ky = 0; ky < p.kh; ky++, it++) {
+                for (int kb = 0; kb < p.kh * p.atoms; kb++, it++) {
+                    const int a = kb % p.atoms;
                     const int s = (int)(it % S);
                     if (!mbar_wait(smem_u32(full + s), (uint32_t)((it / S) & 1), abort, 203)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    for (int kk = 0; kk < p.ksteps; kk++) {
+                    const int ksteps = min(kBK, p.span - a * kBK + 31) / 32;  // 32-byte K steps of this atom
+                    for (int kk = 0; kk < ksteps; kk++) {
                         const uint64_t ad = smem_desc(a0 + (uint32_t)(s * kStageBytes + kk * 32));
-                        const uint64_t bd = smem_desc(b0 + (uint32_t)(ky * p.bn * kBK + kk * 32));
-                        mma_i8(tmem_d, ad, bd, idesc, (ky | kk) ? 1u : 0u);
+                        const uint64_t bd = smem_desc(b0 + (uint32_t)(kb * p.bn * kBK + kk * 32));
+                        mma_i8(tmem_d, ad, bd, idesc, (kb | kk) ? 1u : 0u);
                     }
                     mma_commit(smem_u32(empty + s));
                 }
@@ -354,8 +361,8 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
     const char *env = std::getenv("UNOQ_CONV_ROWS");
     if (env && env[0] == '0') return 0;
     const int s = g.sh;
-    const char *env_ic = std::getenv("UNOQ_CONV_ROWS_IC");  // widest input taken (default 16)
-    const int max_ic = env_ic ? std::atoi(env_ic) : 16;
+    const char *env_ic = std::getenv("UNOQ_CONV_ROWS_IC");  // widest input taken (default 32)
+    const int max_ic = env_ic ? std::atoi(env_ic) : 32;
     if (g.ic < 1 || g.ic > max_ic || g.kh < 1 || g.kh > 3 || g.kw < 1 || g.kw > 3 || g.dh != 1 || g.dw != 1) return 0;
     if (g.sw != s || (s != 1 && s != 2)) return 0;
     if (g.oc % 16 != 0 || g.oc > 256) return 0;
@@ -365,39 +372,43 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
     if ((long long)g.ih * row_bytes >= (1ll << 31) || (long long)g.oh * g.ow * g.oc >= (1ll << 31)) return 0;
     // window offset of every group (constant because a group advances by whole 16-byte units)
     const int o = (((-g.pl * g.ic) % 16) + 16) % 16;
-    int G = 0;
-    for (int c = 256 / g.oc; c >= 1; c /= 2) {
-        if ((s * g.ic * c) % 16 != 0) continue;
-        if (o + s * g.ic * (c - 1) + g.kw * g.ic > kBK) continue;
-        G = c;
-        break;
-    }
+    // G output pixels per column group: the most (a power of two) whose window fits one 128-byte
+    // K block per kernel row, else two (inputs of 17-32 channels), with bn = G * oc split into
+    // 16 / 32 / 64 columns per epilogue warp
+    const int ew = kRowsEW;
+    int G = 0, atoms = 0;
+    for (int na = 1; na <= 2 && !G; na++)
+        for (int c = 256 / g.oc; c >= 1; c /= 2) {
+            const int b = c * g.oc / (ew / 4);
+            if ((s * g.ic * c) % 16 != 0 || (b != 16 && b != 32 && b != 64)) continue;
+            if (o + s * g.ic * (c - 1) + g.kw * g.ic > na * kBK) continue;
+            G = c, atoms = na;
+            break;
+        }
     if (!G) return 0;
     const int bn = G * g.oc;
-    const int ew = kRowsEW;
-    const int box = bn / (ew / 4);  // columns per epilogue warp: 16, 32 or 64
-    if (box != 16 && box != 32 && box != 64) return 0;
+    const int box = bn / (ew / 4);
     const int span = o + s * g.ic * (G - 1) + g.kw * g.ic;
-    const int ksteps = (span + 31) / 32;
     const int out_bytes = (int)(2 * ew * rows_warp_stage(box));
     int stages = 4;
-    while (stages > 2 && RowsLayout(stages, g.kh, bn, g.oc, out_bytes).total > (size_t)kRowsMaxSmem) stages--;
-    const RowsLayout L(stages, g.kh, bn, g.oc, out_bytes);
+    while (stages > 2 && RowsLayout(stages, g.kh * atoms, bn, g.oc, out_bytes).total > (size_t)kRowsMaxSmem) stages--;
+    const RowsLayout L(stages, g.kh * atoms, bn, g.oc, out_bytes);
     if (L.total > (size_t)kRowsMaxSmem) return 0;
 
     // Weights: reference packed layout (gemm.h:9), reduction index t = (ky*kw + kx)*ic + c
-    // (tflite.py:155), into the banded B matrix, one SW128 K-major stage per kernel row.
+    // (tflite.py:155), into the banded B matrix, one SW128 K-major block per (kernel row, atom).
     const int kp = q[18], oc = g.oc, K = g.kh * g.kw * g.ic;
     auto wref = [&](int j, int t) -> int { return w_packed[(j / 4) * kp * 4 + (t / 8) * 32 + (j % 4) * 8 + t % 8]; };
-    std::vector<uint8_t> wt((size_t)g.kh * bn * kBK, 0);
+    std::vector<uint8_t> wt((size_t)g.kh * atoms * bn * kBK, 0);
     for (int ky = 0; ky < g.kh; ky++)
         for (int n = 0; n < bn; n++) {
             const int j = n / oc, ch = n % oc;
             for (int kx = 0; kx < g.kw; kx++)
                 for (int c = 0; c < g.ic; c++) {
-                    const int b = o + s * g.ic * j + kx * g.ic + c;
-                    const int chunk = b / 16;
-                    const size_t off = ((size_t)ky * bn + (n / 8) * 8) * kBK + (n % 8) * kBK + ((chunk ^ (n % 8)) * 16) + b % 16;
+                    const int bw = o + s * g.ic * j + kx * g.ic + c;  // byte of the window
+                    const int a = bw / kBK, b = bw % kBK, chunk = b / 16;
+                    const size_t off = ((size_t)(ky * atoms + a) * bn + (n / 8) * 8) * kBK + (n % 8) * kBK +
+                                       ((chunk ^ (n % 8)) * 16) + b % 16;
                     wt[off] = (uint8_t)(int8_t)wref(ch, (ky * g.kw + kx) * g.ic + c);
                 }
         }
@@ -479,7 +490,8 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
         p.ipt = kBM / best;
     }
     p.row_tiles = (g.oh + p.R - 1) / p.R;
-    p.ksteps = ksteps;
+    p.span = span;
+    p.atoms = atoms;
     p.x0 = -g.pl * g.ic - o;  // = (s*0 - pl)*ic rounded down to 16 bytes
     p.gstep = s * g.ic * G;
     for (int ky = 0; ky < g.kh; ky++) {

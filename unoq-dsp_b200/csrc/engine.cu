@@ -180,8 +180,14 @@ int Engine::prepare() {
                 Requant r{dq + kHead, dq + kHead + g.oc, dq + kHead + 2 * g.oc,
                           o.p[1] ? dconst(o.p[1] - 1) : nullptr, q[13], q[14], q[15]};
                 const uint32_t ta = o.a, tz = o.out;
+                // a following residual add that the conv_tc epilogue can take (see below)
+                const bool add_next = i + 1 < P.h.no && P.ops[i + 1].code == 18 && o.out != P.h.output &&
+                                      death_[o.out] == (int)i + 1 && fuse_adds_;
                 ConvRows *cr = nullptr;
-                int rc = conv_rows_prepare(P.s8(o.b), q, r.post, g, [this](size_t n) { return prep_alloc(n); }, &cr);
+                int rc = 0;
+                // the row GEMM has no fused add: 17-32-channel inputs keep theirs in conv_tc
+                if (!(add_next && g.ic > 16))
+                    rc = conv_rows_prepare(P.s8(o.b), q, r.post, g, [this](size_t n) { return prep_alloc(n); }, &cr);
                 if (rc) return rc;
                 if (cr) {
                     std::shared_ptr<ConvRows> keep(cr, conv_rows_free);
@@ -209,8 +215,7 @@ int Engine::prepare() {
                 // Residual add fused into the epilogue when the next op is an add whose one input is
                 // this conv's output and nothing else reads that output.
                 ConvTc *tc = nullptr;
-                if (i + 1 < P.h.no && P.ops[i + 1].code == 18 && o.out != P.h.output && death_[o.out] == (int)i + 1 &&
-                    fuse_adds_) {
+                if (add_next) {
                     const Op &n = P.ops[i + 1];
                     const bool is_a = n.a == o.out, is_b = n.b == o.out;
                     const uint32_t res = is_a ? n.b : n.a;
