@@ -309,7 +309,10 @@ def all_cases(scale=1):
         ("conv_rows_rgb_s1", lambda r: conv_case(r, (1, 6 * s, 16, 3), 16, (3, 3), (1, 1), xq=(0.02, 4))),
         ("conv_rows_ic4_post", lambda r: conv_post_case(r, (1, 7 * s, 20, 4), 16, (3, 3), (2, 2))),
         ("conv_rows_ic1", lambda r: conv_case(r, (1, 5 * s, 48, 1), 32, (3, 3), (2, 2), act="relu6")),
-        # 24 / 32-channel 3x3 inputs (band producer)
+        # 64-channel 3x3 inputs (row GEMM with three window blocks per kernel row)
+        ("conv_rows_ic64_s1", lambda r: conv_case(r, (1, 7 * s, 12, 64), 16, (3, 3), (1, 1))),
+        ("conv_rows_ic64_s2", lambda r: conv_case(r, (1, 9 * s, 14, 64), 64, (3, 3), (2, 2), xq=(0.03, -9))),
+        # 24 / 32-channel 3x3 inputs
         ("conv_rows2_ic32_s2", lambda r: conv_case(r, (1, 9 * s, 22, 32), 32, (3, 3), (2, 2), xq=(0.03, 11))),
         ("conv_rows2_ic32_s1", lambda r: conv_case(r, (1, 6 * s, 13, 32), 16, (3, 3), (1, 1))),
         ("conv_rows2_ic24_post", lambda r: conv_post_case(r, (1, 5 * s, 11, 24), 32, (3, 3), (1, 1))),

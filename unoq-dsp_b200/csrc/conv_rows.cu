@@ -58,7 +58,7 @@ struct RowsParams {
     int groups, row_tiles, tiles;
     int R, ipt;            // M tile = R output rows of each of ipt = 128 / R consecutive images
     int span;              // bytes of a kernel row's window (from its 16-byte-aligned start)
-    int atoms;             // 128-byte K blocks per kernel row (1 or 2): stages per tile = kh * atoms
+    int atoms;             // 128-byte K blocks per kernel row (1-4): stages per tile = kh * atoms
     int x0;                // window start (bytes, 16-aligned, may be negative) of group 0; group g adds g * gstep
     int gstep;
     int view[3], dy[3];    // per kernel row: input view and row offset (view row = oy + dy)
@@ -361,8 +361,8 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
     const char *env = std::getenv("UNOQ_CONV_ROWS");
     if (env && env[0] == '0') return 0;
     const int s = g.sh;
-    const char *env_ic = std::getenv("UNOQ_CONV_ROWS_IC");  // widest input taken (default 32)
-    const int max_ic = env_ic ? std::atoi(env_ic) : 32;
+    const char *env_ic = std::getenv("UNOQ_CONV_ROWS_IC");  // widest input taken (default 64)
+    const int max_ic = env_ic ? std::atoi(env_ic) : 64;
     if (g.ic < 1 || g.ic > max_ic || g.kh < 1 || g.kh > 3 || g.kw < 1 || g.kw > 3 || g.dh != 1 || g.dw != 1) return 0;
     if (g.sw != s || (s != 1 && s != 2)) return 0;
     if (g.oc % 16 != 0 || g.oc > 256) return 0;
@@ -372,16 +372,21 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
     if ((long long)g.ih * row_bytes >= (1ll << 31) || (long long)g.oh * g.ow * g.oc >= (1ll << 31)) return 0;
     // window offset of every group (constant because a group advances by whole 16-byte units)
     const int o = (((-g.pl * g.ic) % 16) + 16) % 16;
-    // G output pixels per column group: the most (a power of two) whose window fits one 128-byte
-    // K block per kernel row, else two (inputs of 17-32 channels), with bn = G * oc split into
-    // 16 / 32 / 64 columns per epilogue warp
+    // G output pixels per column group: the most (a power of two) whose window fits the fewest
+    // 128-byte K blocks per kernel row (one for few channels, up to four for 64), with bn = G * oc
+    // split into 16 / 32 / 64 columns per epilogue warp and the banded weights resident. Inputs of
+    // 33-64 channels only with oc <= 32, where band-mode tiles are narrowest (64 -> 16 channels:
+    // 2.2x faster than band mode; 64 -> 64 stride 2: 9% slower)
     const int ew = kRowsEW;
+    const int max_atoms = g.ic <= 32 ? 2 : (g.oc <= 32 ? 4 : 0);
     int G = 0, atoms = 0;
-    for (int na = 1; na <= 2 && !G; na++)
+    for (int na = 1; na <= max_atoms && !G; na++)
         for (int c = 256 / g.oc; c >= 1; c /= 2) {
             const int b = c * g.oc / (ew / 4);
             if ((s * g.ic * c) % 16 != 0 || (b != 16 && b != 32 && b != 64)) continue;
             if (o + s * g.ic * (c - 1) + g.kw * g.ic > na * kBK) continue;
+            const int ob = (int)(2 * ew * rows_warp_stage(b));
+            if (RowsLayout(2, g.kh * na, c * g.oc, g.oc, ob).total > (size_t)kRowsMaxSmem) continue;
             G = c, atoms = na;
             break;
         }
