@@ -2,22 +2,23 @@
 // 5th-generation tensor cores (tcgen05 kind::i8).
 //
 // Plan code 14 (runtime/qnn.c:1101-1227) for kh x kw kernels (kh, kw <= 3) over ic <= 32 channels
-// with stride s in both directions (the RGB stems, the 8 / 16-channel layers of YOLO26n, and
-// 24 / 32-channel 3x3 layers). For G adjacent output columns ox0..ox0+G-1 of output row oy,
-// every tap of kernel row ky reads input row iy = s*oy - pt + ky, and all their bytes lie in one
-// window of that row: bytes [X, X + s*ic*(G-1) + kw*ic) with X = (s*ox0 - pl)*ic. Hence
+// (or <= 64 with at most 32 outputs) with stride s in both directions: the RGB stems, the 8 /
+// 16-channel layers of YOLO26n, 24 / 32-channel 3x3 layers and YOLO26n's 64 -> 16 head conv. For
+// G adjacent output columns ox0..ox0+G-1 of output row oy, every tap of kernel row ky reads input
+// row iy = s*oy - pt + ky, and all their bytes lie in one window of that row: bytes
+// [X, X + s*ic*(G-1) + kw*ic) with X = (s*ox0 - pl)*ic. Hence
 //
 //     Y[oy][ox0 + j][oc] = sum_ky sum_b  In[iy][A + b] * W_ky[j*OC + oc][b]      (0 <= b < span)
 //
 // with A = X rounded down to 16 bytes and W_ky[j*OC + oc][b] = w[oc][ky][kx][c] where
-// b = (X - A) + s*ic*j + kx*ic + c (zero elsewhere). That is a GEMM with M = output rows of one
-// image (128 per tile), N = G*OC (G output pixels x OC channels, <= 256) and K = one or two
-// 128-byte blocks ("atoms") of window per kernel row: two when a 17-32-channel input leaves no
-// tile width whose window fits one. The A operand of each (tile, ky, atom) is a plain box of the
-// input tensor, loaded by TMA straight into the UMMA SWIZZLE_128B layout from a 3-D tensor map
-// {row bytes, every s-th row, images} whose out-of-range rows and columns read as zero: no im2col
-// assembly at all. The banded
-// B matrix is built once at load time and stays resident in shared memory.
+// b = (X - A) + s*ic*j + kx*ic + c (zero elsewhere). That is a GEMM with M = 128 output rows (R
+// rows from each of 128 / R consecutive images), N = G*OC (G output pixels x OC channels, <= 256)
+// and K = one to four 128-byte blocks ("atoms") of window per kernel row: more than one when a
+// 17-64-channel input leaves no tile width whose window fits one. The A operand of each (tile,
+// ky, atom) is a plain box {128 bytes, R rows, 128 / R images} of the input tensor, loaded by TMA
+// straight into the UMMA SWIZZLE_128B layout from a 3-D tensor map {row bytes, every s-th row,
+// images} whose out-of-range rows, columns and images read as zero: no im2col assembly at all.
+// The banded B matrix is built once at load time and stays resident in shared memory.
 //
 // Zero fill stands where the reference reads the input zero point (qnn.c:1166-1168): an output
 // whose taps leave the image gets xzp * (sum of those taps' weights) added to its accumulator,
@@ -26,8 +27,8 @@
 //
 // Roles: warp 0 issues the TMA loads, warp 1 the MMAs (M=128, N=G*OC, K=32 per instruction) into
 // two TMEM accumulators, warps 2.. requantise (tcgen05.ld, exact scale, clamp, post table) into
-// per-warp staging buffers and write them with 3-D TMA tensor stores, which clip the rows past
-// the image. Every wait is bounded (about 2 s); on expiry the kernel records a site code, waits
+// per-warp staging buffers and write them with 3-D TMA tensor stores, which clip the rows and
+// images past the tensor. Every wait is bounded (about 2 s); on expiry the kernel records a site code, waits
 // for its copies and MMAs, frees its TMEM and exits.
 #include <algorithm>
 #include <cstdlib>

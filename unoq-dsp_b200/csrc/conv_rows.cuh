@@ -12,7 +12,8 @@ namespace uq {
 
 struct ConvRows;  // prepared banded weights, epilogue constants and border corrections
 
-// Take the conv if it has ic <= 32 (UNOQ_CONV_ROWS_IC lowers the bound), a kh x kw <= 3 x 3 kernel
+// Take the conv if it has ic <= 32, or ic <= 64 with oc <= 32 (UNOQ_CONV_ROWS_IC lowers the input
+// bound), a kh x kw <= 3 x 3 kernel
 // with dilation 1, equal strides 1 or 2, oc a multiple of 16 (<= 256) and 16-byte input rows;
 // prepare its device data with `alloc`. *out = nullptr when another path should run. Returns 0
 // or 2001.
