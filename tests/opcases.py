@@ -312,6 +312,8 @@ def all_cases(scale=1):
         # 64-channel 3x3 inputs (row GEMM with three window blocks per kernel row)
         ("conv_rows_ic64_s1", lambda r: conv_case(r, (1, 7 * s, 12, 64), 16, (3, 3), (1, 1))),
         ("conv_rows_ic64_s2", lambda r: conv_case(r, (1, 9 * s, 14, 64), 64, (3, 3), (2, 2), xq=(0.03, -9))),
+        # 48-column epilogue parts (G = 2 pixels x 96 channels)
+        ("conv_rows_oc96_s2", lambda r: conv_case(r, (1, 9 * s, 16, 16), 96, (3, 3), (2, 2))),
         # 24 / 32-channel 3x3 inputs
         ("conv_rows2_ic32_s2", lambda r: conv_case(r, (1, 9 * s, 22, 32), 32, (3, 3), (2, 2), xq=(0.03, 11))),
         ("conv_rows2_ic32_s1", lambda r: conv_case(r, (1, 6 * s, 13, 32), 16, (3, 3), (1, 1))),

@@ -375,16 +375,17 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
     const int o = (((-g.pl * g.ic) % 16) + 16) % 16;
     // G output pixels per column group: the most (a power of two) whose window fits the fewest
     // 128-byte K blocks per kernel row (one for few channels, up to four for 64), with bn = G * oc
-    // split into 16 / 32 / 64 columns per epilogue warp and the banded weights resident. Inputs of
-    // 33-64 channels only with oc <= 32, where band-mode tiles are narrowest (64 -> 16 channels:
-    // 2.2x faster than band mode; 64 -> 64 stride 2: 9% slower)
+    // split into 16 / 32 / 48 / 64 columns per epilogue warp (48-byte staging rows are stored
+    // unswizzled: their 16-byte lanes still fall in distinct banks) and the banded weights
+    // resident. Inputs of 33-64 channels only with oc <= 32, where band-mode tiles are narrowest
+    // (64 -> 16 channels: 2.2x faster than band mode; 64 -> 64 stride 2: 9% slower)
     const int ew = kRowsEW;
     const int max_atoms = g.ic <= 32 ? 2 : (g.oc <= 32 ? 4 : 0);
     int G = 0, atoms = 0;
     for (int na = 1; na <= max_atoms && !G; na++)
         for (int c = 256 / g.oc; c >= 1; c /= 2) {
             const int b = c * g.oc / (ew / 4);
-            if ((s * g.ic * c) % 16 != 0 || (b != 16 && b != 32 && b != 64)) continue;
+            if ((s * g.ic * c) % 16 != 0 || (b != 16 && b != 32 && b != 48 && b != 64)) continue;
             if (o + s * g.ic * (c - 1) + g.kw * g.ic > na * kBK) continue;
             const int ob = (int)(2 * ew * rows_warp_stage(b));
             if (RowsLayout(2, g.kh * na, c * g.oc, g.oc, ob).total > (size_t)kRowsMaxSmem) continue;
@@ -469,6 +470,8 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
         if (!allow(conv_rows_kernel<kRelu, 1>) || !allow(conv_rows_kernel<kTies, 1>) ||
             !allow(conv_rows_kernel<kGeneral, 1>) || !allow(conv_rows_kernel<kRelu, 2>) ||
             !allow(conv_rows_kernel<kTies, 2>) || !allow(conv_rows_kernel<kGeneral, 2>) ||
+            !allow(conv_rows_kernel<kRelu, 3>) || !allow(conv_rows_kernel<kTies, 3>) ||
+            !allow(conv_rows_kernel<kGeneral, 3>) ||
             !allow(conv_rows_kernel<kRelu, 4>) || !allow(conv_rows_kernel<kTies, 4>) ||
             !allow(conv_rows_kernel<kGeneral, 4>))
             return 2001;
@@ -564,6 +567,7 @@ int conv_rows_launch(const ConvRows &c, const int8_t *x, int8_t *y, const ConvGe
         else conv_rows_kernel<kGeneral, CH><<<grid, T, c.smem, s>>>(p);
     };
     if (c.chunks == 4) go(std::integral_constant<int, 4>{});
+    else if (c.chunks == 3) go(std::integral_constant<int, 3>{});
     else if (c.chunks == 2) go(std::integral_constant<int, 2>{});
     else go(std::integral_constant<int, 1>{});
     return 0;
