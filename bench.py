@@ -396,13 +396,15 @@ def bench_model(lib, dist, name, global_batch, steps, warmup, peaks, want_roofli
         value = global_batch * steps / t_dev
         # e2e through the public batch API (pinned host buffers, copies inside the timed region)
         for _ in range(1):
-            lib.ug_infer_batch(handle, h_in, per_gpu, h_out)
+            rc = lib.ug_infer_batch(handle, h_in, per_gpu, h_out)
+            if rc:
+                raise RuntimeError(f"e2e warm-up rc={rc}: {lib.ug_last_error()}")
         dist.barrier()
         e2e_ms = 0.0
         for _ in range(steps):
             rc = lib.ug_infer_batch(handle, h_in, per_gpu, h_out)
             if rc:
-                raise RuntimeError(f"e2e rc={rc}")
+                raise RuntimeError(f"e2e rc={rc}: {lib.ug_last_error()}")
             e2e_ms += lib.ug_last_infer_ms(handle)
         dist.barrier()
         t_e2e = dist.max(e2e_ms / 1e3)

@@ -880,8 +880,9 @@ int Engine::run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint
     // run at close to whole-batch efficiency (a 512-image MobileNetV4 graph runs about 17% slower
     // per image than a 4096-image one: tail waves and launch gaps). The growth is the ratio of
     // compute to upload time per image measured on the previous call's last piece (1.25 at first;
-    // about 1.2 for MobileNetV4, 2.7 for YOLO26n). At most kMaxPieces; a small remainder joins the
-    // last piece. UNOQ_PIPE_GROWTH fixes the factor.
+    // about 1.2 for MobileNetV4, 2.7 for YOLO26n; with a multi-GPU output gather the factor stays
+    // at its initial value on every rank). At most kMaxPieces; a small remainder joins the last
+    // piece. UNOQ_PIPE_GROWTH fixes the factor.
     constexpr size_t kMaxPieces = 16;
     static const double fixed_growth = [] {
         const char *env = std::getenv("UNOQ_PIPE_GROWTH");
@@ -959,7 +960,10 @@ int Engine::run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint
     if ((rc = finish(ev1_))) return rc;
     UQ_CUDA(cudaEventElapsedTime(&last_ms_, ev0_, ev1_));
     last_images_ = images;
-    if (sizes.size() > 1) {
+    // Adapt the growth from this process's own timing only when no output gather runs: every rank
+    // must cut its batch into the same pieces, because each piece enqueues one gather step, and
+    // per-rank timings differ.
+    if (sizes.size() > 1 && !gathering) {
         float up = 0.f, comp = 0.f;
         if (cudaEventElapsedTime(&up, pipe_t_[0], pipe_t_[1]) == cudaSuccess &&
             cudaEventElapsedTime(&comp, pipe_t_[2], pipe_t_[3]) == cudaSuccess && up > 0.f && comp > 0.f)
