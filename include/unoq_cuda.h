@@ -46,7 +46,8 @@ UG_API int ug_run(const void *input, uint32_t input_bytes, void *output, uint32_
  * before any stream capture and before allocation is forbidden. A plan whose one-image
  * activations exceed 16 MiB gets 20 and stays loaded. Nothing in the array must start at zero.
  * Overlapping calls on one device would race on the shared array; the graph ABI's lock
- * serialises them within a process. */
+ * serialises them within a process. ug_snapshot after this call reads the static array. The
+ * ug_profile counters count ug_run calls only, not calls of this variant. */
 UG_API int ug_run_static(const void *input, uint32_t input_bytes, void *output, uint32_t output_bytes);
 /* Replace ug_input_bytes / ug_output_bytes (runtime/graph.c:263-264); 0 when nothing loaded. */
 UG_API uint32_t ug_input_bytes(void);

@@ -3,7 +3,7 @@
 Run where the reference checkout is mounted (it imports the reference's src/unoq_dsp in a
 separate interpreter so it does not clash with this repository's package):
 
-    python tests/golden/make_decode_golden.py
+    UNOQ_REFERENCE_DIR=<reference checkout> python tests/golden/make_decode_golden.py
 
 Writes decode.json: for seeded inputs, the reference's profile_lookup / image_lookup tables
 (as SHA-256 of the bytes), prepare_profile / prepare_image outputs (SHA-256), the one-to-one YOLO
@@ -11,12 +11,14 @@ decode of the bundled detector's metadata on seeded raw int8 heads, and SSD fixe
 of a seeded synthetic task. tests/test_vision.py regenerates the same inputs and compares.
 """
 import json
+import os
 import subprocess
 import sys
 from pathlib import Path
 
 OUT = Path(__file__).resolve().parent / "decode.json"
-REF_SRC = Path("/root/reference/src")
+# the reference checkout: UNOQ_REFERENCE_DIR, else a `reference` directory beside this repository
+REF_SRC = Path(os.environ.get("UNOQ_REFERENCE_DIR", Path(__file__).resolve().parents[3] / "reference")) / "src"
 
 WORKER = r'''
 import base64, hashlib, json, sys

@@ -3,7 +3,10 @@
 Run where the reference checkout is mounted (it builds oracle/_ref/libug_ref.so from the
 reference's own runtime/graph.c, qnn.c, gemm.c -- see oracle/Makefile):
 
-    make -C oracle ref && python tests/golden/make_golden.py
+    make -C oracle ref REF=<reference checkout> && python tests/golden/make_golden.py
+
+The bundled models are read from models/ (staged by __graft_entry__.build()), else from the
+checkout named by UNOQ_REFERENCE_DIR (default: a `reference` directory beside this repository).
 
 Writes:
 * ops.npz     -- every case of tests/opcases.py at scale 1: plan bytes, input, and the
@@ -19,6 +22,7 @@ The reference has no golden tensors of its own (its kernel tests compare against
 interpreter, which is absent here); these fixtures pin our oracle to the reference instead.
 """
 import hashlib
+import os
 import sys
 from pathlib import Path
 
@@ -39,7 +43,9 @@ MODEL_SEEDS = (0, 1)
 
 def model_dir():
     local = ROOT / "models"
-    return local if (local / "mobilenetv4-small.uqmodel").is_file() else Path("/root/reference/models")
+    if (local / "mobilenetv4-small.uqmodel").is_file():
+        return local
+    return Path(os.environ.get("UNOQ_REFERENCE_DIR", ROOT.parent / "reference")) / "models"
 
 
 def main():

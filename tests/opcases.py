@@ -312,6 +312,11 @@ def all_cases(scale=1):
         # 64-channel 3x3 inputs (row GEMM with three window blocks per kernel row)
         ("conv_rows_ic64_s1", lambda r: conv_case(r, (1, 7 * s, 12, 64), 16, (3, 3), (1, 1))),
         ("conv_rows_ic64_s2", lambda r: conv_case(r, (1, 9 * s, 14, 64), 64, (3, 3), (2, 2), xq=(0.03, -9))),
+        # 33-64-channel inputs with at most 32 outputs at stride 2 (three or four window blocks per
+        # kernel row), and 48 channels (three blocks) at strides 1 and 2
+        ("conv_rows_ic64_s2_oc32", lambda r: conv_case(r, (1, 9 * s, 14, 64), 32, (3, 3), (2, 2), xq=(0.03, -9))),
+        ("conv_rows_ic48_s2_oc16", lambda r: conv_case(r, (1, 9 * s, 15, 48), 16, (3, 3), (2, 2), xq=(0.02, 6))),
+        ("conv_rows_ic48_s1_oc32", lambda r: conv_case(r, (1, 7 * s, 12, 48), 32, (3, 3), (1, 1))),
         # 48-column epilogue parts (G = 2 pixels x 96 channels)
         ("conv_rows_oc96_s2", lambda r: conv_case(r, (1, 9 * s, 16, 16), 96, (3, 3), (2, 2))),
         # 24 / 32-channel 3x3 inputs

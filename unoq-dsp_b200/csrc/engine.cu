@@ -73,7 +73,9 @@ void Engine::release() {
         if (e) cudaEventDestroy(e);
         e = nullptr;
     }
-    pipe_growth_ = 1.25;
+    pipe_growth_ = kInitialPieceGrowth;
+    last_ctx_ = nullptr;
+    last_images_ = 0;
     for (auto &row : pipe_ev_)
         for (auto &e : row) {
             if (e) cudaEventDestroy(e);
@@ -870,6 +872,7 @@ int Engine::run_batch_host(const void *in, void *out, uint32_t images, uint32_t 
     if ((rc = finish(ev1_))) return rc;
     UQ_CUDA(cudaEventElapsedTime(&last_ms_, ev0_, ev1_));
     last_images_ = images;
+    last_ctx_ = B;
     return device_status();
 }
 
@@ -880,28 +883,16 @@ int Engine::run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint
     // run at close to whole-batch efficiency (a 512-image MobileNetV4 graph runs about 17% slower
     // per image than a 4096-image one: tail waves and launch gaps). The growth is the ratio of
     // compute to upload time per image measured on the previous call's last piece (1.25 at first;
-    // about 1.2 for MobileNetV4, 2.7 for YOLO26n; with a multi-GPU output gather the factor stays
-    // at its initial value on every rank). At most kMaxPieces; a small remainder joins the last
-    // piece. UNOQ_PIPE_GROWTH fixes the factor.
-    constexpr size_t kMaxPieces = 16;
+    // about 1.2 for MobileNetV4, 2.7 for YOLO26n; once the session has joined a multi-GPU output
+    // gather the factor stays at its initial value on every rank, see pipeline_growth). At most
+    // kMaxPieces; a small remainder joins the last piece. UNOQ_PIPE_GROWTH fixes the factor.
     static const double fixed_growth = [] {
         const char *env = std::getenv("UNOQ_PIPE_GROWTH");
         const double g = env ? std::atof(env) : 0.0;
         return g >= 1.0 && g <= 4.0 ? g : 0.0;
     }();
-    const double growth = fixed_growth > 0 ? fixed_growth : pipe_growth_;
-    std::vector<uint32_t> sizes;
-    {
-        uint32_t left = images;
-        double cur = std::min(256.0, std::max(64.0, images / 16.0));
-        while (left) {
-            uint32_t n = std::min<uint32_t>(left, (uint32_t)cur);
-            if (left - n < (uint32_t)(cur * 0.5) || sizes.size() + 1 == kMaxPieces) n = left;
-            sizes.push_back(n);
-            left -= n;
-            cur *= growth;
-        }
-    }
+    const bool joined = gather_ && gather_->active();
+    const std::vector<uint32_t> sizes = pipeline_pieces(images, pipeline_growth(joined, pipe_growth_, fixed_growth));
     const size_t ni = input_bytes(), no = k ? sizeof(UgDetectionRecord) * k : output_bytes();
     // one batch context per piece (slot p + 1): no arena is refilled within a call
     std::vector<BatchCtx *> ctx(sizes.size(), nullptr);
@@ -912,7 +903,7 @@ int Engine::run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint
     }
     if (rc) return rc;
     UQ_CUDA(cudaSetDevice(device_));
-    const bool gathering = !k && gather_ && gather_->active();
+    const bool gathering = !k && joined;
     uint8_t *root = gathering ? gather_->root_buffer(no * images) : nullptr;
     if (gathering && gather_->rank() == 0 && !root) return 1002;
     // every stream starts after the work already queued on the compute stream
@@ -960,10 +951,10 @@ int Engine::run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint
     if ((rc = finish(ev1_))) return rc;
     UQ_CUDA(cudaEventElapsedTime(&last_ms_, ev0_, ev1_));
     last_images_ = images;
-    // Adapt the growth from this process's own timing only when no output gather runs: every rank
-    // must cut its batch into the same pieces, because each piece enqueues one gather step, and
-    // per-rank timings differ.
-    if (sizes.size() > 1 && !gathering) {
+    last_ctx_ = ctx.back();
+    // Learn the growth from this process's own timing only while the session has no output gather
+    // (pipeline_growth ignores it afterwards anyway): per-rank timings differ.
+    if (sizes.size() > 1 && !joined) {
         float up = 0.f, comp = 0.f;
         if (cudaEventElapsedTime(&up, pipe_t_[0], pipe_t_[1]) == cudaSuccess &&
             cudaEventElapsedTime(&comp, pipe_t_[2], pipe_t_[3]) == cudaSuccess && up > 0.f && comp > 0.f)
@@ -1011,6 +1002,8 @@ int Engine::run_static(const void *in, void *out) {
         set_error(std::string("inference: ") + cudaGetErrorString(e));
         return 2001;
     }
+    last_ctx_ = &static_;
+    last_images_ = 1;
     return device_status();
 }
 
@@ -1046,6 +1039,7 @@ int Engine::launch(uint32_t images) {
     if ((rc = stage_in(*B, stream_))) return rc;
     UQ_CUDA(cudaGraphLaunch(B->exec, stream_));
     last_images_ = images;
+    last_ctx_ = B;
     return gather(*B);
 }
 
@@ -1095,6 +1089,7 @@ int Engine::time_launches(uint32_t images, uint32_t iterations, float *ms) {
     if ((rc = finish(ev1_))) return rc;
     UQ_CUDA(cudaEventElapsedTime(ms, ev0_, ev1_));
     last_images_ = images;
+    last_ctx_ = B;
     return device_status();
 }
 
@@ -1204,6 +1199,7 @@ int Engine::launch_detect(uint32_t images, uint32_t k) {
     if ((rc = stage_in(*B, stream_))) return rc;
     UQ_CUDA(cudaGraphLaunch(B->exec, stream_));
     last_images_ = images;
+    last_ctx_ = B;
     return stage_out(*B, k, stream_);
 }
 
@@ -1244,6 +1240,7 @@ int Engine::dist_init(int rank, int world, const void *id, uint32_t bytes) {
     const int rc = g->init(device_, rank, world, id, bytes);
     if (rc) return rc;
     gather_ = std::move(g);
+    pipe_growth_ = kInitialPieceGrowth;  // nothing learned alone carries over into gathered calls
     return 0;
 }
 
@@ -1265,11 +1262,17 @@ int Engine::kernel_count(uint32_t images) {
 
 int Engine::snapshot(uint32_t tensor, void *out, uint32_t bytes) {
     if (!ready_ || tensor >= P_.h.nt || !out || bytes != P_.ts[tensor].bytes) return 22;
-    auto it = batches_.find(last_images_ ? last_images_ : 1);
-    const uint8_t *src = nullptr;
-    if (it != batches_.end()) src = it->second->ptr[tensor];
-    else src = d_const_ + P_.ts[tensor].offset;
+    // The tensor as the last run left it: the last image of the context that ran last (the static
+    // arena after ug_run_static, the last piece of a pipelined batch). Per-image tensors live in
+    // the context's arena, one copy per image; constants read in place have a single copy.
+    const uint8_t *src = d_const_ + P_.ts[tensor].offset;
+    if (last_ctx_ && !last_ctx_->ptr.empty()) {
+        const BatchCtx &B = *last_ctx_;
+        src = B.ptr[tensor];
+        if (src >= B.arena && src < B.arena + B.arena_bytes) src += (size_t)(B.images - 1) * bytes;
+    }
     UQ_CUDA(cudaSetDevice(device_));
+    UQ_CUDA(cudaStreamSynchronize(stream_));
     UQ_CUDA(cudaMemcpy(out, src, bytes, cudaMemcpyDeviceToHost));
     return 0;
 }

@@ -23,6 +23,34 @@ namespace uq {
 constexpr size_t kStaticArenaBytes = (size_t)16 << 20;  // fixed arena of run_static (runtime/graph.h:7)
 constexpr size_t kNoOffset = ~(size_t)0;
 
+// Piece schedule of a pipelined host batch (Engine::run_pipelined), host-only and pure so that
+// every rank of a gathered run can be shown to cut the same pieces. The first piece is 1/16 of
+// the batch (64 to 256 images); each next one is `growth` times the previous; at most
+// kMaxPieces; a remainder under half a piece joins the last one.
+constexpr double kInitialPieceGrowth = 1.25;
+constexpr size_t kMaxPieces = 16;
+inline std::vector<uint32_t> pipeline_pieces(uint32_t images, double growth) {
+    std::vector<uint32_t> sizes;
+    uint32_t left = images;
+    double cur = images / 16.0 < 64.0 ? 64.0 : images / 16.0 > 256.0 ? 256.0 : images / 16.0;
+    while (left) {
+        uint32_t n = left < (uint32_t)cur ? left : (uint32_t)cur;
+        if (left - n < (uint32_t)(cur * 0.5) || sizes.size() + 1 == kMaxPieces) n = left;
+        sizes.push_back(n);
+        left -= n;
+        cur *= growth;
+    }
+    return sizes;
+}
+// The growth a call uses. `fixed` (UNOQ_PIPE_GROWTH, 0 when unset) wins. A session that has joined
+// an output gather always uses the initial factor: each piece enqueues one gather step, so every
+// rank must cut identical pieces, whatever it measured on calls made before joining or on
+// calls that gather nothing (decoder calls). Otherwise the factor learned from the last call.
+inline double pipeline_growth(bool gather_joined, double learned, double fixed) {
+    if (fixed > 0) return fixed;
+    return gather_joined ? kInitialPieceGrowth : learned;
+}
+
 struct BatchCtx;
 
 // One plan op lowered to device work. `run` enqueues its kernels on the stream and returns 0
@@ -145,9 +173,10 @@ class Engine {
     cudaEvent_t pipe_ev_[3][2] = {};                         // per slot: input landed, computed, output read
     cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
     cudaEvent_t pipe_t_[4] = {};         // timing of the last piece: upload start / end, graph start / end
-    double pipe_growth_ = 1.25;          // piece growth: compute / upload time per image, from the last call
+    double pipe_growth_ = kInitialPieceGrowth;  // piece growth: compute / upload time per image, from the last call
     float last_ms_ = 0.f;
     uint32_t last_images_ = 0;
+    const BatchCtx *last_ctx_ = nullptr; // context of the last run (a batch piece or the static arena)
     bool profiling_ = false;
     std::vector<uint64_t> ticks_;        // [0] runs, [1] total ns, [2+i] op ns
     std::unique_ptr<OutputGather> gather_;
