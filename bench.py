@@ -183,6 +183,14 @@ class Dist:
             raise RuntimeError("bad broadcast")
         return obj[0]
 
+    def gather_object(self, obj):
+        """Every rank's `obj` as a list on rank 0 (None elsewhere), over the gloo group."""
+        if not self.pg:
+            return [obj]
+        out = [None] * self.world if self.rank == 0 else None
+        self.dist.gather_object(obj, out, dst=0)
+        return out
+
     def close(self):
         if self.pg:
             self.dist.destroy_process_group()
@@ -195,6 +203,31 @@ def shard(global_batch, world, rank):
         raise ValueError(f"global batch {global_batch} does not divide over {world} GPUs")
     per = global_batch // world
     return rank * per, per
+
+
+def image_input(index, ni):
+    """Seeded synthetic image `index` of the global batch (uniform int8). Each image has its own
+    random stream, so the output check can regenerate any sample without the rest of the batch."""
+    return np.random.default_rng([1234, index]).integers(-128, 128, size=ni, dtype=np.int8)
+
+
+def sample_rows(per_gpu):
+    """Local image indices checked on every rank: the first, middle and last of its shard."""
+    return sorted({0, per_gpu // 2, per_gpu - 1})
+
+
+def verify_outputs(plan, ni, samples, dist):
+    """Rank 0: compare sampled output rows with the reference runtime's outputs for the same seeded
+    images (oracle/_ref/libug_ref.so in a spawn pool; outside every timed region). `samples` maps
+    a path name to {global image index: output bytes}. Returns the line's "verify" entry."""
+    from oracle.refpool import checker_kind, reference_outputs
+    index = sorted({g for rows in samples.values() for g in rows})
+    expect = dict(zip(index, reference_outputs(plan, [image_input(g, ni) for g in index])))
+    mismatch = {path: [g for g, row in rows.items() if row != expect[g].tobytes()] for path, rows in samples.items()}
+    return {"images": len(index), "mismatch": sum(len(v) for v in mismatch.values()),
+            "checked": {path: len(rows) for path, rows in samples.items()},
+            "mismatched_images": {p: v[:8] for p, v in mismatch.items() if v}, "checker": checker_kind(),
+            "ranks": dist.world}
 
 
 def join_gather(lib, handle, dist):
@@ -355,7 +388,7 @@ def bench_model(lib, dist, name, global_batch, steps, warmup, peaks, want_roofli
     spec = MODELS[name]
     model = load(ROOT / "models" / f"{name}.uqmodel")
     plan = model.plan
-    _, per_gpu = shard(global_batch, dist.world, dist.rank)
+    start, per_gpu = shard(global_batch, dist.world, dist.rank)
     err = C.c_int()
     buf = C.create_string_buffer(plan, len(plan))
     handle = lib.ug_open_mode(buf, len(plan), 0, C.byref(err))
@@ -375,8 +408,8 @@ def bench_model(lib, dist, name, global_batch, steps, warmup, peaks, want_roofli
         out_images = per_gpu * (dist.world if dist.rank == 0 else 1)
         h_out = lib.ug_host_alloc(no * out_images)
         x_host = np.ctypeslib.as_array(C.cast(h_in, C.POINTER(C.c_int8)), shape=(ni * per_gpu,))
-        x_host[:] = np.random.default_rng(1234 + dist.rank).integers(-128, 128, size=ni * per_gpu,
-                                                                        dtype=np.int64).astype(np.int8)
+        for i in range(per_gpu):
+            x_host[i * ni:(i + 1) * ni] = image_input(start + i, ni)
         # device-resident inputs: the seeded images are uploaded once into the batch's arena
         rc = lib.ug_upload_batch(handle, h_in, per_gpu)
         if rc:
@@ -394,6 +427,13 @@ def bench_model(lib, dist, name, global_batch, steps, warmup, peaks, want_roofli
         dist.barrier()
         t_dev = dist.max(ms.value / 1e3)
         value = global_batch * steps / t_dev
+        # outputs of the device-resident graph that was just timed, sampled on every rank
+        rc = lib.ug_download_batch(handle, h_out, per_gpu)
+        if rc:
+            raise RuntimeError(f"ug_download_batch rc={rc}: {lib.ug_last_error()}")
+        y_host = np.ctypeslib.as_array(C.cast(h_out, C.POINTER(C.c_int8)), shape=(no * out_images,))
+        local = {start + i: y_host[i * no:(i + 1) * no].tobytes() for i in sample_rows(per_gpu)}
+        resident = dist.gather_object(local)
         # e2e through the public batch API (pinned host buffers, copies inside the timed region)
         for _ in range(1):
             rc = lib.ug_infer_batch(handle, h_in, per_gpu, h_out)
@@ -408,6 +448,13 @@ def bench_model(lib, dist, name, global_batch, steps, warmup, peaks, want_roofli
             e2e_ms += lib.ug_last_infer_ms(handle)
         dist.barrier()
         t_e2e = dist.max(e2e_ms / 1e3)
+        verify = None
+        if dist.rank == 0:
+            # rank 0 holds the whole gathered batch of the last ug_infer_batch call, rank-major
+            gathered = {r * per_gpu + i: y_host[(r * per_gpu + i) * no:(r * per_gpu + i + 1) * no].tobytes()
+                        for r in range(dist.world) for i in sample_rows(per_gpu)}
+            merged = {g: row for part in resident for g, row in part.items()}
+            verify = verify_outputs(plan, ni, {"device_resident": merged, "ug_infer_batch": gathered}, dist)
         h2d_gbs = pcie_h2d_gbs(ni * per_gpu, dist.local)
         roof = breakdown = None
         if want_roofline:
@@ -422,6 +469,7 @@ def bench_model(lib, dist, name, global_batch, steps, warmup, peaks, want_roofli
                     "pcie_h2d_gbs": h2d_gbs,
                     "h2d_bound_images_per_s": round(h2d_gbs * 1e9 / ni * dist.world, 1) if h2d_gbs else None},
             "clocks": clocks.summary(), "roofline": roof, "breakdown": breakdown, "detect_e2e": detected,
+            "verify": verify,
         }
     finally:
         lib.ug_close(handle)
@@ -565,6 +613,13 @@ def main():
         "roofline": roof, "cpu_baseline": cpu, "clocks": res["clocks"], "gpu_launches": launches,
         "per_gpu_batch": res["per_gpu_batch"], "kernel_breakdown": res["breakdown"],
     }
+    checks = {"mobilenetv4-small": res["verify"]}
+    if yolo is not None:
+        checks["yolo26n-320"] = yolo["verify"]
+    line["verify"] = {"images": sum(c["images"] for c in checks.values()),
+                      "mismatch": sum(c["mismatch"] for c in checks.values()), "models": checks,
+                      "what": "first, middle and last image of every rank's shard, from the timed device-resident "
+                              "graph and from the gathered ug_infer_batch output, against the reference runtime"}
     if yolo is not None:
         line[MODELS["yolo26n-320"]["key"]] = {
             "value": round(yolo["value"], 2), "unit": "images/s", "global_batch": args.yolo_batch,
