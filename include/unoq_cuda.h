@@ -181,6 +181,12 @@ UG_API int ug_detect_batch(void *session, const void *input, uint32_t images, ui
 UG_API int ug_launch_detect(void *session, uint32_t images, uint32_t k);
 UG_API int ug_detect_buffer(void *session, uint32_t images, uint32_t k, void **device_records);
 
+/* Dense INT8 tensor-core throughput of the selected device, measured: one CTA per SM issues
+ * `iterations` rounds of four tcgen05.mma kind::i8 (M 128, N 256, K 32) on shared-memory operands
+ * into TMEM; best of three launches, in TOPS (milliseconds of that launch optional). The roofline
+ * denominator of the tensor-core convolutions. */
+UG_API int ug_measure_int8_peak(uint32_t iterations, float *tops, float *milliseconds);
+
 /* Last CUDA error string seen by the library (empty if none). */
 UG_API const char *ug_last_error(void);
 

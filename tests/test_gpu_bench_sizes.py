@@ -45,8 +45,9 @@ def test_every_image_of_a_timed_batch_matches_reference(name, images, native):
 
 @pytest.mark.parametrize("name,images,count", [("mobilenetv4-small", 4096, 12), ("yolo26n-320", 1024, 8)])
 def test_bench_batch_device_resident_and_pipelined(name, images, count, native):
-    """The bench's own batch sizes: the device-resident graph (the `value` path) and the pipelined
-    host batch (the `e2e` path) give identical outputs, and sampled images equal the reference's."""
+    """The bench's own batch sizes: the device-resident graph (the `value` path, replayed three times
+    after one upload, so the input tensor must survive each replay) and the pipelined host batch
+    (the `e2e` path) give identical outputs, and sampled images equal the reference's."""
     from unoq_dsp import load
     plan = load(model_path(name)).plan
     shape = SHAPES[name]
@@ -60,7 +61,8 @@ def test_bench_batch_device_resident_and_pipelined(name, images, count, native):
         try:
             C.memmove(h_in, xs.ctypes.data, xs.nbytes)
             assert native.ug_upload_batch(s.handle, h_in, images) == 0, native.ug_last_error()
-            assert native.ug_launch_batch(s.handle, images) == 0, native.ug_last_error()
+            for _ in range(3):  # replays after one upload, as the bench times them
+                assert native.ug_launch_batch(s.handle, images) == 0, native.ug_last_error()
             assert native.ug_synchronize(s.handle) == 0, native.ug_last_error()
             assert native.ug_download_batch(s.handle, h_out, images) == 0, native.ug_last_error()
             resident = np.ctypeslib.as_array(C.cast(h_out, C.POINTER(C.c_int8)), shape=(images, no)).copy()
@@ -74,3 +76,23 @@ def test_bench_batch_device_resident_and_pipelined(name, images, count, native):
         np.testing.assert_array_equal(resident[i], expect[j], err_msg=f"device-resident image {i}")
     diff = np.flatnonzero((resident != piped).any(axis=1))
     assert diff.size == 0, f"pipelined batch differs from the device-resident one on images {diff[:8].tolist()}"
+
+
+@pytest.mark.parametrize("case", ["block", "c2f_bytes", "transpose_nchw", "bmm_attn_qk"])
+def test_replays_after_one_upload_keep_their_input(case, native, golden_ops):
+    """ug_launch_batch replayed without a new upload gives the same bytes every time: no tensor of
+    the step reuses the input tensor's storage."""
+    plan, x = golden_ops[f"{case}/plan"].tobytes(), golden_ops[f"{case}/x"]
+    images = 37
+    rng = np.random.default_rng(8)
+    xs = np.concatenate([x.reshape(1, -1)] + [rng.integers(-128, 128, size=(1, x.size), dtype=np.int64)
+                                              .astype(np.int8) for _ in range(images - 1)])
+    with NativeSession(native, plan) as s:
+        expect = s.run(xs, images)
+        assert native.ug_upload_batch(s.handle, xs.ctypes.data, images) == 0
+        y = np.empty_like(expect)
+        for _ in range(4):
+            assert native.ug_launch_batch(s.handle, images) == 0
+        assert native.ug_download_batch(s.handle, y.ctypes.data, images) == 0, native.ug_last_error()
+    np.testing.assert_array_equal(y, expect)
+    np.testing.assert_array_equal(y[:golden_ops[f"{case}/y"].size], golden_ops[f"{case}/y"])

@@ -15,7 +15,7 @@ CSRC = HERE / "csrc"
 LIB = HERE / "lib" / "libunoq_cuda.so"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-SOURCES = ["plan.cpp", "k_simt.cu", "k_bytes.cu", "k_dw.cu", "k_conv_small.cu", "conv_tc.cu", "conv_rows.cu", "conv_taps.cu", "k_decode.cu", "gather.cu", "engine.cu", "abi.cu"]
+SOURCES = ["plan.cpp", "k_simt.cu", "k_bytes.cu", "k_dw.cu", "k_conv_small.cu", "conv_tc.cu", "conv_rows.cu", "conv_taps.cu", "k_decode.cu", "gather.cu", "engine.cu", "abi.cu", "k_gemm.cu", "ops_abi.cu", "k_peak.cu"]
 
 
 def build(debug=False, verbose=False):
@@ -29,7 +29,7 @@ def build(debug=False, verbose=False):
     for src in SOURCES:
         obj = objdir / (src + ".o")
         path = CSRC / src
-        deps = [path] + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.hpp")) + [ROOT / "include" / "unoq_cuda.h"]
+        deps = [path] + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.hpp")) + list((ROOT / "include").glob("*.h"))
         if not obj.exists() or any(d.stat().st_mtime > obj.stat().st_mtime for d in deps):
             cmd = [NVCC] + common + ["-x", "cu" if src.endswith(".cu") else "c++", "-c", str(path), "-o", str(obj)]
             if verbose:

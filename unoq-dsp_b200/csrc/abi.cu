@@ -33,6 +33,8 @@ int pick_device() {
 
 }  // namespace
 
+int uq::abi_device() { return pick_device(); }
+
 extern "C" {
 
 int ug_load(const void *plan, uint32_t bytes) {
@@ -278,6 +280,11 @@ int ug_detect_buffer(void *session, uint32_t images, uint32_t k, void **device_r
     if (!s || !images) return 1003;
     const int rc = s->engine.detect_buffer(images, k, device_records);
     return rc == 22 ? 1003 : rc;
+}
+
+int ug_measure_int8_peak(uint32_t iterations, float *tops, float *milliseconds) {
+    std::lock_guard<std::mutex> lk(g_graph_mu);
+    return uq::measure_int8_peak(iterations, tops, milliseconds);
 }
 
 const char *ug_last_error(void) { return uq::last_error(); }

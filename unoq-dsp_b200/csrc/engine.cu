@@ -706,6 +706,10 @@ void Engine::layout(uint32_t images, std::vector<size_t> &offset, std::vector<ui
         }
         gid[t] = gid[r];
     }
+    // The input tensor's bytes stay untouched for the whole step: a device-resident batch is
+    // uploaded once and may be launched again (ug_launch_batch, ug_time_batch), so no later
+    // tensor may reuse its storage after its last reader.
+    if (gid[root[P.h.input]] >= 0) groups[gid[root[P.h.input]]].death = (int)P.h.no;
     std::vector<int> order(groups.size());
     std::iota(order.begin(), order.end(), 0);
     std::sort(order.begin(), order.end(), [&](int x, int y) { return groups[x].size > groups[y].size; });
@@ -1004,6 +1008,28 @@ int Engine::run_static(const void *in, void *out) {
     }
     last_ctx_ = &static_;
     last_images_ = 1;
+    return device_status();
+}
+
+int Engine::run_device(const void *in, void *out, uint32_t images) {
+    if (!ready_ || !in || !out || !images) return 22;
+    BatchCtx B;
+    B.images = images;
+    B.ptr.assign(P_.h.nt, nullptr);
+    for (uint32_t t = 0; t < P_.h.nt; t++) {
+        if (t == P_.h.input) B.ptr[t] = static_cast<uint8_t *>(const_cast<void *>(in));
+        else if (t == P_.h.output) B.ptr[t] = static_cast<uint8_t *>(out);
+        else if (P_.ts[t].flags) B.ptr[t] = d_const_ + P_.ts[t].offset;
+        else return 22;
+    }
+    UQ_CUDA(cudaSetDevice(device_));
+    int rc = run_steps(B, stream_, false);
+    if (rc) return rc;
+    const cudaError_t e = cudaStreamSynchronize(stream_);
+    if (e != cudaSuccess) {
+        set_error(std::string("operator run: ") + cudaGetErrorString(e));
+        return 2001;
+    }
     return device_status();
 }
 

@@ -96,6 +96,10 @@ class Engine {
     // lays the plan out (host) and looks up the arena's address; calls that overlap on one device
     // share the arena and must be serialised by the caller.
     int run_static(const void *in, void *out);
+    // Eager run over caller-owned device buffers: `in` / `out` hold `images` back-to-back copies of
+    // the plan's input / output tensor. Only plans whose activations are exactly the input and the
+    // output qualify (the one-op plans of the operator ABI); others get 22. Synchronous.
+    int run_device(const void *in, void *out, uint32_t images);
     // Device buffers of the batch context (input tensor, output tensor of image 0).
     int buffers(uint32_t images, void **d_in, void **d_out);
     int launch(uint32_t images);   // async on stream_
@@ -189,6 +193,13 @@ class Engine {
     int gather(const BatchCtx &b);       // enqueue the output gather when multi-rank
     int finish(cudaEvent_t ev);          // wait for `ev`, bounded when a collective is pending
 };
+
+// The CUDA device the C ABI works on: ug_set_device's choice, else UNOQ_CUDA_DEVICE, else 0.
+int abi_device();
+
+// Dense INT8 tensor-core throughput of that device (k_peak.cu): best of three launches of
+// `iterations` MMA rounds per SM, in TOPS; *ms gets that launch's time.
+int measure_int8_peak(uint32_t iterations, float *tops, float *ms);
 
 // Records the last CUDA failure for ug_last_error().
 void set_error(const std::string &msg);

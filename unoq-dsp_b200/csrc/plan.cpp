@@ -45,6 +45,9 @@ bool broadcastable(const Tensor &a, const Tensor &b) {  // graph.c:33-40
     return same_shape(a, b);
 }
 
+
+}  // namespace
+
 // qnn.c:209-252: vision op parameter block (codes 14-17).
 int validate_vision(const Op &o, const Tensor &a, const Tensor &b, const Tensor &z, const Tensor &t,
                     const int32_t *q, const int8_t *w, uint64_t &work) {
@@ -115,8 +118,6 @@ int validate_vision(const Op &o, const Tensor &a, const Tensor &b, const Tensor 
     work += rows * k * q[17];
     return 0;
 }
-
-}  // namespace
 
 int parse_plan(const void *blob, uint32_t len, Plan &out) {
     Plan P;

@@ -43,6 +43,11 @@ struct Plan {
 // loader's overflow proofs and by weight preparation.
 int32_t host_scale(int32_t v, int32_t m, int shift);
 
+// The vision ops' parameter-block check (qnn.c:209-252, uq_validate): codes 14-17, host copies of
+// the q block and weights. Returns 0 (adding the op's work to `work`) or 18.
+int validate_vision(const Op &o, const Tensor &a, const Tensor &b, const Tensor &z, const Tensor &t,
+                    const int32_t *q, const int8_t *w, uint64_t &work);
+
 // Parse and validate; on success `out` holds the plan and lifetimes. Returns 0 or 10..25.
 int parse_plan(const void *blob, uint32_t len, Plan &out);
 

@@ -72,6 +72,7 @@ _SIGNATURES = {
     "ug_detect_batch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]),
     "ug_launch_detect": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32]),
     "ug_detect_buffer": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.POINTER(C.c_void_p)]),
+    "ug_measure_int8_peak": (C.c_int, [C.c_uint32, C.POINTER(C.c_float), C.POINTER(C.c_float)]),
     "ug_last_error": (C.c_char_p, []),
 }
 
