@@ -293,7 +293,7 @@ def roofline(lib, handle, plan, images, iters, peaks, kernel_names):
     t = d["ns"] * 1e-9
     gbs = d["bytes"] / t / 1e9
     tops = d["ops"] / t / 1e12
-    int8_peak = 2 * peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
+    int8_peak = peaks.get("int8_tops") or 2 * peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
     hbm = peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])
     ai = d["ops"] / max(d["bytes"], 1)
     bound = "hbm" if ai < int8_peak * 1e12 / (hbm * 1e9) else "tensor"
@@ -475,25 +475,175 @@ def bench_model(lib, dist, name, global_batch, steps, warmup, peaks, want_roofli
         lib.ug_close(handle)
 
 
-TRAFFIC_PROFILES = {"mobilenetv4-small": "mnv4_b512_launches.md", "yolo26n-320": "yolo26n_b128_launches.md"}
+# --------------------------------------------------------------------------- BASELINE configs 0-3
+class L2Flush:
+    """Writes a buffer twice the L2 size between timed launches, so that a config whose working
+    set fits in the 126 MB L2 is still timed from HBM."""
+
+    def __init__(self, device):
+        import torch
+        self.torch = torch
+        self.buf = torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{device}")
+        self.n = 0
+
+    def __call__(self):
+        self.n += 1
+        self.buf.fill_(self.n & 255)
+        self.torch.cuda.synchronize()
 
 
-def conv_traffic_per_image(model="mobilenetv4-small"):
-    """DRAM bytes per image of the conv launches of one step of `model`, from the committed ncu
-    launch-list summary under profiles/; None when absent."""
-    import re
-    p = ROOT / "profiles" / TRAFFIC_PROFILES[model]
-    m = re.search(r"conv_dram_bytes_per_image = (\d+)", p.read_text()) if p.is_file() else None
-    return int(m.group(1)) if m else None
+def time_plan(lib, plan, images, reps, flush):
+    """Median milliseconds of one graph launch of `plan` at `images` (device-resident seeded inputs),
+    L2 flushed before each launch, CUDA events on the session stream (ug_time_batch, 1 iteration)."""
+    err = C.c_int()
+    buf = C.create_string_buffer(plan, len(plan))
+    h = lib.ug_open_mode(buf, len(plan), 0, C.byref(err))
+    if not h:
+        raise RuntimeError(f"ug_open_mode {err.value}: {lib.ug_last_error()}")
+    try:
+        ni = lib_input_bytes(plan)
+        x = np.random.default_rng(5).integers(-128, 128, size=ni * images, dtype=np.int8)
+        if lib.ug_upload_batch(h, x.ctypes.data, images):
+            raise RuntimeError(lib.ug_last_error())
+        ms = C.c_float()
+        for _ in range(3):
+            lib.ug_time_batch(h, images, 1, C.byref(ms))
+        times = []
+        for _ in range(reps):
+            flush()
+            if lib.ug_time_batch(h, images, 1, C.byref(ms)):
+                raise RuntimeError(lib.ug_last_error())
+            times.append(ms.value)
+        return statistics.median(times)
+    finally:
+        lib.ug_close(h)
+
+
+def lib_input_bytes(plan):
+    import struct
+    inp = struct.unpack_from("<I", plan, 20)[0]
+    return struct.unpack_from("<12I", plan, 32 + 48 * inp)[1]
+
+
+def infer_latency(lib, plan, reps=100):
+    """Batch-1 latency of the public single-image call ug_infer (pageable host buffers in and out,
+    synchronous): median and 99th percentile wall-clock milliseconds over `reps` calls."""
+    err = C.c_int()
+    buf = C.create_string_buffer(plan, len(plan))
+    h = lib.ug_open_mode(buf, len(plan), 0, C.byref(err))
+    if not h:
+        raise RuntimeError(f"ug_open_mode {err.value}: {lib.ug_last_error()}")
+    try:
+        import struct
+        out_t = struct.unpack_from("<I", plan, 24)[0]
+        ni, no = lib_input_bytes(plan), struct.unpack_from("<12I", plan, 32 + 48 * out_t)[1]
+        x = np.random.default_rng(6).integers(-128, 128, size=ni, dtype=np.int8)
+        y = np.empty(no, dtype=np.int8)
+        for _ in range(10):
+            lib.ug_infer(h, x.ctypes.data, ni, y.ctypes.data, no)
+        t = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            if lib.ug_infer(h, x.ctypes.data, ni, y.ctypes.data, no):
+                raise RuntimeError(lib.ug_last_error())
+            t.append((time.perf_counter() - t0) * 1e3)
+        t.sort()
+        return {"median_ms": round(statistics.median(t), 4), "p99_ms": round(t[int(0.99 * (len(t) - 1))], 4),
+                "calls": reps, "device_ms": round(lib.ug_last_infer_ms(h), 4)}
+    finally:
+        lib.ug_close(h)
+
+
+def bench_configs(lib, device, peaks, int8_peak, cores):
+    """BASELINE configs 0-3 on one GPU, each beside the reference C path on this host (1 core and
+    all cores): config 0 (pointwise conv) and config 1 (16 depthwise layers) per layer at batch 1
+    and 256 with GB/s against the measured HBM copy rate; config 2 (MobileNetV4) at batch 1 / 64 /
+    256 and config 3 (YOLO26n) at batch 1 / 128 in images/s; and ug_infer batch-1 latency."""
+    from unoq_dsp import synth
+    from unoq_dsp.bundle import load
+    hbm = peaks["hbm_gbs"]
+    flush = L2Flush(device)
+    gpu, jobs = {}, []
+    for name, _ in synth.baseline_config_cases():
+        plan, xs, _ = synth.baseline_config(name)
+        row = {}
+        for images in (1, 256):
+            ms = time_plan(lib, plan, images, 9, flush)
+            t = op_traffic(plan, images)
+            byt, ops = sum(r["bytes"] for r in t), sum(r["ops"] for r in t)
+            row[f"b{images}"] = {"ms": round(ms, 5), "GB/s": round(byt / (ms * 1e-3) / 1e9, 1),
+                                 "frac_hbm": round(byt / (ms * 1e-3) / 1e9 / hbm, 4),
+                                 "TOPS": round(ops / (ms * 1e-3) / 1e12, 2),
+                                 "frac_int8": round(ops / (ms * 1e-3) / 1e12 / int8_peak, 4),
+                                 "images_per_s": round(images / (ms * 1e-3), 1), "algorithmic_bytes": byt}
+        gpu[name] = row
+        jobs.append((name, plan, int(np.prod(xs)), 3 if name.startswith("config1") else 5))
+    models = {"mobilenetv4-small": (1, 64, 256), "yolo26n-320": (1, 128)}
+    latency = {}
+    for name, batches in models.items():
+        plan = load(ROOT / "models" / f"{name}.uqmodel").plan
+        row = {}
+        for images in batches:
+            ms = time_plan(lib, plan, images, 5, flush)
+            row[f"b{images}"] = {"ms": round(ms, 4), "images_per_s": round(images / (ms * 1e-3), 1)}
+        gpu[name] = row
+        latency[name] = infer_latency(lib, plan)
+        jobs.append((name, plan, lib_input_bytes(plan), 2))
+    del flush
+    from oracle.refpool import reference_timings
+    ref = reference_timings(jobs, cores)
+    return {"gpu": gpu, "ug_infer_batch1_latency": latency, "reference_cpu": ref,
+            "timing": "CUDA events around one graph launch, L2 flushed (256 MB write) before each, median; "
+                      "device-resident seeded inputs", "int8_peak_tops": int8_peak,
+            "reference_kind": "oracle/_ref/libug_ref.so (the reference runtime's C, gcc -O2, VISION_FLAGS)"}
+
+
+TRAFFIC_FILE = ROOT / "profiles" / "dram_traffic.json"
+CONV_KERNELS = ("conv_tc_kernel", "conv_rows_kernel", "conv_taps_kernel", "conv_small_kernel", "conv_simt_kernel")
+
+
+def traffic_from_ncu_csv(csv_path, images, step_launches=None):
+    """DRAM bytes per image of the conv launches in an ncu launch list (--csv, with the metrics
+    dram__bytes_read.sum and dram__bytes_write.sum) of one step at `images` images per launch:
+    the first `step_launches` launches of the list (all when None)."""
+    import csv
+    total, launches = 0.0, set()
+    with open(csv_path, newline="") as f:
+        rows = [r for r in csv.reader(line for line in f if line.startswith('"'))]
+    head = rows[0]
+    col = {k: head.index(k) for k in ("ID", "Kernel Name", "Metric Name", "Metric Unit", "Metric Value")}
+    scale = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9, "KB": 1024, "MB": 1024 ** 2, "GB": 1024 ** 3}
+    for r in rows[1:]:
+        if step_launches is not None and int(r[col["ID"]]) >= step_launches:
+            continue
+        if r[col["Metric Name"]] in ("dram__bytes_read.sum", "dram__bytes_write.sum") and \
+                any(k in r[col["Kernel Name"]] for k in CONV_KERNELS):
+            total += float(r[col["Metric Value"]].replace(",", "")) * scale.get(r[col["Metric Unit"]], 1)
+            launches.add(r[col["ID"]])
+    return {"conv_dram_bytes_per_image": int(round(total / images)), "conv_launches": len(launches),
+            "images_per_launch": images, "step_launches": step_launches, "csv": Path(csv_path).name}
+
+
+def write_traffic(model, csv_path, images, step_launches):
+    """Record one model's conv DRAM traffic per image in profiles/dram_traffic.json."""
+    data = json.loads(TRAFFIC_FILE.read_text()) if TRAFFIC_FILE.is_file() else {}
+    data[model] = traffic_from_ncu_csv(csv_path, images, step_launches)
+    TRAFFIC_FILE.write_text(json.dumps(data, indent=1, sort_keys=True) + "\n")
+    return data[model]
 
 
 def attach_traffic(roof, model, images):
-    """Fill roofline.traffic of the conv family from the model's committed launch list."""
-    per_image = conv_traffic_per_image(model)
-    if roof is not None and per_image and roof.get("kernel") == "conv":
-        roof["traffic"] = per_image * images
-        roof["traffic_source"] = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of the conv launches of one step "
-                                  f"(profiles/{TRAFFIC_PROFILES[model]}), scaled by images")
+    """Fill roofline.traffic of the conv family from profiles/dram_traffic.json (written from the
+    ncu launch-list CSV by `bench.py --write-traffic`), scaled to this step's images: every image
+    is an independent slice of each launch, so DRAM traffic grows with the images processed."""
+    if roof is None or roof.get("kernel") != "conv" or not TRAFFIC_FILE.is_file():
+        return
+    entry = json.loads(TRAFFIC_FILE.read_text()).get(model)
+    if entry:
+        roof["traffic"] = entry["conv_dram_bytes_per_image"] * images
+        roof["traffic_source"] = (f"ncu dram__bytes_read.sum + dram__bytes_write.sum of the {entry['conv_launches']} "
+                                  f"conv launches of one step at {entry['images_per_launch']} images "
+                                  f"(profiles/dram_traffic.json from {entry['csv']}), scaled by images")
 
 
 def load_peaks():
@@ -514,9 +664,17 @@ def main():
     ap.add_argument("--yolo-batch", type=int, default=MODELS["yolo26n-320"]["batch"])
     ap.add_argument("--no-yolo", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip the BASELINE config 0-3 section (1 GPU only)")
     ap.add_argument("--yolo-only", action="store_true",
                     help="profiling aid: run only the YOLO26n section and print its fields")
+    ap.add_argument("--write-traffic", nargs=4, metavar=("MODEL", "CSV", "IMAGES", "STEP_LAUNCHES"),
+                    help="record a model's conv DRAM traffic from the first STEP_LAUNCHES launches (one step) "
+                         "of an ncu launch-list CSV, then exit")
     args = ap.parse_args()
+    if args.write_traffic:
+        model, csv_path, images, step = args.write_traffic
+        print(json.dumps(write_traffic(model, csv_path, int(images), int(step))))
+        return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     mpath = ROOT / "models" / "mobilenetv4-small.uqmodel"
@@ -572,6 +730,11 @@ def main():
     if lib.ug_set_device(dist.local) != 0:
         raise SystemExit(f"cannot select CUDA device {dist.local}")
     peaks = load_peaks()
+    # the INT8 tensor-core peak of this device, measured (tcgen05 kind::i8 on shared-memory operands)
+    tops, peak_ms = C.c_float(), C.c_float()
+    if lib.ug_measure_int8_peak(8192, C.byref(tops), C.byref(peak_ms)) == 0 and tops.value > 0:
+        peaks["int8_tops"] = round(float(tops.value), 1)
+        peaks["int8_source"] = f"measured: ug_measure_int8_peak, {peak_ms.value:.2f} ms launch, burst"
     if args.yolo_only:
         yolo = bench_model(lib, dist, "yolo26n-320", args.yolo_batch, args.steps, args.warmup, peaks, True, detect=True)
         dist.close()
@@ -593,6 +756,10 @@ def main():
         cpu = {"value": round(value, 3), "unit": "images/s", "cores": cores, "kind": "reference",
                "sample": f"{per_proc * cores} MobileNetV4 images ({per_proc} per process on {cores} processes), "
                          f"{wall:.1f} s wall"}
+    configs = None
+    if world == 1 and not args.no_configs:
+        int8 = peaks.get("int8_tops") or 2 * peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
+        configs = bench_configs(lib, dist.local, peaks, int8, cores)
     launches = int(dist.sum(res["kernels_per_step"] * args.steps))  # whole job: every rank's launches
     dist.close()
     if rank != 0:
@@ -612,7 +779,10 @@ def main():
         "e2e": {k: (round(v, 2) if isinstance(v, float) else v) for k, v in res["e2e"].items()},
         "roofline": roof, "cpu_baseline": cpu, "clocks": res["clocks"], "gpu_launches": launches,
         "per_gpu_batch": res["per_gpu_batch"], "kernel_breakdown": res["breakdown"],
+        "int8_peak": {"tops": peaks.get("int8_tops"), "source": peaks.get("int8_source", "2 x measured bf16 (stand-in)")},
     }
+    if configs is not None:
+        line["baseline_configs"] = configs
     checks = {"mobilenetv4-small": res["verify"]}
     if yolo is not None:
         checks["yolo26n-320"] = yolo["verify"]

@@ -53,3 +53,40 @@ def reference_outputs(plan, images, procs=None):
     with mp.get_context("spawn").Pool(procs, initializer=_init, initargs=(bytes(plan),)) as pool:
         outs = pool.map(_one, images, chunksize=max(1, len(images) // (4 * procs)))
     return np.stack([np.frombuffer(o, dtype=np.int8) for o in outs])
+
+
+def _time_worker(args):
+    """Seconds per image of the reference runtime on `plan` (one process, one core): one warm-up
+    image, then `reps` timed images."""
+    import time
+    plan, ni, reps, seed = args
+    for p in (str(ROOT), str(ROOT / "unoq-dsp_b200")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    from oracle.oracle import Reference
+    ref = Reference()
+    if ref.load(plan):
+        raise RuntimeError("reference ug_load failed")
+    x = np.random.default_rng(seed).integers(-128, 128, size=ni, dtype=np.int8)
+    ref.run(plan, x)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        ref.run(plan, x)
+    return (time.perf_counter() - t0) / reps
+
+
+def reference_timings(jobs, procs=None):
+    """The reference C runtime (oracle/_ref/libug_ref.so, single-threaded off Hexagon) timed two
+    ways per job (name, plan, input bytes, reps): on one core (one process alone) and on every
+    core (`procs` processes at once, each running whole images). Returns {name: {...}}."""
+    procs = max(1, procs or os.cpu_count() or 1)
+    out = {}
+    with mp.get_context("spawn").Pool(procs) as pool:
+        for name, plan, ni, reps in jobs:
+            one = pool.apply(_time_worker, ((bytes(plan), ni, reps, 1),))
+            # every process times its own images after its load and warm-up; the slowest sets the rate
+            per = pool.map(_time_worker, [(bytes(plan), ni, reps, 2 + i) for i in range(procs)], chunksize=1)
+            out[name] = {"one_core_ms": round(one * 1e3, 3), "one_core_images_per_s": round(1.0 / one, 3),
+                         "all_cores_images_per_s": round(procs / max(per), 3), "cores": procs,
+                         "images_per_process": reps}
+    return out
