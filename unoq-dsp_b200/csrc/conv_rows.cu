@@ -36,6 +36,7 @@
 #include <type_traits>
 #include <vector>
 
+#include "device_state.hpp"
 #include "conv_rows.cuh"
 #include "plan.hpp"
 #include "tc_common.cuh"
@@ -345,11 +346,11 @@ __global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const 
     }
 }
 
-int g_rows_sm_count = 0;
 
 }  // namespace
 
 struct ConvRows {
+    int sm_count = 148;  // of the device the op was prepared on
     RowsParams p{};
     size_t smem = 0;
     int epi_mode = kGeneral;
@@ -456,28 +457,21 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
         cudaMemcpy(de, epi.data(), epi.size() * sizeof(EpiChan), cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMemcpy(dc, corr.data(), corr.size() * sizeof(int32_t), cudaMemcpyHostToDevice) != cudaSuccess)
         return 2001;
-    if (!g_rows_sm_count) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g_rows_sm_count, cudaDevAttrMultiProcessorCount, dev);
-        if (g_rows_sm_count <= 0) g_rows_sm_count = 148;
-    }
-    static bool attr_set = false;
-    if (!attr_set) {
+    const bool attrs = once_per_device(kFamilyConvRows, [] {
         auto allow = [](auto fn) {
             return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsMaxSmem) == cudaSuccess;
         };
-        if (!allow(conv_rows_kernel<kRelu, 1>) || !allow(conv_rows_kernel<kTies, 1>) ||
-            !allow(conv_rows_kernel<kGeneral, 1>) || !allow(conv_rows_kernel<kRelu, 2>) ||
-            !allow(conv_rows_kernel<kTies, 2>) || !allow(conv_rows_kernel<kGeneral, 2>) ||
-            !allow(conv_rows_kernel<kRelu, 3>) || !allow(conv_rows_kernel<kTies, 3>) ||
-            !allow(conv_rows_kernel<kGeneral, 3>) ||
-            !allow(conv_rows_kernel<kRelu, 4>) || !allow(conv_rows_kernel<kTies, 4>) ||
-            !allow(conv_rows_kernel<kGeneral, 4>))
-            return 2001;
-        attr_set = true;
-    }
+        return allow(conv_rows_kernel<kRelu, 1>) && allow(conv_rows_kernel<kTies, 1>) &&
+            allow(conv_rows_kernel<kGeneral, 1>) && allow(conv_rows_kernel<kRelu, 2>) &&
+            allow(conv_rows_kernel<kTies, 2>) && allow(conv_rows_kernel<kGeneral, 2>) &&
+            allow(conv_rows_kernel<kRelu, 3>) && allow(conv_rows_kernel<kTies, 3>) &&
+            allow(conv_rows_kernel<kGeneral, 3>) &&
+            allow(conv_rows_kernel<kRelu, 4>) && allow(conv_rows_kernel<kTies, 4>) &&
+            allow(conv_rows_kernel<kGeneral, 4>);
+    });
+    if (!attrs) return 2001;
     ConvRows *c = new ConvRows();
+    c->sm_count = current_sm_count();
     RowsParams &p = c->p;
     p.w = static_cast<const int8_t *>(dw);
     p.epi = static_cast<const EpiChan *>(de);
@@ -558,7 +552,7 @@ int conv_rows_launch(const ConvRows &c, const int8_t *x, int8_t *y, const ConvGe
                 CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return 2001;
     }
-    const int grid = std::min(g_rows_sm_count, p.tiles);
+    const int grid = std::min(c.sm_count, p.tiles);
     constexpr int T = (2 + kRowsEW) * 32;
     auto go = [&](auto chunks) {
         constexpr int CH = decltype(chunks)::value;

@@ -27,6 +27,7 @@
 #include <type_traits>
 #include <vector>
 
+#include "device_state.hpp"
 #include "conv_taps.cuh"
 #include "plan.hpp"
 #include "tc_common.cuh"
@@ -268,27 +269,30 @@ __global__ void __launch_bounds__((2 + kTapsEW) * 32, 1) conv_taps_kernel(const 
             const int32_t *cr = (rmask | cmask) && valid ? p.corr + (size_t)((rmask << p.kw) | cmask) * p.oc + n0 : nullptr;
             int8_t *dst = p.y + (((size_t)img * p.oh + oy) * p.ow + ox) * p.oc + n0;
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.bn);
+            auto chunk = [&](uint32_t(&r)[16], int ci) {
+                if (!valid) return;
+                if (cr) {
+#pragma unroll
+                    for (int i = 0; i < 16; i++) r[i] = (uint32_t)((int32_t)r[i] + __ldg(cr + ci * 16 + i));
+                }
+                const uint4 v = epilogue_chunk<EPI>(r, E, lut, ci * 16, p.lo, p.hi);
+                *reinterpret_cast<uint4 *>(dst + ci * 16) = v;
+            };
             uint32_t ra[16], rb[16];
-            int ci = part;
-            if (ci < live_chunks) {
-                tmem_ld16_nowait(taddr + ci * 16, ra);
+            if (part < live_chunks) {  // chunks part, part + nparts, ... in two buffers in turn
+                tmem_ld16_nowait(taddr + part * 16, ra);
                 tmem_wait_ld(ra);
             }
-            while (ci < live_chunks) {
-                const int next = ci + nparts;
-                if (next < live_chunks) tmem_ld16_nowait(taddr + next * 16, rb);
-                if (valid) {
-                    if (cr) {
-#pragma unroll
-                        for (int i = 0; i < 16; i++) ra[i] = (uint32_t)((int32_t)ra[i] + __ldg(cr + ci * 16 + i));
-                    }
-                    const uint4 v = epilogue_chunk<EPI>(ra, E, lut, ci * 16, p.lo, p.hi);
-                    *reinterpret_cast<uint4 *>(dst + ci * 16) = v;
+            for (int ci = part; ci < live_chunks; ci += 2 * nparts) {
+                const int nb = ci + nparts, na = ci + 2 * nparts;
+                if (nb < live_chunks) tmem_ld16_nowait(taddr + nb * 16, rb);
+                chunk(ra, ci);
+                if (nb < live_chunks) {
+                    tmem_wait_ld(rb);
+                    if (na < live_chunks) tmem_ld16_nowait(taddr + na * 16, ra);
+                    chunk(rb, nb);
+                    if (na < live_chunks) tmem_wait_ld(ra);
                 }
-                if (next < live_chunks) tmem_wait_ld(rb);
-#pragma unroll
-                for (int q = 0; q < 16; q++) ra[q] = rb[q];
-                ci = next;
             }
             tc_fence_before();
             __syncwarp();
@@ -304,11 +308,11 @@ __global__ void __launch_bounds__((2 + kTapsEW) * 32, 1) conv_taps_kernel(const 
     }
 }
 
-int g_taps_sm_count = 0;
 
 }  // namespace
 
 struct ConvTaps {
+    int sm_count = 148;  // of the device the op was prepared on
     TapsParams p{};
     size_t smem = 0;
     int epi_mode = kGeneral;
@@ -418,22 +422,15 @@ int conv_taps_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
         cudaMemcpy(de, epi.data(), epi.size() * sizeof(EpiChan), cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMemcpy(dc, corr.data(), corr.size() * sizeof(int32_t), cudaMemcpyHostToDevice) != cudaSuccess)
         return 2001;
-    if (!g_taps_sm_count) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g_taps_sm_count, cudaDevAttrMultiProcessorCount, dev);
-        if (g_taps_sm_count <= 0) g_taps_sm_count = 148;
-    }
-    static bool attr_set = false;
-    if (!attr_set) {
+    const bool attrs = once_per_device(kFamilyConvTaps, [] {
         auto allow = [](auto fn) {
             return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kTapsMaxSmem) == cudaSuccess;
         };
-        if (!allow(conv_taps_kernel<kRelu>) || !allow(conv_taps_kernel<kTies>) || !allow(conv_taps_kernel<kGeneral>))
-            return 2001;
-        attr_set = true;
-    }
+        return allow(conv_taps_kernel<kRelu>) && allow(conv_taps_kernel<kTies>) && allow(conv_taps_kernel<kGeneral>);
+    });
+    if (!attrs) return 2001;
     ConvTaps *c = new ConvTaps();
+    c->sm_count = current_sm_count();
     TapsParams &p = c->p;
     p.w = static_cast<const int8_t *>(dw);
     p.epi = static_cast<const EpiChan *>(de);
@@ -481,7 +478,7 @@ int conv_taps_launch(const ConvTaps &c, const int8_t *x, int8_t *y, const ConvGe
     // CTAs per N tile: floor, so that all n_tiles * per_tile CTAs are resident at once (one per SM).
     // Rounding up would start the extra CTAs only after a first wave had finished, and the static
     // tile schedule would make them run a full share of tiles on their own.
-    int per_tile = g_taps_sm_count / c.n_tiles;
+    int per_tile = c.sm_count / c.n_tiles;
     if (per_tile < 1) per_tile = 1;
     if (per_tile > p.tiles) per_tile = p.tiles;
     const dim3 grid(per_tile, c.n_tiles);

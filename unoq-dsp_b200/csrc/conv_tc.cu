@@ -42,6 +42,7 @@
 #include <cuda.h>
 
 #include "conv_tc.cuh"
+#include "device_state.hpp"
 #include "plan.hpp"
 #include "requant.cuh"
 #include "tc_common.cuh"
@@ -642,28 +643,36 @@ __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(con
                 if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
                 __syncwarp();
                 const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.bn + c0);
-                uint32_t ra[16], rb[16];
-                if (my_chunks > 0) {
-                    tmem_ld16_nowait(taddr, ra);
-                    tmem_wait_ld(ra);
-                }
-                for (int ci = 0; ci < my_chunks; ci++) {
-                    const bool more = ci + 1 < my_chunks;
-                    if (more) tmem_ld16_nowait(taddr + (ci + 1) * 16, rb);
+                auto chunk = [&](const uint32_t(&r)[16], int ci) {
                     uint4 v;
                     if (p.res) {
                         const int row = mt * kBM + quarter * 32 + lane;
                         uint4 rr = make_uint4(0, 0, 0, 0);  // rows past M read no residual (never stored)
                         if (row < p.M)
                             rr = __ldg(reinterpret_cast<const uint4 *>(p.res + (size_t)row * p.oc + n0 + c0 + ci * 16));
-                        v = epilogue_chunk<EPI>(ra, E, lut, c0 + ci * 16, p.lo, p.hi, &p.add, sAdd, rr);
+                        v = epilogue_chunk<EPI>(r, E, lut, c0 + ci * 16, p.lo, p.hi, &p.add, sAdd, rr);
                     } else {
-                        v = epilogue_chunk<EPI>(ra, E, lut, c0 + ci * 16, p.lo, p.hi);
+                        v = epilogue_chunk<EPI>(r, E, lut, c0 + ci * 16, p.lo, p.hi);
                     }
                     st_shared16(smem_u32(stage + (size_t)lane * p.box + ((ci ^ swz_row) << 4)), v);
-                    if (more) tmem_wait_ld(rb);
-#pragma unroll
-                    for (int q = 0; q < 16; q++) ra[q] = rb[q];
+                };
+                // two register buffers in turn: chunk ci + 1 loads from TMEM while chunk ci is
+                // requantised, and no register copies between them
+                uint32_t ra[16], rb[16];
+                if (my_chunks > 0) {
+                    tmem_ld16_nowait(taddr, ra);
+                    tmem_wait_ld(ra);
+                }
+                for (int ci = 0; ci < my_chunks; ci += 2) {
+                    const bool has_b = ci + 1 < my_chunks, has_a = ci + 2 < my_chunks;
+                    if (has_b) tmem_ld16_nowait(taddr + (ci + 1) * 16, rb);
+                    chunk(ra, ci);
+                    if (has_b) {
+                        tmem_wait_ld(rb);
+                        if (has_a) tmem_ld16_nowait(taddr + (ci + 2) * 16, ra);
+                        chunk(rb, ci + 1);
+                        if (has_a) tmem_wait_ld(ra);
+                    }
                 }
                 tc_fence_before();
                 fence_proxy_async();  // staged bytes visible to the TMA (async proxy)
@@ -688,21 +697,25 @@ __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(con
                 tc_fence_after();
                 uint8_t *stage = sOut + (size_t)(lt & 1) * out_stride(p.bn);
                 const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.bn);
+                auto chunk = [&](const uint32_t(&r)[16], int ci) {
+                    const uint4 v = epilogue_chunk<EPI>(r, E, lut, ci * 16, p.lo, p.hi);
+                    st_shared16(smem_u32(stage + (size_t)row * (p.bn + 16) + ci * 16), v);
+                };
                 uint32_t ra[16], rb[16];
-                int ci = half;  // chunks half, half + kParts, ...
-                if (ci < live_chunks) {
-                    tmem_ld16_nowait(taddr + ci * 16, ra);
+                if (half < live_chunks) {  // chunks half, half + kParts, ... in two buffers in turn
+                    tmem_ld16_nowait(taddr + half * 16, ra);
                     tmem_wait_ld(ra);
                 }
-                while (ci < live_chunks) {
-                    const int next = ci + kParts;
-                    if (next < live_chunks) tmem_ld16_nowait(taddr + next * 16, rb);
-                    const uint4 v = epilogue_chunk<EPI>(ra, E, lut, ci * 16, p.lo, p.hi);
-                    st_shared16(smem_u32(stage + (size_t)row * (p.bn + 16) + ci * 16), v);
-                    if (next < live_chunks) tmem_wait_ld(rb);
-#pragma unroll
-                    for (int q = 0; q < 16; q++) ra[q] = rb[q];
-                    ci = next;
+                for (int ci = half; ci < live_chunks; ci += 2 * kParts) {
+                    const int nb = ci + kParts, na = ci + 2 * kParts;
+                    if (nb < live_chunks) tmem_ld16_nowait(taddr + nb * 16, rb);
+                    chunk(ra, ci);
+                    if (nb < live_chunks) {
+                        tmem_wait_ld(rb);
+                        if (na < live_chunks) tmem_ld16_nowait(taddr + na * 16, ra);
+                        chunk(rb, nb);
+                        if (na < live_chunks) tmem_wait_ld(ra);
+                    }
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -735,12 +748,11 @@ __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(con
     }
 }
 
-int g_sm_count = 0;
-
 }  // namespace
 
 struct ConvTc {
     Params p{};
+    int sm_count = 148;  // of the device the op was prepared on
     int n_tiles = 1;
     size_t smem = 0;
     int producer_warps = 8;
@@ -929,26 +941,19 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
         cudaMemcpy(de, epi.data(), epi.size() * sizeof(EpiChan), cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMemcpy(dt, tab.data(), tab.size() * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess)
         return 2001;
-    if (!g_sm_count) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev);
-        if (g_sm_count <= 0) g_sm_count = 148;
-    }
-    static bool attr_set = false;
-    if (!attr_set) {
+    const bool attrs = once_per_device(kFamilyConvTc, [] {
         auto allow = [](auto fn) {
             return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) == cudaSuccess;
         };
-        if (!allow(conv_tc_kernel<kRelu, 4, 8>) || !allow(conv_tc_kernel<kTies, 4, 8>) ||
-            !allow(conv_tc_kernel<kGeneral, 4, 8>) || !allow(conv_tc_kernel<kRelu, 8, 8>) ||
-            !allow(conv_tc_kernel<kTies, 8, 8>) || !allow(conv_tc_kernel<kGeneral, 8, 8>) ||
-            !allow(conv_tc_kernel<kRelu, 4, 16>) || !allow(conv_tc_kernel<kTies, 4, 16>) ||
-            !allow(conv_tc_kernel<kGeneral, 4, 16>))
-            return 2001;
-        attr_set = true;
-    }
+        return allow(conv_tc_kernel<kRelu, 4, 8>) && allow(conv_tc_kernel<kTies, 4, 8>) &&
+               allow(conv_tc_kernel<kGeneral, 4, 8>) && allow(conv_tc_kernel<kRelu, 8, 8>) &&
+               allow(conv_tc_kernel<kTies, 8, 8>) && allow(conv_tc_kernel<kGeneral, 8, 8>) &&
+               allow(conv_tc_kernel<kRelu, 4, 16>) && allow(conv_tc_kernel<kTies, 4, 16>) &&
+               allow(conv_tc_kernel<kGeneral, 4, 16>);
+    });
+    if (!attrs) return 2001;
     ConvTc *c = new ConvTc();
+    c->sm_count = current_sm_count();
     Params &p = c->p;
     p.w = static_cast<const int8_t *>(dw);
     p.epi = static_cast<const EpiChan *>(de);
@@ -1050,7 +1055,7 @@ int conv_tc_launch(const ConvTc &c, const int8_t *x, int8_t *y, const ConvGeom &
     // CTAs per N tile: floor, so that all n_tiles * per_tile CTAs are resident at once (one per SM).
     // Rounding up would start the extra CTAs only after a first wave had finished, and the static
     // tile schedule would make them run a full share of tiles on their own.
-    int per_tile = g_sm_count / c.n_tiles;
+    int per_tile = c.sm_count / c.n_tiles;
     if (per_tile < 1) per_tile = 1;
     if (per_tile > m_tiles) per_tile = m_tiles;
     dim3 grid(per_tile, c.n_tiles);
