@@ -194,10 +194,16 @@ def test_softmax_exact(ops, ref, dev, native):
     x = seeded(nbytes, 4)
     y_ref = np.empty(nbytes, dtype=np.int8)
     ref.uq_softmax_exact(x.ctypes.data, y_ref.ctypes.data, nbytes, q.ctypes.data)
-    dy = dev.empty(nbytes)
-    ops.uq_softmax_exact(dev.put(x), dy, nbytes, dev.put(q))
+    dy, dx, dq = dev.empty(nbytes), dev.put(x), dev.put(q)
+    np.testing.assert_array_equal(dev.get(dx, nbytes), x)  # the device copies hold what was put
+    np.testing.assert_array_equal(dev.get(dq, q.nbytes, np.int32), q)
+    ops.uq_softmax_exact(dx, dy, nbytes, dq)
     assert ops.uq_status() == 0, ops.ug_last_error()
     got = dev.get(dy, nbytes)
+    dy2 = dev.empty(nbytes)
+    ops.uq_softmax_exact(dx, dy2, nbytes, dq)
+    again = dev.get(dy2, nbytes)
+    assert np.array_equal(got, again), "two calls on the same device buffers differ"
     # the same rows through the graph path (one plan image per 1000 bytes)
     from gpuhelp import NativeSession
     with NativeSession(native, plan.blob) as s:

@@ -269,30 +269,27 @@ __global__ void __launch_bounds__((2 + kTapsEW) * 32, 1) conv_taps_kernel(const 
             const int32_t *cr = (rmask | cmask) && valid ? p.corr + (size_t)((rmask << p.kw) | cmask) * p.oc + n0 : nullptr;
             int8_t *dst = p.y + (((size_t)img * p.oh + oy) * p.ow + ox) * p.oc + n0;
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.bn);
-            auto chunk = [&](uint32_t(&r)[16], int ci) {
-                if (!valid) return;
-                if (cr) {
-#pragma unroll
-                    for (int i = 0; i < 16; i++) r[i] = (uint32_t)((int32_t)r[i] + __ldg(cr + ci * 16 + i));
-                }
-                const uint4 v = epilogue_chunk<EPI>(r, E, lut, ci * 16, p.lo, p.hi);
-                *reinterpret_cast<uint4 *>(dst + ci * 16) = v;
-            };
             uint32_t ra[16], rb[16];
-            if (part < live_chunks) {  // chunks part, part + nparts, ... in two buffers in turn
-                tmem_ld16_nowait(taddr + part * 16, ra);
+            int ci = part;
+            if (ci < live_chunks) {
+                tmem_ld16_nowait(taddr + ci * 16, ra);
                 tmem_wait_ld(ra);
             }
-            for (int ci = part; ci < live_chunks; ci += 2 * nparts) {
-                const int nb = ci + nparts, na = ci + 2 * nparts;
-                if (nb < live_chunks) tmem_ld16_nowait(taddr + nb * 16, rb);
-                chunk(ra, ci);
-                if (nb < live_chunks) {
-                    tmem_wait_ld(rb);
-                    if (na < live_chunks) tmem_ld16_nowait(taddr + na * 16, ra);
-                    chunk(rb, nb);
-                    if (na < live_chunks) tmem_wait_ld(ra);
+            while (ci < live_chunks) {
+                const int next = ci + nparts;
+                if (next < live_chunks) tmem_ld16_nowait(taddr + next * 16, rb);
+                if (valid) {
+                    if (cr) {
+#pragma unroll
+                        for (int i = 0; i < 16; i++) ra[i] = (uint32_t)((int32_t)ra[i] + __ldg(cr + ci * 16 + i));
+                    }
+                    const uint4 v = epilogue_chunk<EPI>(ra, E, lut, ci * 16, p.lo, p.hi);
+                    *reinterpret_cast<uint4 *>(dst + ci * 16) = v;
                 }
+                if (next < live_chunks) tmem_wait_ld(rb);
+#pragma unroll
+                for (int q = 0; q < 16; q++) ra[q] = rb[q];
+                ci = next;
             }
             tc_fence_before();
             __syncwarp();

@@ -643,36 +643,28 @@ __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(con
                 if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
                 __syncwarp();
                 const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.bn + c0);
-                auto chunk = [&](const uint32_t(&r)[16], int ci) {
+                uint32_t ra[16], rb[16];
+                if (my_chunks > 0) {
+                    tmem_ld16_nowait(taddr, ra);
+                    tmem_wait_ld(ra);
+                }
+                for (int ci = 0; ci < my_chunks; ci++) {
+                    const bool more = ci + 1 < my_chunks;
+                    if (more) tmem_ld16_nowait(taddr + (ci + 1) * 16, rb);
                     uint4 v;
                     if (p.res) {
                         const int row = mt * kBM + quarter * 32 + lane;
                         uint4 rr = make_uint4(0, 0, 0, 0);  // rows past M read no residual (never stored)
                         if (row < p.M)
                             rr = __ldg(reinterpret_cast<const uint4 *>(p.res + (size_t)row * p.oc + n0 + c0 + ci * 16));
-                        v = epilogue_chunk<EPI>(r, E, lut, c0 + ci * 16, p.lo, p.hi, &p.add, sAdd, rr);
+                        v = epilogue_chunk<EPI>(ra, E, lut, c0 + ci * 16, p.lo, p.hi, &p.add, sAdd, rr);
                     } else {
-                        v = epilogue_chunk<EPI>(r, E, lut, c0 + ci * 16, p.lo, p.hi);
+                        v = epilogue_chunk<EPI>(ra, E, lut, c0 + ci * 16, p.lo, p.hi);
                     }
                     st_shared16(smem_u32(stage + (size_t)lane * p.box + ((ci ^ swz_row) << 4)), v);
-                };
-                // two register buffers in turn: chunk ci + 1 loads from TMEM while chunk ci is
-                // requantised, and no register copies between them
-                uint32_t ra[16], rb[16];
-                if (my_chunks > 0) {
-                    tmem_ld16_nowait(taddr, ra);
-                    tmem_wait_ld(ra);
-                }
-                for (int ci = 0; ci < my_chunks; ci += 2) {
-                    const bool has_b = ci + 1 < my_chunks, has_a = ci + 2 < my_chunks;
-                    if (has_b) tmem_ld16_nowait(taddr + (ci + 1) * 16, rb);
-                    chunk(ra, ci);
-                    if (has_b) {
-                        tmem_wait_ld(rb);
-                        if (has_a) tmem_ld16_nowait(taddr + (ci + 2) * 16, ra);
-                        chunk(rb, ci + 1);
-                        if (has_a) tmem_wait_ld(ra);
-                    }
+                    if (more) tmem_wait_ld(rb);
+#pragma unroll
+                    for (int q = 0; q < 16; q++) ra[q] = rb[q];
                 }
                 tc_fence_before();
                 fence_proxy_async();  // staged bytes visible to the TMA (async proxy)
@@ -697,25 +689,21 @@ __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(con
                 tc_fence_after();
                 uint8_t *stage = sOut + (size_t)(lt & 1) * out_stride(p.bn);
                 const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.bn);
-                auto chunk = [&](const uint32_t(&r)[16], int ci) {
-                    const uint4 v = epilogue_chunk<EPI>(r, E, lut, ci * 16, p.lo, p.hi);
-                    st_shared16(smem_u32(stage + (size_t)row * (p.bn + 16) + ci * 16), v);
-                };
                 uint32_t ra[16], rb[16];
-                if (half < live_chunks) {  // chunks half, half + kParts, ... in two buffers in turn
-                    tmem_ld16_nowait(taddr + half * 16, ra);
+                int ci = half;  // chunks half, half + kParts, ...
+                if (ci < live_chunks) {
+                    tmem_ld16_nowait(taddr + ci * 16, ra);
                     tmem_wait_ld(ra);
                 }
-                for (int ci = half; ci < live_chunks; ci += 2 * kParts) {
-                    const int nb = ci + kParts, na = ci + 2 * kParts;
-                    if (nb < live_chunks) tmem_ld16_nowait(taddr + nb * 16, rb);
-                    chunk(ra, ci);
-                    if (nb < live_chunks) {
-                        tmem_wait_ld(rb);
-                        if (na < live_chunks) tmem_ld16_nowait(taddr + na * 16, ra);
-                        chunk(rb, nb);
-                        if (na < live_chunks) tmem_wait_ld(ra);
-                    }
+                while (ci < live_chunks) {
+                    const int next = ci + kParts;
+                    if (next < live_chunks) tmem_ld16_nowait(taddr + next * 16, rb);
+                    const uint4 v = epilogue_chunk<EPI>(ra, E, lut, ci * 16, p.lo, p.hi);
+                    st_shared16(smem_u32(stage + (size_t)row * (p.bn + 16) + ci * 16), v);
+                    if (next < live_chunks) tmem_wait_ld(rb);
+#pragma unroll
+                    for (int q = 0; q < 16; q++) ra[q] = rb[q];
+                    ci = next;
                 }
                 tc_fence_before();
                 __syncwarp();
