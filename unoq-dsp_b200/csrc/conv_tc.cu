@@ -83,6 +83,7 @@ struct Params {
     CUtensorMap ymap;          // output [M rows][oc] int8, box {min(bn,128), 128}, swizzled (TMA store)
     CUtensorMap xmap;          // pointwise input [M rows][ic] int8, box {128, 128}, SWIZZLE_128B (a_tma)
     int a_tma;                 // pointwise A tiles by TMA (one thread) instead of cp.async
+    int withhold;              // failure-detection tests only: CTA (0, 0) never signals its first accumulator
     const int8_t *x;
     int8_t *y;
     const int8_t *w;           // [n_tiles][kc][BN x 128] swizzled
@@ -562,7 +563,9 @@ __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(con
                     mma_commit(smem_u32(empty + s));
                 }
                 if (!ok) break;
-                mma_commit(smem_u32(tfull + acc));
+                // p.withhold (tests of the bounded waits): the epilogue of this CTA's first tile is
+                // never released, so its wait runs out and every role leaves by its abort path
+                if (!(p.withhold && lt == 0 && blockIdx.x == 0 && blockIdx.y == 0)) mma_commit(smem_u32(tfull + acc));
             }
             // Drain: every MMA this thread issued has completed before TMEM can be freed,
             // including on the abort path.
@@ -980,6 +983,10 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
         // pointwise A tiles by TMA unless switched off (UNOQ_CONV_TC_ATMA=0: per-thread cp.async)
         const char *ea = std::getenv("UNOQ_CONV_TC_ATMA");
         p.a_tma = mode == kPointwise && !(ea && ea[0] == '0');
+        // test-only fault injection for the bounded device waits (UNOQ_FAULT_WITHHOLD_COMMIT=1): the
+        // launch then takes about 2 s, records a timeout and the run returns 2003
+        const char *fw = std::getenv("UNOQ_FAULT_WITHHOLD_COMMIT");
+        p.withhold = fw && fw[0] == '1';
     }
     p.band_bytes = mode == kBand ? (int)bg.bytes() : 0;
     p.nbands = nbands;
