@@ -62,7 +62,10 @@ UG_API int ug_profile(uint32_t command, void *out, uint32_t bytes);
 /* ---- Session ABI: replaces runtime/bridge.c (libuno_backend.so exports). -------------- */
 
 /* Replaces ug_open_mode (runtime/bridge.c:99-125). One active session per process (1001).
- * pipeline 0 = blocking, 1 = "mailbox" (accepted for compatibility; both are stream-ordered). */
+ * pipeline 0 = blocking calls; 1 = "mailbox" (bridge.c:161-184): ug_infer then runs one resident
+ * CUDA graph per call -- pinned input slot in, the network, pinned output slot out -- and waits
+ * for it at most 4 s (1006, as the reference's mailbox response). ug_snapshot_tensor is refused
+ * (1003) in mailbox mode, as in the reference; profiling runs take the ordinary path. */
 UG_API void *ug_open_mode(const void *plan, uint32_t bytes, int pipeline, int *error);
 /* Replaces ug_open (runtime/bridge.c:126). */
 UG_API void *ug_open(const void *plan, uint32_t bytes, int *error);

@@ -127,6 +127,7 @@ int ug_infer(void *session, const void *input, uint32_t input_bytes, void *outpu
     Session *s = static_cast<Session *>(session);
     if (!s || !input || !output || input_bytes != s->engine.input_bytes() || output_bytes != s->engine.output_bytes())
         return 1003;  // bridge.c:149
+    if (s->pipeline) return s->engine.run_mailbox(input, output);  // bridge.c:161-184
     return s->engine.run_host(input, output, 1);
 }
 

@@ -398,7 +398,10 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
     const int box = bn / (ew / 4);
     const int span = o + s * g.ic * (G - 1) + g.kw * g.ic;
     const int out_bytes = (int)(2 * ew * rows_warp_stage(box));
-    int stages = 4;
+    // as many A stages as shared memory holds (up to 12): a tile takes kh * atoms of them, and the
+    // loads in flight are what hides their latency (4 stages left a 3x3 stride-2 32-channel layer,
+    // 6 stages per tile, waiting on its loads)
+    int stages = 12;
     while (stages > 2 && RowsLayout(stages, g.kh * atoms, bn, g.oc, out_bytes).total > (size_t)kRowsMaxSmem) stages--;
     const RowsLayout L(stages, g.kh * atoms, bn, g.oc, out_bytes);
     if (L.total > (size_t)kRowsMaxSmem) return 0;

@@ -2,10 +2,12 @@
 #include "engine.hpp"
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstring>
 #include <mutex>
 #include <numeric>
+#include <thread>
 
 #include "conv_rows.cuh"
 #include "conv_taps.cuh"
@@ -41,9 +43,20 @@ const char *last_error() { return g_err.c_str(); }
 
 Engine::~Engine() { release(); }
 
+void Engine::drop_mailbox() {
+    if (mb_exec_) cudaGraphExecDestroy(mb_exec_);
+    if (mb_graph_) cudaGraphDestroy(mb_graph_);
+    if (mb_in_) cudaFreeHost(mb_in_);
+    if (mb_out_) cudaFreeHost(mb_out_);
+    mb_exec_ = nullptr;
+    mb_graph_ = nullptr;
+    mb_in_ = mb_out_ = nullptr;
+}
+
 void Engine::release() {
     if (device_ >= 0 && (d_const_ || stream_)) cudaSetDevice(device_);
     if (stream_) cudaStreamSynchronize(stream_);
+    drop_mailbox();
     gather_.reset();
     for (auto &kv : batches_) {
         BatchCtx &b = *kv.second;
@@ -967,6 +980,67 @@ int Engine::run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint
     return device_status();
 }
 
+int Engine::run_mailbox(const void *in, void *out) {
+    if (!ready_ || !in || !out) return 22;
+    // profiling runs op by op, and a gathered session returns every rank's outputs: both take
+    // the ordinary path
+    if (profiling_ || (gather_ && gather_->active())) return run_host(in, out, 1);
+    UQ_CUDA(cudaSetDevice(device_));
+    const size_t ni = input_bytes(), no = output_bytes();
+    if (!mb_exec_) {
+        BatchCtx *B = nullptr;
+        int rc = batch(1, &B);
+        if (!rc) rc = stage_buffers(*B, false);
+        if (rc) return rc;
+        UQ_CUDA(cudaHostAlloc(&mb_in_, ni, cudaHostAllocDefault));
+        UQ_CUDA(cudaHostAlloc(&mb_out_, no, cudaHostAllocDefault));
+        UQ_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+        cudaMemcpyAsync(landing(*B), mb_in_, ni, cudaMemcpyHostToDevice, stream_);
+        rc = stage_in(*B, stream_);
+        if (!rc) rc = run_steps(*B, stream_, false);
+        cudaMemcpyAsync(mb_out_, B->ptr[P_.h.output], no, cudaMemcpyDeviceToHost, stream_);
+        cudaGraph_t g = nullptr;
+        const cudaError_t e = cudaStreamEndCapture(stream_, &g);
+        if (rc || e != cudaSuccess) {
+            if (g) cudaGraphDestroy(g);
+            drop_mailbox();
+            if (!rc) set_error(std::string("mailbox capture: ") + cudaGetErrorString(e));
+            return rc ? rc : 2001;
+        }
+        mb_graph_ = g;
+        if (cudaGraphInstantiate(&mb_exec_, g, 0) != cudaSuccess) {
+            drop_mailbox();
+            set_error("mailbox graph instantiation failed");
+            return 2001;
+        }
+        last_ctx_ = B;
+    }
+    std::memcpy(mb_in_, in, ni);
+    UQ_CUDA(cudaEventRecord(ev0_, stream_));
+    UQ_CUDA(cudaGraphLaunch(mb_exec_, stream_));
+    UQ_CUDA(cudaEventRecord(ev1_, stream_));
+    // bounded like the reference's mailbox response (bridge.c:172-183): 4 s, then 1006
+    const auto t0 = std::chrono::steady_clock::now();
+    cudaError_t q;
+    while ((q = cudaEventQuery(ev1_)) == cudaErrorNotReady) {
+        if (std::chrono::steady_clock::now() - t0 > std::chrono::seconds(4)) {
+            set_error("mailbox response timed out");
+            return 1006;
+        }
+        std::this_thread::yield();
+    }
+    if (q != cudaSuccess) {
+        set_error(std::string("mailbox run: ") + cudaGetErrorString(q));
+        return 2001;
+    }
+    UQ_CUDA(cudaEventElapsedTime(&last_ms_, ev0_, ev1_));
+    last_images_ = 1;
+    const int rc = device_status();
+    if (rc) return rc;
+    std::memcpy(out, mb_out_, no);
+    return 0;
+}
+
 // Fixed device arena of the allocation-free entry point (ug_run_static): the reference's own
 // arena bound (runtime/graph.h:7). Nothing in it needs to start at zero: every activation is
 // written before it is read, and replicated constants are copied in at every call.
@@ -1153,6 +1227,7 @@ int Engine::set_input_table(const void *table, uint32_t channels) {
     if (!ready_) return 22;
     UQ_CUDA(cudaSetDevice(device_));
     UQ_CUDA(cudaStreamSynchronize(stream_));
+    drop_mailbox();  // its graph lands the input through the old table setting
     if (!table || !channels) {
         table_channels_ = 0;
         return 0;

@@ -91,6 +91,11 @@ class Engine {
 
     // Host buffers; `pinned` skips the staging copy. Synchronous.
     int run_host(const void *in, void *out, uint32_t images);
+    // One image through the session's mailbox (pipeline mode 1, runtime/bridge.c:161-184): a
+    // resident CUDA graph that copies the pinned input slot in, runs the network and copies the
+    // output into the pinned output slot, launched once per call. The wait for it is bounded by
+    // 4 s (1006 on expiry, as the reference's mailbox response). Synchronous.
+    int run_mailbox(const void *in, void *out);
     // One image through the fixed device arena g_static_arena (kStaticArenaBytes), with no device
     // allocation: eager launches on the engine stream, host buffers, synchronous. The first call
     // lays the plan out (host) and looks up the arena's address; calls that overlap on one device
@@ -185,6 +190,11 @@ class Engine {
     std::vector<uint64_t> ticks_;        // [0] runs, [1] total ns, [2+i] op ns
     std::unique_ptr<OutputGather> gather_;
     BatchCtx static_;                    // one-image context over g_static_arena (not owned)
+    // mailbox mode: pinned input / output slots and the graph that runs one image between them
+    uint8_t *mb_in_ = nullptr, *mb_out_ = nullptr;
+    cudaGraph_t mb_graph_ = nullptr;
+    cudaGraphExec_t mb_exec_ = nullptr;
+    void drop_mailbox();
     std::vector<uint32_t> static_replicated_;
     int8_t *d_table_ = nullptr;          // [256][channels] input table (device)
     uint32_t table_channels_ = 0;        // 0: inputs are the int8 input tensor itself

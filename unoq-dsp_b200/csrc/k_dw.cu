@@ -17,6 +17,7 @@
 //    feeds both output rows.
 //  * Epilogue: exact requantisation (requant.cuh constants in registers) and the optional post
 //    table; the bytes are staged NHWC in shared memory and written with 16-byte stores.
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -42,6 +43,7 @@ struct DwParams {
     int tiles_x, tiles_y;
     int ir, pw, plane;      // input rows per tile, words per plane row, words per plane (odd)
     int cb_shift;           // log2(cb)
+    int half_fill;          // fill in 8-channel units (when 16-channel ones would leave threads idle)
     // multiply-shift division (no run-time divide in the per-unit index arithmetic)
     FastDiv f_tx, f_ty, f_pw, f_ir;
 };
@@ -95,8 +97,36 @@ __global__ void __launch_bounds__(512, (K == 3 && S == 1) ? 4 : 3) dw_kernel(con
 
     if (p.post)
         for (int i = threadIdx.x; i < 256; i += blockDim.x) sLut[i] = p.post[i];
-    // ---- fill: unit = (16-channel chunk, input row, 4-column group)
-    {
+    // ---- fill: unit = (16-channel chunk, input row, 4-column group), or 8-channel half chunks when
+    // the tile has too few 16-channel units to occupy the block (every thread then reaches the
+    // barrier after a similar share of the fill)
+    if (p.half_fill) {
+        const uint32_t fillw = 0x01010101u * (uint8_t)p.xzp;
+        const uint2 fill = make_uint2(fillw, fillw);
+        const int units = (cb / 8) * p.ir * p.pw;
+        for (int u = threadIdx.x; u < units; u += blockDim.x) {
+            const int rest = p.f_pw.div(u), wc = u - rest * p.pw;
+            const int chunk = p.f_ir.div(rest), row = rest - chunk * p.ir;
+            const int iy = iy0 + row;
+            uint2 px[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int ix = ix0 + wc * 4 + i;
+                px[i] = fill;
+                if (iy >= 0 && iy < p.ih && ix >= 0 && ix < p.iw)
+                    px[i] = __ldg(reinterpret_cast<const uint2 *>(
+                        p.x + (((size_t)n * p.ih + iy) * p.iw + ix) * p.c + c0 + chunk * 8));
+            }
+            uint32_t *dst = sPlane + (size_t)(chunk * 8) * p.plane + row * p.pw + wc;
+            uint32_t t[4];
+            transpose4(px[0].x, px[1].x, px[2].x, px[3].x, t);
+#pragma unroll
+            for (int k = 0; k < 4; k++) dst[(size_t)k * p.plane] = t[k];
+            transpose4(px[0].y, px[1].y, px[2].y, px[3].y, t);
+#pragma unroll
+            for (int k = 0; k < 4; k++) dst[(size_t)(4 + k) * p.plane] = t[k];
+        }
+    } else {
         const uint32_t fillw = 0x01010101u * (uint8_t)p.xzp;
         const uint4 fill = make_uint4(fillw, fillw, fillw, fillw);
         const int units = (cb / 16) * p.ir * p.pw;
@@ -277,6 +307,10 @@ int dw_prepare(const int8_t *w, const int32_t *q, const uint8_t *post_dev, const
     p.plane = p.ir * p.pw;
     if ((p.plane & 1) == 0) p.plane++;  // odd plane stride: lanes (channels) fall in distinct banks
     d->k = K, d->s = S, d->epi = epi_mode, d->threads = cb * rg, d->tw = tw;
+    {
+        const char *hf = std::getenv("UNOQ_DW_HALF_FILL");  // 0: always 16-channel fill units
+        p.half_fill = !(hf && hf[0] == '0') && 4 * (cb / 16) * p.ir * p.pw < 3 * d->threads;
+    }
     d->smem = 256 + (size_t)cb * p.plane * 4 + (size_t)p.th * tw * cb;
     if (d->smem > 200 * 1024) {
         delete d;

@@ -389,7 +389,15 @@ void uq_softmax_exact(const int8_t *x, int8_t *y, unsigned bytes, const int32_t 
         fail(18, "uq_softmax_exact: row width must be 1..2048 and divide the bytes");
         return;
     }
-    uq::launch_softmax_exact(x, y, bytes / (unsigned)width, width, q, s);
+    // the kernel reads the exponent table through the read-only data path: give it the library's
+    // own copy of the 257 words rather than the caller's buffer
+    void *qcopy = nullptr;
+    if (staging(device, 1, 257 * sizeof(int32_t), &qcopy)) return;
+    if (cudaMemcpyAsync(qcopy, q, 257 * sizeof(int32_t), cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
+        fail(2001, "uq_softmax_exact: table copy");
+        return;
+    }
+    uq::launch_softmax_exact(x, y, bytes / (unsigned)width, width, static_cast<const int32_t *>(qcopy), s);
     finish(s);
 }
 
