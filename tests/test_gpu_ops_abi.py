@@ -210,8 +210,25 @@ def test_softmax_exact(ops, ref, dev, native):
         graph = s.run(x, nbytes // plan.tensors[o.a].bytes)
     rows = sorted(set((np.flatnonzero(got != y_ref) // width).tolist()))
     grows = sorted(set((np.flatnonzero(graph != y_ref) // width).tolist()))
-    assert not rows and not grows, (f"operator ABI rows differing: {rows[:12]}; graph path rows differing: {grows[:12]}; "
-                                    f"row 0 ours {got[:8].tolist()} ref {y_ref[:8].tolist()}")
+    # the operator call on the library's own device buffers (a session's batch buffers)
+    import ctypes as C2
+    with NativeSession(native, plan.blob) as s:
+        images = nbytes // plan.tensors[o.a].bytes
+        din, dout = C2.c_void_p(), C2.c_void_p()
+        assert native.ug_batch_buffers(s.handle, images, C2.byref(din), C2.byref(dout)) == 0
+        assert native.ug_upload_batch(s.handle, x.ctypes.data, images) == 0
+        ops.uq_softmax_exact(din.value, dout.value, nbytes, dq)
+        own = np.empty(nbytes, dtype=np.int8)
+        assert native.ug_download_batch(s.handle, own.ctypes.data, images) == 0
+    orows = sorted(set((np.flatnonzero(own != y_ref) // width).tolist()))
+    detail = ""
+    for r in rows[:2]:
+        sl = slice(r * width, (r + 1) * width)
+        detail += (f" | row {r}: x max {int(x[sl].max())}, ours {got[sl][:10].tolist()} ref {y_ref[sl][:10].tolist()}"
+                   f" own {own[sl][:10].tolist()}")
+    assert not orows, f"on library buffers too: {orows[:12]}{detail}"
+    assert not rows and not grows, (f"operator ABI rows differing: {rows[:12]}; graph path rows differing: {grows[:12]}"
+                                    f"{detail}")
 
 
 @pytest.mark.parametrize("name", ["bmm", "bmm_adj", "bmm_attn_qk", "bmm_attn_v", "bmm_odd_k"])

@@ -65,7 +65,12 @@ struct RowsParams {
     int gstep;
     int view[3], dy[3];    // per kernel row: input view and row offset (view row = oy + dy)
     int stages, lo, hi, box, swz, out_bytes, tmem_cols;
+    int nparts;            // epilogue warps of a lane quarter that share one tile (1, 2 or 4), box = bn / nparts
+    int fold;              // tiles in flight per lane quarter: 4 / nparts (a warp takes every fold-th tile)
+    int n_acc;             // TMEM accumulators in rotation (2..8)
 };
+
+constexpr int kRowsMaxAcc = 8;
 
 struct RowsLayout {
     size_t a, b, out, epi, lut, bars, total;
@@ -82,7 +87,7 @@ struct RowsLayout {
         lut = o;
         o += 256;
         bars = (o + 7) & ~(size_t)7;
-        o = bars + (size_t)(2 * stages + 5) * 8 + 16;
+        o = bars + (size_t)(2 * stages + 2 * kRowsMaxAcc + 1) * 8 + 16;
         total = o + 1024;  // base alignment slack
     }
 };
@@ -106,7 +111,6 @@ constexpr int kRowsEW = 16;
 
 template <int EPI, int CHUNKS>
 __global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const __grid_constant__ RowsParams p) {
-    constexpr int EW = kRowsEW;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int S = p.stages;
@@ -120,8 +124,8 @@ __global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const 
     uint8_t *sLut = smem + L.lut;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
     uint64_t *full = bars, *empty = bars + S;
-    uint64_t *tfull = bars + 2 * S, *tempty = bars + 2 * S + 2, *drain = bars + 2 * S + 4;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 5);
+    uint64_t *tfull = bars + 2 * S, *tempty = bars + 2 * S + kRowsMaxAcc, *drain = bars + 2 * S + 2 * kRowsMaxAcc;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 2 * kRowsMaxAcc + 1);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
@@ -130,9 +134,9 @@ __global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const 
             mbar_init(smem_u32(full + s), 1);
             mbar_init(smem_u32(empty + s), 1);
         }
-        for (int a = 0; a < 2; a++) {
+        for (int a = 0; a < p.n_acc; a++) {
             mbar_init(smem_u32(tfull + a), 1);
-            mbar_init(smem_u32(tempty + a), EW);
+            mbar_init(smem_u32(tempty + a), 4 * p.nparts);  // the warps that take that tile
         }
         mbar_init(smem_u32(drain), 1);
         *abort = 0;
@@ -207,8 +211,8 @@ __global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const 
             bool ok = true;
             int lt = 0;
             for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, lt++) {
-                const int acc = lt & 1;
-                if (!mbar_wait(smem_u32(tempty + acc), (uint32_t)(((lt >> 1) & 1) ^ 1), abort, 202)) break;
+                const int acc = lt % p.n_acc;
+                if (!mbar_wait(smem_u32(tempty + acc), (uint32_t)(((lt / p.n_acc) & 1) ^ 1), abort, 202)) break;
                 tc_fence_after();
                 const uint32_t tmem_d = tmem_base + (uint32_t)(acc * p.bn);
                 for (int kb = 0; kb < p.kh * p.atoms; kb++, it++) {
@@ -241,7 +245,11 @@ __global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const 
         // ------------------------------------------------------------------ epilogue
         const int e = warp - 2;
         const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31 (warp id % 4 rule)
-        const int part = e >> 2;       // column part [part * box, part * box + box) of the tile
+        // The 4 warps of a lane quarter split into fold groups of nparts: a warp takes column part
+        // [part * box, part * box + box) of every fold-th tile, starting with tile ph. On narrow
+        // tiles (nparts 1 or 2) a warp thus covers more columns per tile, and the per-tile fixed
+        // costs (tile indices, masks, waits, store issue) are paid over more outputs.
+        const int part = (e >> 2) % p.nparts, ph = (e >> 2) / p.nparts;
         constexpr int kBox = CHUNKS * 16;
         const int c0 = part * kBox;
         const uint8_t *lut = p.post ? sLut : nullptr;
@@ -257,13 +265,13 @@ __global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const 
         }
         // output columns whose taps all lie inside the image: [ox_lo, ox_hi]
         const int ox_lo = (p.pl + p.s - 1) / p.s, ox_hi = (p.iw - p.kw + p.pl) / p.s;
-        int lt = 0;
-        for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, lt++) {
+        int lt = ph, k = 0;
+        for (int t = blockIdx.x + ph * gridDim.x; t < p.tiles; t += p.fold * gridDim.x, lt += p.fold, k++) {
             const int ig = t / per_group, rem = t - ig * per_group;
             const int rt = rem / p.groups, g = rem - rt * p.groups;
             const int oy0 = rt * p.R, ox0 = g * p.G;
-            const int acc = lt & 1;
-            if (!mbar_wait(smem_u32(tfull + acc), (uint32_t)((lt >> 1) & 1), abort, 204)) break;
+            const int acc = lt % p.n_acc;
+            if (!mbar_wait(smem_u32(tfull + acc), (uint32_t)((lt / p.n_acc) & 1), abort, 204)) break;
             tc_fence_after();
             // TMEM lane m = (image ig * ipt + m / R, row oy0 + m % R). A lane quarter covers rows
             // r0.. of one image when R >= 32, else 32 / R whole images (rows oy0 .. oy0 + R - 1).
@@ -271,7 +279,7 @@ __global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const 
             const int r0 = oy0 + (p.R >= 32 ? m0 % p.R : 0);  // first output row of this warp
             const int img = ig * p.ipt + m0 / p.R;            // first image of this warp
             const bool live = r0 < p.oh;
-            uint8_t *stage = wstage0 + (size_t)(lt & 1) * wsb;
+            uint8_t *stage = wstage0 + (size_t)(k & 1) * wsb;
             // this buffer's previous store (two tiles back) must have been read out
             if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
             __syncwarp();
@@ -395,16 +403,29 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
         }
     if (!G) return 0;
     const int bn = G * g.oc;
-    const int box = bn / (ew / 4);
     const int span = o + s * g.ic * (G - 1) + g.kw * g.ic;
-    const int out_bytes = (int)(2 * ew * rows_warp_stage(box));
-    // as many A stages as shared memory holds (up to 12): a tile takes kh * atoms of them, and the
-    // loads in flight are what hides their latency (4 stages left a 3x3 stride-2 32-channel layer,
-    // 6 stages per tile, waiting on its loads)
-    int stages = 12;
+    // Epilogue split: the fewest warps per tile (nparts of each lane quarter) whose column part is
+    // at most 64 columns and a staging width the swizzle / bank rules take (16 / 32 / 48 / 64); the
+    // other warps of the quarter take the next tiles (fold = 4 / nparts tiles in flight), over a
+    // ring of as many accumulators as TMEM holds (up to 8). UNOQ_CONV_ROWS_FOLD=0 keeps one tile
+    // per quarter (every warp a quarter of the tile's columns).
+    const char *env_fold = std::getenv("UNOQ_CONV_ROWS_FOLD");
+    const bool allow_fold = !(env_fold && env_fold[0] == '0');
+    int nparts = ew / 4, box = bn / nparts, stages = 4, out_bytes = 0;
+    for (int np = allow_fold ? 1 : ew / 4; np <= ew / 4; np *= 2) {
+        const int b = bn / np;
+        if (bn % np || (b != 16 && b != 32 && b != 48 && b != 64)) continue;
+        const int ob = (int)(2 * ew * rows_warp_stage(b));
+        if (RowsLayout(2, g.kh * atoms, bn, g.oc, ob).total > (size_t)kRowsMaxSmem) continue;
+        nparts = np, box = b;
+        break;
+    }
+    out_bytes = (int)(2 * ew * rows_warp_stage(box));
     while (stages > 2 && RowsLayout(stages, g.kh * atoms, bn, g.oc, out_bytes).total > (size_t)kRowsMaxSmem) stages--;
     const RowsLayout L(stages, g.kh * atoms, bn, g.oc, out_bytes);
     if (L.total > (size_t)kRowsMaxSmem) return 0;
+    int n_acc = 2;
+    while (n_acc * 2 <= kRowsMaxAcc && n_acc * 2 * bn <= 512) n_acc *= 2;
 
     // Weights: reference packed layout (gemm.h:9), reduction index t = (ky*kw + kx)*ic + c
     // (tflite.py:155), into the banded B matrix, one SW128 K-major block per (kernel row, atom).
@@ -511,8 +532,11 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
     p.box = box;
     p.swz = box == 128 ? 3 : box == 64 ? 2 : box == 32 ? 1 : 0;
     p.out_bytes = out_bytes;
+    p.nparts = nparts;
+    p.fold = (ew / 4) / nparts;
+    p.n_acc = n_acc;
     int cols = 32;
-    while (cols < 2 * bn) cols *= 2;
+    while (cols < n_acc * bn) cols *= 2;
     p.tmem_cols = cols;
     c->smem = L.total;
     c->epi_mode = epi_mode;

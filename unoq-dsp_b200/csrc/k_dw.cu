@@ -43,7 +43,6 @@ struct DwParams {
     int tiles_x, tiles_y;
     int ir, pw, plane;      // input rows per tile, words per plane row, words per plane (odd)
     int cb_shift;           // log2(cb)
-    int half_fill;          // fill in 8-channel units (when 16-channel ones would leave threads idle)
     // multiply-shift division (no run-time divide in the per-unit index arithmetic)
     FastDiv f_tx, f_ty, f_pw, f_ir;
 };
@@ -97,36 +96,8 @@ __global__ void __launch_bounds__(512, (K == 3 && S == 1) ? 4 : 3) dw_kernel(con
 
     if (p.post)
         for (int i = threadIdx.x; i < 256; i += blockDim.x) sLut[i] = p.post[i];
-    // ---- fill: unit = (16-channel chunk, input row, 4-column group), or 8-channel half chunks when
-    // the tile has too few 16-channel units to occupy the block (every thread then reaches the
-    // barrier after a similar share of the fill)
-    if (p.half_fill) {
-        const uint32_t fillw = 0x01010101u * (uint8_t)p.xzp;
-        const uint2 fill = make_uint2(fillw, fillw);
-        const int units = (cb / 8) * p.ir * p.pw;
-        for (int u = threadIdx.x; u < units; u += blockDim.x) {
-            const int rest = p.f_pw.div(u), wc = u - rest * p.pw;
-            const int chunk = p.f_ir.div(rest), row = rest - chunk * p.ir;
-            const int iy = iy0 + row;
-            uint2 px[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const int ix = ix0 + wc * 4 + i;
-                px[i] = fill;
-                if (iy >= 0 && iy < p.ih && ix >= 0 && ix < p.iw)
-                    px[i] = __ldg(reinterpret_cast<const uint2 *>(
-                        p.x + (((size_t)n * p.ih + iy) * p.iw + ix) * p.c + c0 + chunk * 8));
-            }
-            uint32_t *dst = sPlane + (size_t)(chunk * 8) * p.plane + row * p.pw + wc;
-            uint32_t t[4];
-            transpose4(px[0].x, px[1].x, px[2].x, px[3].x, t);
-#pragma unroll
-            for (int k = 0; k < 4; k++) dst[(size_t)k * p.plane] = t[k];
-            transpose4(px[0].y, px[1].y, px[2].y, px[3].y, t);
-#pragma unroll
-            for (int k = 0; k < 4; k++) dst[(size_t)(4 + k) * p.plane] = t[k];
-        }
-    } else {
+    // ---- fill: unit = (16-channel chunk, input row, 4-column group)
+    {
         const uint32_t fillw = 0x01010101u * (uint8_t)p.xzp;
         const uint4 fill = make_uint4(fillw, fillw, fillw, fillw);
         const int units = (cb / 16) * p.ir * p.pw;
@@ -282,13 +253,22 @@ int dw_prepare(const int8_t *w, const int32_t *q, const uint8_t *post_dev, const
     const int epi_mode = !fast ? 2 : (q[14] >= yzp ? 0 : 1);
     if (epi_mode != 2)
         for (auto &e : epi) e.sh = e.sh >= 32 ? e.sh - 32 : 0;
-    // Tile: 7 or 8 columns; the whole image height when it is at most 32 rows, else 16 rows.
-    const int rg = g.oh <= 32 ? (g.oh + kR - 1) / kR : 8;
+    // Tile: 7 or 8 columns; the whole image height when it is at most 32 rows, else 16 rows
+    // (UNOQ_DW_ROWS=r caps the output rows per tile; a tuning switch, results are unchanged).
+    int rg = g.oh <= 32 ? (g.oh + kR - 1) / kR : 8;
+    if (const char *er = std::getenv("UNOQ_DW_ROWS")) {
+        const int cap = std::atoi(er) / kR;
+        if (cap >= 1 && cap < rg) rg = cap;
+    }
     // tile width: 7 or 8 output columns, whichever leaves fewer computed columns past the image
     const int tw = ((g.ow + 6) / 7 * 7 - g.ow) < ((g.ow + 7) / 8 * 8 - g.ow) ? 7 : 8;
     // channels per block: 32 for stride 1 (smaller blocks, more of them resident: 7-10% faster on
     // the 14x14 and 28x28 layers), 64 for stride 2 (wider halo reuse; 32 was up to 45% slower)
     int cb = S == 1 ? 32 : 64;
+    if (const char *ec = std::getenv(S == 1 ? "UNOQ_DW_CB1" : "UNOQ_DW_CB2")) {  // tuning switch
+        const int v = std::atoi(ec);
+        if (v == 16 || v == 32 || v == 64) cb = v;
+    }
     while (cb > 16 && (C % cb != 0 || cb * rg > 512)) cb /= 2;
     if (C % cb != 0 || cb * rg > 512) return 0;
     DwFast *d = new DwFast();
@@ -307,10 +287,6 @@ int dw_prepare(const int8_t *w, const int32_t *q, const uint8_t *post_dev, const
     p.plane = p.ir * p.pw;
     if ((p.plane & 1) == 0) p.plane++;  // odd plane stride: lanes (channels) fall in distinct banks
     d->k = K, d->s = S, d->epi = epi_mode, d->threads = cb * rg, d->tw = tw;
-    {
-        const char *hf = std::getenv("UNOQ_DW_HALF_FILL");  // 0: always 16-channel fill units
-        p.half_fill = !(hf && hf[0] == '0') && 4 * (cb / 16) * p.ir * p.pw < 3 * d->threads;
-    }
     d->smem = 256 + (size_t)cb * p.plane * 4 + (size_t)p.th * tw * cb;
     if (d->smem > 200 * 1024) {
         delete d;
