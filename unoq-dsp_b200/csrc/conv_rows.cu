@@ -67,7 +67,8 @@ struct RowsParams {
     int stages, lo, hi, box, swz, out_bytes, tmem_cols;
     int nparts;            // epilogue warps of a lane quarter that share one tile (1, 2 or 4), box = bn / nparts
     int fold;              // tiles in flight per lane quarter: 4 / nparts (a warp takes every fold-th tile)
-    int n_acc;             // TMEM accumulators in rotation (2..8)
+    int n_acc;             // TMEM accumulators in rotation (2, 4 or 8)
+    int acc_shift;         // log2(n_acc)
 };
 
 constexpr int kRowsMaxAcc = 8;
@@ -211,8 +212,8 @@ __global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const 
             bool ok = true;
             int lt = 0;
             for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, lt++) {
-                const int acc = lt % p.n_acc;
-                if (!mbar_wait(smem_u32(tempty + acc), (uint32_t)(((lt / p.n_acc) & 1) ^ 1), abort, 202)) break;
+                const int acc = lt & (p.n_acc - 1);
+                if (!mbar_wait(smem_u32(tempty + acc), (uint32_t)(((lt >> p.acc_shift) & 1) ^ 1), abort, 202)) break;
                 tc_fence_after();
                 const uint32_t tmem_d = tmem_base + (uint32_t)(acc * p.bn);
                 for (int kb = 0; kb < p.kh * p.atoms; kb++, it++) {
@@ -270,8 +271,8 @@ __global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const 
             const int ig = t / per_group, rem = t - ig * per_group;
             const int rt = rem / p.groups, g = rem - rt * p.groups;
             const int oy0 = rt * p.R, ox0 = g * p.G;
-            const int acc = lt % p.n_acc;
-            if (!mbar_wait(smem_u32(tfull + acc), (uint32_t)((lt / p.n_acc) & 1), abort, 204)) break;
+            const int acc = lt & (p.n_acc - 1);
+            if (!mbar_wait(smem_u32(tfull + acc), (uint32_t)((lt >> p.acc_shift) & 1), abort, 204)) break;
             tc_fence_after();
             // TMEM lane m = (image ig * ipt + m / R, row oy0 + m % R). A lane quarter covers rows
             // r0.. of one image when R >= 32, else 32 / R whole images (rows oy0 .. oy0 + R - 1).
@@ -535,6 +536,7 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
     p.nparts = nparts;
     p.fold = (ew / 4) / nparts;
     p.n_acc = n_acc;
+    p.acc_shift = n_acc == 8 ? 3 : n_acc == 4 ? 2 : 1;
     int cols = 32;
     while (cols < n_acc * bn) cols *= 2;
     p.tmem_cols = cols;

@@ -168,6 +168,35 @@ __global__ void softmax_exact_kernel(const int8_t *__restrict__ x, int8_t *__res
     }
 }
 
+// Code 28 for the operator ABI (uq_softmax_exact over caller rows): one thread per row, the
+// reference's three passes over the row in order (qnn.c:87-107).
+__global__ void softmax_exact_rows_kernel(const int8_t *__restrict__ x, int8_t *__restrict__ y, size_t rows, int width,
+                                          const int32_t *__restrict__ q) {
+    const int32_t *lut = q + 1;
+    for (size_t row = (size_t)blockIdx.x * blockDim.x + threadIdx.x; row < rows; row += (size_t)gridDim.x * blockDim.x) {
+        const int8_t *xr = x + row * width;
+        int mx = -128;
+        for (int j = 0; j < width; j++) mx = xr[j] > mx ? xr[j] : mx;
+        uint32_t sum = 0;
+        for (int j = 0; j < width; j++) sum += ((uint32_t)lut[mx - xr[j]] + 2048u) >> 12;
+        const unsigned leading = (unsigned)__clz(sum), exponent = 35u - leading;
+        const uint32_t normalized = (sum << leading) - 0x80000000u;
+        const int32_t half = (int32_t)(((uint64_t)normalized + 2147483648ull) >> 1);
+        int32_t rcp = (int32_t)(1515870810u + (uint32_t)dev_scale(half, -1010580540, 0));
+        for (int step = 0; step < 3; step++) {
+            const int32_t err = (int32_t)(536870912u - (uint32_t)dev_scale(half, rcp, 0));
+            rcp = (int32_t)((uint32_t)rcp + (uint32_t)dev_scale(rcp, err, 0) * 4u);
+        }
+        const int64_t doubled = (int64_t)rcp * 2;
+        rcp = doubled > 2147483647ll ? 2147483647 : (int32_t)doubled;
+        for (int j = 0; j < width; j++) {
+            const uint32_t value = (uint32_t)dev_scale(rcp, lut[mx - xr[j]], 0);
+            const unsigned rounded = exponent >= 32 ? 0u : (value + (1u << (exponent - 1))) >> exponent;
+            y[row * width + j] = (int8_t)(rounded > 255 ? 127 : (int)rounded - 128);
+        }
+    }
+}
+
 // ---------------------------------------------------------------- code 18 -------------
 // qnn.c:175-183: y = clamp(scale(TX[x+128] + TB[b+128], m, s) + yzp). Tables staged in
 // shared memory; 16 bytes per thread per step.
@@ -291,6 +320,10 @@ void launch_softmax_table(const int8_t *x, int8_t *y, size_t rows, int width, co
 
 void launch_softmax_exact(const int8_t *x, int8_t *y, size_t rows, int width, const int32_t *q, cudaStream_t s) {
     softmax_exact_kernel<<<grid_for(rows * 32, kThreads), kThreads, 0, s>>>(x, y, rows, width, q);
+}
+
+void launch_softmax_exact_rows(const int8_t *x, int8_t *y, size_t rows, int width, const int32_t *q, cudaStream_t s) {
+    softmax_exact_rows_kernel<<<grid_for(rows, 128), 128, 0, s>>>(x, y, rows, width, q);
 }
 
 void launch_add(const int8_t *x, const int8_t *b, int8_t *y, size_t count, const int32_t *q, cudaStream_t s) {

@@ -36,6 +36,8 @@ void launch_softmax_table(const int8_t *x, int8_t *y, size_t rows, int width, co
                           cudaStream_t s);
 // Code 28: exact fixed-point softmax, q = [width, 256-entry Q31 exp table].
 void launch_softmax_exact(const int8_t *x, int8_t *y, size_t rows, int width, const int32_t *q, cudaStream_t s);
+// The same arithmetic, one thread per row (the operator ABI's uq_softmax_exact).
+void launch_softmax_exact_rows(const int8_t *x, int8_t *y, size_t rows, int width, const int32_t *q, cudaStream_t s);
 // Code 18: residual add through prepared tables; q is the 520-word device parameter block.
 void launch_add(const int8_t *x, const int8_t *b, int8_t *y, size_t count, const int32_t *q, cudaStream_t s);
 // Code 25: equal-shape multiply; q7 = xz, bz, yz, mult, shift, lo, hi (host values).

@@ -397,7 +397,7 @@ void uq_softmax_exact(const int8_t *x, int8_t *y, unsigned bytes, const int32_t 
         fail(2001, "uq_softmax_exact: table copy");
         return;
     }
-    uq::launch_softmax_exact(x, y, bytes / (unsigned)width, width, static_cast<const int32_t *>(qcopy), s);
+    uq::launch_softmax_exact_rows(x, y, bytes / (unsigned)width, width, static_cast<const int32_t *>(qcopy), s);
     finish(s);
 }
 
