@@ -1,6 +1,8 @@
 """Host logic of the multi-GPU path, run as two gloo ranks on CPU: the batch sharding, the
-out-of-band exchange of the collective's id (rank 0 -> all) and the max/sum reductions the bench
-uses for its device times. The NCCL gather itself needs GPUs and is exercised by bench.py --gpus N."""
+out-of-band exchange of the collective's id (rank 0 -> all), the max/sum reductions the bench
+uses for its device times and the gather of every rank's sampled output rows to rank 0 for the
+output check. The NCCL gather of the outputs themselves needs GPUs: bench.py --gpus N checks its
+result against the reference runtime on every run ("verify")."""
 import os
 import socket
 import sys
@@ -26,8 +28,9 @@ def _rank_main(rank, world, port, results):
     try:
         blob = bytes(range(128)) if rank == 0 else None
         got = dist.broadcast_bytes(blob, 128)
+        gathered = dist.gather_object({bench.shard(4096, world, rank)[0]: bytes([rank]) * 3})
         results[rank] = {"id": got, "max": dist.max(10.0 + rank), "sum": dist.sum(1.5 * (rank + 1)),
-                         "shard": bench.shard(4096, world, rank)}
+                         "shard": bench.shard(4096, world, rank), "gathered": gathered}
         dist.barrier()
     finally:
         dist.close()
@@ -44,6 +47,8 @@ def test_two_gloo_ranks_share_the_id_and_reduce_times():
     assert res[0]["max"] == res[1]["max"] == 11.0
     assert res[0]["sum"] == res[1]["sum"] == 4.5
     assert [res[r]["shard"] for r in range(world)] == [(0, 2048), (2048, 2048)]
+    # the bench's output check: every rank's sampled rows reach rank 0, rank-ordered
+    assert res[0]["gathered"] == [{0: b"\0\0\0"}, {2048: b"\1\1\1"}] and res[1]["gathered"] is None
 
 
 def test_shards_cover_the_global_batch_in_order():
