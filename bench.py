@@ -455,6 +455,18 @@ def bench_model(lib, dist, name, global_batch, steps, warmup, peaks, want_roofli
                         for r in range(dist.world) for i in sample_rows(per_gpu)}
             merged = {g: row for part in resident for g, row in part.items()}
             verify = verify_outputs(plan, ni, {"device_resident": merged, "ug_infer_batch": gathered}, dist)
+        gather = None
+        if dist.world > 1:
+            # the one collective alone: every rank's outputs into GPU 0, timed on the device (max
+            # over ranks), the bytes that cross NVLink per step being the other ranks' outputs
+            gms = C.c_float()
+            rc = lib.ug_time_gather(handle, per_gpu, steps, C.byref(gms))
+            if rc:
+                raise RuntimeError(f"ug_time_gather rc={rc}: {lib.ug_last_error()}")
+            t_g = dist.max(gms.value / 1e3) / steps
+            moved = no * per_gpu * (dist.world - 1)
+            gather = {"ms_per_step": round(t_g * 1e3, 4), "bytes_into_gpu0_per_step": moved,
+                      "GB/s": round(moved / t_g / 1e9, 1), "share_of_step": round(t_g / (t_dev / steps), 4)}
         h2d_gbs = pcie_h2d_gbs(ni * per_gpu, dist.local)
         roof = breakdown = None
         if want_roofline:
@@ -469,7 +481,7 @@ def bench_model(lib, dist, name, global_batch, steps, warmup, peaks, want_roofli
                     "pcie_h2d_gbs": h2d_gbs,
                     "h2d_bound_images_per_s": round(h2d_gbs * 1e9 / ni * dist.world, 1) if h2d_gbs else None},
             "clocks": clocks.summary(), "roofline": roof, "breakdown": breakdown, "detect_e2e": detected,
-            "verify": verify,
+            "verify": verify, "gather": gather,
         }
     finally:
         lib.ug_close(handle)
@@ -780,6 +792,7 @@ def main():
         "roofline": roof, "cpu_baseline": cpu, "clocks": res["clocks"], "gpu_launches": launches,
         "per_gpu_batch": res["per_gpu_batch"], "kernel_breakdown": res["breakdown"],
         "int8_peak": {"tops": peaks.get("int8_tops"), "source": peaks.get("int8_source", "2 x measured bf16 (stand-in)")},
+        "gather": res["gather"],
     }
     if configs is not None:
         line["baseline_configs"] = configs
@@ -795,7 +808,8 @@ def main():
             "value": round(yolo["value"], 2), "unit": "images/s", "global_batch": args.yolo_batch,
             "ms_per_step": round(yolo["ms_per_step"], 4), "e2e": yolo["e2e"], "detect_e2e": yolo["detect_e2e"],
             "roofline": yolo["roofline"],
-            "kernels_per_step": yolo["kernels_per_step"], "kernel_breakdown": yolo["breakdown"], "clocks": yolo["clocks"]}
+            "kernels_per_step": yolo["kernels_per_step"], "kernel_breakdown": yolo["breakdown"], "clocks": yolo["clocks"],
+            "gather": yolo["gather"]}
     print(json.dumps(line))
 
 

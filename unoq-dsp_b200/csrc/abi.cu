@@ -185,6 +185,12 @@ int ug_dist_init(void *session, int rank, int world, const void *id, uint32_t by
     return s->engine.dist_init(rank, world, id, bytes);
 }
 
+int ug_time_gather(void *session, uint32_t images, uint32_t iterations, float *milliseconds) {
+    Session *s = static_cast<Session *>(session);
+    if (!s || !images || !iterations || !milliseconds) return 1003;
+    return s->engine.time_gather(images, iterations, milliseconds);
+}
+
 int ug_gather_buffer(void *session, uint32_t images, void **root_device_output) {
     Session *s = static_cast<Session *>(session);
     if (!s || !images) return 1003;

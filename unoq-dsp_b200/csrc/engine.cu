@@ -1345,6 +1345,23 @@ int Engine::dist_init(int rank, int world, const void *id, uint32_t bytes) {
     return 0;
 }
 
+int Engine::time_gather(uint32_t images, uint32_t iterations, float *ms) {
+    if (!ms || !iterations) return 22;
+    if (!gather_ || !gather_->active()) return 22;
+    BatchCtx *B = nullptr;
+    int rc = batch(images, &B);
+    if (rc) return rc;
+    UQ_CUDA(cudaSetDevice(device_));
+    UQ_CUDA(cudaStreamSynchronize(stream_));
+    UQ_CUDA(cudaEventRecord(ev0_, stream_));
+    for (uint32_t i = 0; i < iterations; i++)
+        if ((rc = gather(*B))) return rc;
+    UQ_CUDA(cudaEventRecord(ev1_, stream_));
+    if ((rc = finish(ev1_))) return rc;
+    UQ_CUDA(cudaEventElapsedTime(ms, ev0_, ev1_));
+    return 0;
+}
+
 int Engine::gather_buffer(uint32_t images, void **root) {
     if (!root) return 1003;
     *root = nullptr;

@@ -123,6 +123,9 @@ class Engine {
     // Multi-GPU: join the output gather of a `world`-rank batch-sharded run. From then on every
     // batch launch ends with the gather of this rank's outputs into rank 0's root buffer.
     int dist_init(int rank, int world, const void *id, uint32_t bytes);
+    // Time `iterations` gathers alone of the batch context's outputs (every rank calls it; CUDA
+    // events on the session stream, bounded wait); 22 when no gather has been joined.
+    int time_gather(uint32_t images, uint32_t iterations, float *ms);
     int gather_buffer(uint32_t images, void **root);
     // On-device preparation and decoding (include/unoq_cuda.h). The table maps uploaded pixels to
     // the input tensor before the graph; the decoder turns the output tensor into k records.

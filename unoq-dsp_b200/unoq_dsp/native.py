@@ -65,6 +65,7 @@ _SIGNATURES = {
     "ug_dist_unique_id": (C.c_int, [C.c_void_p, C.c_uint32]),
     "ug_dist_init": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_uint32]),
     "ug_gather_buffer": (C.c_int, [C.c_void_p, C.c_uint32, C.POINTER(C.c_void_p)]),
+    "ug_time_gather": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.POINTER(C.c_float)]),
     "ug_profile_batch": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.POINTER(C.c_uint64), C.c_uint32,
                                    C.POINTER(C.c_float)]),
     "ug_set_input_table": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32]),
