@@ -143,25 +143,6 @@ __global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const 
         *abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    // The first ring of A stages does not depend on the weights or constants copied below: the
-    // thread that initialised the barriers issues those TMA loads now, and the producer warp
-    // continues after them.
-    const int per_group0 = p.row_tiles * p.groups;
-    const int kblocks = p.kh * p.atoms;
-    long long early = 0;
-    if (threadIdx.x == 0) {
-        const long long local = p.tiles > (int)blockIdx.x ? (long long)(p.tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-        early = local * kblocks < S ? local * kblocks : S;
-        for (long long q = 0; q < early; q++) {
-            const int t = blockIdx.x + (int)(q / kblocks) * gridDim.x, kb = (int)(q % kblocks);
-            const int ig = t / per_group0, rem = t - ig * per_group0;
-            const int rt = rem / p.groups, g = rem - rt * p.groups;
-            const int ky = kb / p.atoms, a = kb - ky * p.atoms;
-            mbar_expect_tx(smem_u32(full + (int)q), (uint32_t)kStageBytes);
-            tma_load_3d(smem_u32(sA + (size_t)q * kStageBytes), &p.xmap[p.view[ky]], p.x0 + g * p.gstep + a * kBK,
-                        rt * p.R + p.dy[ky], ig * p.ipt, smem_u32(full + (int)q));
-        }
-    }
     for (int i = threadIdx.x; i < p.oc; i += blockDim.x) {
         const EpiChan c = p.epi[i];
         sK[i] = c.k;
@@ -202,7 +183,6 @@ __global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const 
                 const int rt = rem / p.groups, g = rem - rt * p.groups;
                 const int x = p.x0 + g * p.gstep, oy0 = rt * p.R, img = ig * p.ipt;
                 for (int kb = 0; kb < p.kh * p.atoms; kb++, it++) {  // K block kb: kernel row ky, atom a
-                    if (it < early) continue;  // issued before the weight copy
                     const int ky = kb / p.atoms, a = kb - ky * p.atoms;
                     const int s = (int)(it % S);
                     if (!mbar_wait(smem_u32(empty + s), (uint32_t)(((it / S) & 1) ^ 1), abort, 201)) {

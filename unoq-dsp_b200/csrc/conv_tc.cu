@@ -291,18 +291,6 @@ __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(con
     if (warp < kProducerWarps) {
         // ------------------------------------------------------------------ producers
         const int t = threadIdx.x;  // 0..127
-        // Pointwise A tiles by TMA: the first ring of stages does not depend on the weights, so
-        // producer thread 0 issues those loads before it joins the weight copy below.
-        long long early = 0;
-        if (p.a_tma && t == 0) {
-            const long long local = m_tiles > (int)blockIdx.x ? (long long)(m_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-            early = local * p.kc < S ? local * p.kc : S;
-            for (long long q = 0; q < early; q++) {
-                const int mt = blockIdx.x + (int)(q / p.kc) * gridDim.x, kc = (int)(q % p.kc);
-                mbar_expect_tx(smem_u32(full + (int)q), (uint32_t)kStageBytes);
-                tma_load_2d(smem_u32(sA + (size_t)q * kStageBytes), &p.xmap, kc * kBK, mt * kBM, smem_u32(full + (int)q));
-            }
-        }
         const uint8_t *wsrc = reinterpret_cast<const uint8_t *>(p.w) + (size_t)ntile * b_bytes;
         for (size_t off = (size_t)t * 16; off < b_bytes; off += kProducers * 16) cp_async16(smem_u32(sB + off), wsrc + off);
         cp_async_commit();
@@ -320,7 +308,6 @@ __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(con
                 bool ok = true;
                 for (int mt = blockIdx.x; mt < m_tiles && ok; mt += gridDim.x)
                     for (int kc = 0; kc < p.kc; kc++, it++) {
-                        if (it < early) continue;  // issued before the weight copy
                         const int s = (int)(it % S);
                         if (!mbar_wait(smem_u32(empty + s), (uint32_t)(((it / S) & 1) ^ 1), abort, 111)) {
                             ok = false;
