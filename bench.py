@@ -460,6 +460,7 @@ def bench_model(lib, dist, name, global_batch, steps, warmup, peaks, want_roofli
             # the one collective alone: every rank's outputs into GPU 0, timed on the device (max
             # over ranks), the bytes that cross NVLink per step being the other ranks' outputs
             gms = C.c_float()
+            dist.barrier()  # rank 0 has just run the output check on the host
             rc = lib.ug_time_gather(handle, per_gpu, steps, C.byref(gms))
             if rc:
                 raise RuntimeError(f"ug_time_gather rc={rc}: {lib.ug_last_error()}")

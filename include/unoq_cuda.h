@@ -126,7 +126,8 @@ UG_API int ug_dist_unique_id(void *id, uint32_t bytes);
  * (world x images outputs, rank-major) in `output`, and returns nothing on the other ranks. */
 UG_API int ug_dist_init(void *session, int rank, int world, const void *id, uint32_t bytes);
 /* Time `iterations` output gathers alone (no network) of the `images`-image batch on the session
- * stream with CUDA events; every rank calls it together. Writes the elapsed milliseconds. */
+ * stream with CUDA events, after one untimed gather that brings the ranks in step; every rank
+ * calls it together. Writes the elapsed milliseconds. */
 UG_API int ug_time_gather(void *session, uint32_t images, uint32_t iterations, float *milliseconds);
 /* Rank 0's device buffer holding the gathered outputs of `images` per rank (NULL on others). */
 UG_API int ug_gather_buffer(void *session, uint32_t images, void **root_device_output);

@@ -1353,6 +1353,9 @@ int Engine::time_gather(uint32_t images, uint32_t iterations, float *ms) {
     if (rc) return rc;
     UQ_CUDA(cudaSetDevice(device_));
     UQ_CUDA(cudaStreamSynchronize(stream_));
+    // one untimed gather first: it completes only once every rank has joined, so the timed ones
+    // start with the ranks in step rather than measuring a late rank's arrival
+    if ((rc = gather(*B))) return rc;
     UQ_CUDA(cudaEventRecord(ev0_, stream_));
     for (uint32_t i = 0; i < iterations; i++)
         if ((rc = gather(*B))) return rc;
