@@ -29,7 +29,6 @@ namespace uq {
 
 namespace {
 
-constexpr int kR = 2;    // output rows per thread
 
 struct DwParams {
     const int8_t *x;
@@ -72,14 +71,17 @@ __device__ __forceinline__ int32_t requant(int32_t acc, const EpiChan &e, int lo
     return v < lo ? lo : (v > hi ? hi : v);
 }
 
-// Blocks per SM the compiler must fit in registers: 4 for 3x3 stride 1 (14% faster on 14x14x192
-// than 2), 3 elsewhere (4 spills on the 5x5 and stride-2 shapes). Each block's fill, compute and
-// store run back to back, so resident blocks are what overlaps one block's loads with another's
-// arithmetic.
+// Blocks per SM the compiler must fit in registers: with 2 output rows per thread, 4 for 3x3
+// stride 1 (14% faster on 14x14x192 than 2), 3 elsewhere (4 spills on the 5x5 and stride-2
+// shapes); with 4 rows per thread, 2 (64 registers). Each block's fill, compute and store run back
+// to back, so resident blocks are what overlaps one block's loads with another's arithmetic.
 // TW = output columns per tile (one thread's row of outputs): 7 or 8, whichever wastes fewer
 // columns of the layer's width (7 for MobileNetV4's 28 / 14 / 7-wide layers).
-template <int K, int S, int EPI, int TW>
-__global__ void __launch_bounds__(512, (K == 3 && S == 1) ? 4 : 3) dw_kernel(const DwParams p) {
+// kR = output rows per thread: 4 for stride-1 layers whose whole image height is one tile (each
+// loaded input row and its windows then feed up to 3-5 outputs per tap row: 15-17% faster on
+// 28x28x64 5x5 and 7x7x512 3x3), else 2 (4 rows was 68% slower on 28x28x192 5x5 stride 2).
+template <int K, int S, int EPI, int TW, int kR>
+__global__ void __launch_bounds__(512, kR == 4 ? 2 : ((K == 3 && S == 1) ? 4 : 3)) dw_kernel(const DwParams p) {
     extern __shared__ __align__(16) uint8_t smem[];
     constexpr int TWIN = (TW - 1) * S + K;       // input columns per tile
     constexpr int NWORD = (TWIN + 3) / 4;         // words per input row
@@ -127,7 +129,7 @@ __global__ void __launch_bounds__(512, (K == 3 && S == 1) ? 4 : 3) dw_kernel(con
         }
     }
 
-    // ---- this thread: channel ch, output rows 2 * rg, 2 * rg + 1 of the tile
+    // ---- this thread: channel ch, output rows kR * rg .. kR * rg + kR - 1 of the tile
     const int ch = threadIdx.x & (cb - 1), rg = threadIdx.x >> p.cb_shift;
     const int c = c0 + ch;
     uint32_t wa[K], wb[K];
@@ -145,7 +147,7 @@ __global__ void __launch_bounds__(512, (K == 3 && S == 1) ? 4 : 3) dw_kernel(con
 #pragma unroll
         for (int j = 0; j < TW; j++) acc[r][j] = 0;
     const uint32_t *plane = sPlane + (size_t)ch * p.plane + (size_t)(rg * kR * S) * p.pw;
-    // input rows used by the thread's two output rows: (kR - 1) * S + K
+    // input rows used by the thread's kR output rows: (kR - 1) * S + K
 #pragma unroll
     for (int ir = 0; ir < (kR - 1) * S + K; ir++) {
         uint32_t wd[NWORD + 1];
@@ -188,39 +190,49 @@ __global__ void __launch_bounds__(512, (K == 3 && S == 1) ? 4 : 3) dw_kernel(con
     }
 }
 
-template <int K, int S, int TW>
+template <int K, int S, int TW, int R>
 void launch_shape(const DwParams &p, int epi, dim3 grid, int threads, size_t smem, cudaStream_t s) {
-    if (epi == 0) dw_kernel<K, S, 0, TW><<<grid, threads, smem, s>>>(p);
-    else if (epi == 1) dw_kernel<K, S, 1, TW><<<grid, threads, smem, s>>>(p);
-    else dw_kernel<K, S, 2, TW><<<grid, threads, smem, s>>>(p);
+    if (epi == 0) dw_kernel<K, S, 0, TW, R><<<grid, threads, smem, s>>>(p);
+    else if (epi == 1) dw_kernel<K, S, 1, TW, R><<<grid, threads, smem, s>>>(p);
+    else dw_kernel<K, S, 2, TW, R><<<grid, threads, smem, s>>>(p);
 }
 
-template <int K, int S, int TW>
+template <int K, int S, int TW, int R>
 bool allow_smem_tw(size_t bytes) {
-    return cudaFuncSetAttribute(dw_kernel<K, S, 0, TW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) ==
+    return cudaFuncSetAttribute(dw_kernel<K, S, 0, TW, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) ==
                cudaSuccess &&
-           cudaFuncSetAttribute(dw_kernel<K, S, 1, TW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) ==
+           cudaFuncSetAttribute(dw_kernel<K, S, 1, TW, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) ==
                cudaSuccess &&
-           cudaFuncSetAttribute(dw_kernel<K, S, 2, TW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) ==
+           cudaFuncSetAttribute(dw_kernel<K, S, 2, TW, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) ==
                cudaSuccess;
 }
 
+// Stride 1 has both row counts per thread; stride 2 only 2.
 template <int K, int S>
 bool allow_smem(size_t bytes) {
-    return allow_smem_tw<K, S, 7>(bytes) && allow_smem_tw<K, S, 8>(bytes);
+    bool ok = allow_smem_tw<K, S, 7, 2>(bytes) && allow_smem_tw<K, S, 8, 2>(bytes);
+    if constexpr (S == 1) ok = ok && allow_smem_tw<K, S, 7, 4>(bytes) && allow_smem_tw<K, S, 8, 4>(bytes);
+    return ok;
 }
 
 template <int K, int S>
-void launch_tw(const DwParams &p, int tw, int epi, dim3 grid, int threads, size_t smem, cudaStream_t s) {
-    if (tw == 7) launch_shape<K, S, 7>(p, epi, grid, threads, smem, s);
-    else launch_shape<K, S, 8>(p, epi, grid, threads, smem, s);
+void launch_tw(const DwParams &p, int tw, int rows, int epi, dim3 grid, int threads, size_t smem, cudaStream_t s) {
+    if constexpr (S == 1) {
+        if (rows == 4) {
+            if (tw == 7) launch_shape<K, S, 7, 4>(p, epi, grid, threads, smem, s);
+            else launch_shape<K, S, 8, 4>(p, epi, grid, threads, smem, s);
+            return;
+        }
+    }
+    if (tw == 7) launch_shape<K, S, 7, 2>(p, epi, grid, threads, smem, s);
+    else launch_shape<K, S, 8, 2>(p, epi, grid, threads, smem, s);
 }
 
 }  // namespace
 
 struct DwFast {
     DwParams p{};
-    int k = 3, s = 1, epi = 0, threads = 0, tw = 8;
+    int k = 3, s = 1, epi = 0, threads = 0, tw = 8, rows = 2;
     size_t smem = 0;
 };
 
@@ -255,7 +267,11 @@ int dw_prepare(const int8_t *w, const int32_t *q, const uint8_t *post_dev, const
         for (auto &e : epi) e.sh = e.sh >= 32 ? e.sh - 32 : 0;
     // Tile: 7 or 8 columns; the whole image height when it is at most 32 rows, else 16 rows
     // (UNOQ_DW_ROWS=r caps the output rows per tile; a tuning switch, results are unchanged).
-    int rg = g.oh <= 32 ? (g.oh + kR - 1) / kR : 8;
+    // Output rows per thread: 4 at stride 1 on whole-image tiles, else 2 (see dw_kernel;
+    // UNOQ_DW_ROWS4=0 keeps 2 everywhere).
+    const char *e4 = std::getenv("UNOQ_DW_ROWS4");
+    const int kR = (S == 1 && g.oh <= 32 && !(e4 && e4[0] == '0')) ? 4 : 2;
+    int rg = g.oh <= 32 ? (g.oh + kR - 1) / kR : 16 / kR;
     if (const char *er = std::getenv("UNOQ_DW_ROWS")) {
         const int cap = std::atoi(er) / kR;
         if (cap >= 1 && cap < rg) rg = cap;
@@ -286,7 +302,7 @@ int dw_prepare(const int8_t *w, const int32_t *q, const uint8_t *post_dev, const
     p.f_ir = FastDiv(p.ir);
     p.plane = p.ir * p.pw;
     if ((p.plane & 1) == 0) p.plane++;  // odd plane stride: lanes (channels) fall in distinct banks
-    d->k = K, d->s = S, d->epi = epi_mode, d->threads = cb * rg, d->tw = tw;
+    d->k = K, d->s = S, d->epi = epi_mode, d->threads = cb * rg, d->tw = tw, d->rows = kR;
     d->smem = 256 + (size_t)cb * p.plane * 4 + (size_t)p.th * tw * cb;
     if (d->smem > 200 * 1024) {
         delete d;
@@ -322,10 +338,10 @@ int dw_launch(const DwFast &d, const int8_t *x, int8_t *y, const ConvGeom &g, cu
     p.y = y;
     p.n = g.n;
     dim3 grid((unsigned)(p.n * p.tiles_y * p.tiles_x), (unsigned)(p.c / p.cb));
-    if (d.k == 3 && d.s == 1) launch_tw<3, 1>(p, d.tw, d.epi, grid, d.threads, d.smem, s);
-    else if (d.k == 3) launch_tw<3, 2>(p, d.tw, d.epi, grid, d.threads, d.smem, s);
-    else if (d.s == 1) launch_tw<5, 1>(p, d.tw, d.epi, grid, d.threads, d.smem, s);
-    else launch_tw<5, 2>(p, d.tw, d.epi, grid, d.threads, d.smem, s);
+    if (d.k == 3 && d.s == 1) launch_tw<3, 1>(p, d.tw, d.rows, d.epi, grid, d.threads, d.smem, s);
+    else if (d.k == 3) launch_tw<3, 2>(p, d.tw, d.rows, d.epi, grid, d.threads, d.smem, s);
+    else if (d.s == 1) launch_tw<5, 1>(p, d.tw, d.rows, d.epi, grid, d.threads, d.smem, s);
+    else launch_tw<5, 2>(p, d.tw, d.rows, d.epi, grid, d.threads, d.smem, s);
     return 0;
 }
 
