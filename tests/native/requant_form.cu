@@ -18,7 +18,7 @@ static uint64_t next() {  // splitmix64
 static int64_t pick(int64_t lo, int64_t hi) { return lo + (int64_t)(next() % (uint64_t)(hi - lo + 1)); }
 
 int main() {
-    long long cases = 0, bad = 0, bad_fast = 0;
+    long long cases = 0, bad = 0, bad_fast = 0, fast_cases = 0;
     const int32_t special_m[] = {0, 1, 2, 3, 1 << 30, (1 << 30) + 1, 0x7FFFFFFF, 0x40000000 - 1, 12345678};
     for (int trial = 0; trial < 40000; trial++) {
         const int shift = (int)pick(-31, 15);
@@ -45,15 +45,19 @@ int main() {
                                     shift, yzp, got, want);
                 bad++;
             }
-            // kRelu fast form: no tie correction when -15 <= s <= -1 and lo >= yzp
-            if (shift <= -1 && shift >= -15 && lo >= yzp) {
+            // short forms (epi_fast): kTies keeps the tie correction; kRelu drops it when lo >= yzp
+            if (uq::epi_fast(e)) {
+                fast_cases++;
                 const long long p = (long long)acc * e.m + e.k;
+                int32_t ties = ((int32_t)((p - ((long long)(acc <= e.cut) << 31)) >> 32)) >> (e.sh - 32);
+                ties = ties < lo ? lo : (ties > hi ? hi : ties);
                 int32_t fast = ((int32_t)(p >> 32)) >> (e.sh - 32);
                 fast = fast < lo ? lo : (fast > hi ? hi : fast);
-                if (fast != want) bad_fast++;
+                if (ties != want || (lo >= yzp && fast != want)) bad_fast++;
             }
         }
     }
-    printf("cases %lld mismatches %lld fast_mismatches %lld\n", cases, bad, bad_fast);
-    return bad || bad_fast ? 1 : 0;
+    printf("cases %lld fast_cases %lld mismatches %lld fast_mismatches %lld\n", cases, fast_cases, bad, bad_fast);
+    // every shift in [-31, -1] and every dead channel must reach the short form at these biases
+    return bad || bad_fast || fast_cases < cases / 2 ? 1 : 0;
 }

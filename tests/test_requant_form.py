@@ -21,4 +21,4 @@ def test_requant_form_matches_reference_scale(tmp_path):
                     f"-Xlinker=-rpath,{lib.parent}", "-o", str(exe)], check=True)
     out = subprocess.run([str(exe)], capture_output=True, text=True)
     assert out.returncode == 0, out.stdout + out.stderr
-    assert "mismatches 0 fast_mismatches 0" in out.stdout
+    assert " mismatches 0 fast_mismatches 0" in out.stdout

@@ -172,6 +172,9 @@ __global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const 
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const int per_group = p.row_tiles * p.groups;  // tiles per group of ipt images
+    // Launched with programmatic serialization: the TMA and epilogue warps wait here for the
+    // previous kernel's activations (the MMA warp touches only shared memory and TMEM).
+    if (warp != 1) grid_dep_wait();
 
     if (warp == 0) {
         // ------------------------------------------------------------------ TMA producer
@@ -235,6 +238,8 @@ __global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const 
                 if (!ok) break;
                 mma_commit(smem_u32(tfull + acc));
             }
+            // all MMAs are issued: the next kernel's CTAs may be scheduled once every CTA is here
+            grid_dep_launch();
             // every MMA issued has completed before TMEM is freed, on the abort path too
             mma_commit(smem_u32(drain));
             const long long start = clock64();
@@ -458,7 +463,7 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
         epi[j] = make_epilogue((long long)cbias[j] + 128ll * sum_all + (long long)xzp * sum_pad, mult[j], shift[j], yzp);
     }
     bool fast = true;
-    for (int j = 0; j < oc; j++) fast &= shift[j] <= -1 && shift[j] >= -15;
+    for (int j = 0; j < oc; j++) fast &= epi_fast(epi[j]);
     const int epi_mode = !fast ? kGeneral : (q[14] >= yzp ? kRelu : kTies);
     if (epi_mode != kGeneral)
         for (auto &e : epi) e.sh = e.sh >= 32 ? e.sh - 32 : 0;  // shift of the high word
@@ -585,9 +590,9 @@ int conv_rows_launch(const ConvRows &c, const int8_t *x, int8_t *y, const ConvGe
     constexpr int T = (2 + kRowsEW) * 32;
     auto go = [&](auto chunks) {
         constexpr int CH = decltype(chunks)::value;
-        if (c.epi_mode == kRelu) conv_rows_kernel<kRelu, CH><<<grid, T, c.smem, s>>>(p);
-        else if (c.epi_mode == kTies) conv_rows_kernel<kTies, CH><<<grid, T, c.smem, s>>>(p);
-        else conv_rows_kernel<kGeneral, CH><<<grid, T, c.smem, s>>>(p);
+        if (c.epi_mode == kRelu) launch_pdl(kPdlConvRows, conv_rows_kernel<kRelu, CH>, grid, T, c.smem, s, p);
+        else if (c.epi_mode == kTies) launch_pdl(kPdlConvRows, conv_rows_kernel<kTies, CH>, grid, T, c.smem, s, p);
+        else launch_pdl(kPdlConvRows, conv_rows_kernel<kGeneral, CH>, grid, T, c.smem, s, p);
     };
     if (c.chunks == 4) go(std::integral_constant<int, 4>{});
     else if (c.chunks == 3) go(std::integral_constant<int, 3>{});

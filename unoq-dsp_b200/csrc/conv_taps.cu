@@ -159,6 +159,9 @@ __global__ void __launch_bounds__((2 + kTapsEW) * 32, 1) conv_taps_kernel(const 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Launched with programmatic serialization: the TMA and epilogue warps wait here for the
+    // previous kernel's activations (the MMA warp touches only shared memory and TMEM).
+    if (warp != 1) grid_dep_wait();
     const int per_image = p.tiles_y * p.tiles_x;
 
     if (warp == 0) {
@@ -225,6 +228,8 @@ __global__ void __launch_bounds__((2 + kTapsEW) * 32, 1) conv_taps_kernel(const 
                 if (!ok) break;
                 mma_commit(smem_u32(tfull + acc));
             }
+            // all MMAs are issued: the next kernel's CTAs may be scheduled once every CTA is here
+            grid_dep_launch();
             // every MMA issued has completed before TMEM is freed, on the abort path too
             mma_commit(smem_u32(drain));
             const long long start = clock64();
@@ -395,7 +400,7 @@ int conv_taps_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
                 make_epilogue((long long)cbias[j] + 128ll * sum_all + (long long)xzp * sum_pad, mult[j], shift[j], yzp);
         }
     bool fast = true;
-    for (int j = 0; j < oc; j++) fast &= shift[j] <= -1 && shift[j] >= -15;
+    for (int j = 0; j < oc; j++) fast &= epi_fast(epi[j]);  // channel j sits at nt * bn + r = j
     const int epi_mode = !fast ? kGeneral : (q[14] >= yzp ? kRelu : kTies);
     if (epi_mode != kGeneral)
         for (auto &e : epi) e.sh = e.sh >= 32 ? e.sh - 32 : 0;  // shift of the high word
@@ -480,9 +485,9 @@ int conv_taps_launch(const ConvTaps &c, const int8_t *x, int8_t *y, const ConvGe
     if (per_tile > p.tiles) per_tile = p.tiles;
     const dim3 grid(per_tile, c.n_tiles);
     constexpr int T = (2 + kTapsEW) * 32;
-    if (c.epi_mode == kRelu) conv_taps_kernel<kRelu><<<grid, T, c.smem, s>>>(p);
-    else if (c.epi_mode == kTies) conv_taps_kernel<kTies><<<grid, T, c.smem, s>>>(p);
-    else conv_taps_kernel<kGeneral><<<grid, T, c.smem, s>>>(p);
+    if (c.epi_mode == kRelu) launch_pdl(kPdlConvTaps, conv_taps_kernel<kRelu>, grid, T, c.smem, s, p);
+    else if (c.epi_mode == kTies) launch_pdl(kPdlConvTaps, conv_taps_kernel<kTies>, grid, T, c.smem, s, p);
+    else launch_pdl(kPdlConvTaps, conv_taps_kernel<kGeneral>, grid, T, c.smem, s, p);
     return 0;
 }
 

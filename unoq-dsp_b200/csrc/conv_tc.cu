@@ -287,6 +287,10 @@ __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(con
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Launched with programmatic serialization: every role but the MMA warp (shared memory and TMEM
+    // only) waits here for the previous kernel's activations -- the producers after their weight
+    // copy, which reads load-time constants.
+    if (warp >= kProducerWarps && warp != kMmaWarp) grid_dep_wait();
 
     if (warp < kProducerWarps) {
         // ------------------------------------------------------------------ producers
@@ -298,6 +302,7 @@ __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(con
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(bfull));
+        grid_dep_wait();
 
         long long it = 0;
         if (p.a_tma) {
@@ -567,6 +572,9 @@ __global__ void __launch_bounds__(Roles<PW, EW>::kThreads, 1) conv_tc_kernel(con
                 // never released, so its wait runs out and every role leaves by its abort path
                 if (!(p.withhold && lt == 0 && blockIdx.x == 0 && blockIdx.y == 0)) mma_commit(smem_u32(tfull + acc));
             }
+            // All MMAs are issued: the next kernel's CTAs may be scheduled once every CTA is here
+            // (earlier, they would sit beside this CTA for its whole run, taking issue slots).
+            grid_dep_launch();
             // Drain: every MMA this thread issued has completed before TMEM can be freed,
             // including on the abort path.
             mma_commit(smem_u32(drain));
@@ -884,9 +892,9 @@ int conv_tc_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *pos
             const long long bias = (long long)cbias[j] + 128ll * sum_all + (long long)xzp * sum_pad;
             epi[(size_t)nt * bn + r] = make_epilogue(bias, mult[j], shift[j], yzp);
         }
-    // Epilogue mode (see EpiMode): the fast forms need every live channel's shift in [-15, -1].
+    // Epilogue mode (see EpiMode): the fast forms need every live channel in the short form.
     bool fast = true;
-    for (int j = 0; j < oc; j++) fast &= shift[j] <= -1 && shift[j] >= -15;
+    for (int j = 0; j < oc; j++) fast &= epi_fast(epi[j]);  // channel j sits at nt * bn + r = j
     const int epi_mode = !fast ? kGeneral : (q[14] >= yzp ? kRelu : kTies);
     if (epi_mode != kGeneral)
         for (auto &e : epi) e.sh = e.sh >= 32 ? e.sh - 32 : 0;  // shift of the high word
@@ -1057,9 +1065,9 @@ int conv_tc_launch(const ConvTc &c, const int8_t *x, int8_t *y, const ConvGeom &
     auto go = [&](auto pw, auto ew) {
         constexpr int PWv = decltype(pw)::value, EWv = decltype(ew)::value;
         constexpr int T = Roles<PWv, EWv>::kThreads;
-        if (p.epi_mode == kRelu) conv_tc_kernel<kRelu, PWv, EWv><<<grid, T, c.smem, s>>>(p);
-        else if (p.epi_mode == kTies) conv_tc_kernel<kTies, PWv, EWv><<<grid, T, c.smem, s>>>(p);
-        else conv_tc_kernel<kGeneral, PWv, EWv><<<grid, T, c.smem, s>>>(p);
+        if (p.epi_mode == kRelu) launch_pdl(kPdlConvTc, conv_tc_kernel<kRelu, PWv, EWv>, grid, T, c.smem, s, p);
+        else if (p.epi_mode == kTies) launch_pdl(kPdlConvTc, conv_tc_kernel<kTies, PWv, EWv>, grid, T, c.smem, s, p);
+        else launch_pdl(kPdlConvTc, conv_tc_kernel<kGeneral, PWv, EWv>, grid, T, c.smem, s, p);
     };
     if (c.producer_warps == 4 && c.epilogue_warps == 16) go(std::integral_constant<int, 4>{}, std::integral_constant<int, 16>{});
     else if (c.producer_warps == 4) go(std::integral_constant<int, 4>{}, std::integral_constant<int, 8>{});

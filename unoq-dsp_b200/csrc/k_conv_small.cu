@@ -249,7 +249,7 @@ int conv_small_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *
             for (int c = 0; c < g.ic; c++)
                 wt[((size_t)j * 9 + tap) * ic4 + c / 4] |= (uint32_t)(uint8_t)wref(j, tap * g.ic + c) << (8 * (c % 4));
         epi[j] = make_epilogue((long long)cbias[j] + 128 * sum_all + (long long)xzp * sum_pad, mult[j], shift[j], yzp);
-        fast &= shift[j] <= -1 && shift[j] >= -15;
+        fast &= epi_fast(epi[j]);
     }
     const int epi_mode = !fast ? 2 : (q[14] >= yzp ? 0 : 1);
     if (epi_mode != 2)

@@ -96,8 +96,12 @@ __global__ void __launch_bounds__(512, kR == 4 ? 2 : ((K == 3 && S == 1) ? 4 : 3
     const int c0 = blockIdx.y * cb;
     const int iy0 = ty * th * S - p.pt, ix0 = tx * TW * S - p.pl;
 
+    // Launched with programmatic serialization: the next kernel may be scheduled once every block
+    // has started; the input is read only after the previous kernel has completed.
+    grid_dep_launch();
     if (p.post)
         for (int i = threadIdx.x; i < 256; i += blockDim.x) sLut[i] = p.post[i];
+    grid_dep_wait();
     // ---- fill: unit = (16-channel chunk, input row, 4-column group)
     {
         const uint32_t fillw = 0x01010101u * (uint8_t)p.xzp;
@@ -192,9 +196,9 @@ __global__ void __launch_bounds__(512, kR == 4 ? 2 : ((K == 3 && S == 1) ? 4 : 3
 
 template <int K, int S, int TW, int R>
 void launch_shape(const DwParams &p, int epi, dim3 grid, int threads, size_t smem, cudaStream_t s) {
-    if (epi == 0) dw_kernel<K, S, 0, TW, R><<<grid, threads, smem, s>>>(p);
-    else if (epi == 1) dw_kernel<K, S, 1, TW, R><<<grid, threads, smem, s>>>(p);
-    else dw_kernel<K, S, 2, TW, R><<<grid, threads, smem, s>>>(p);
+    if (epi == 0) launch_pdl(kPdlDw, dw_kernel<K, S, 0, TW, R>, grid, threads, smem, s, p);
+    else if (epi == 1) launch_pdl(kPdlDw, dw_kernel<K, S, 1, TW, R>, grid, threads, smem, s, p);
+    else launch_pdl(kPdlDw, dw_kernel<K, S, 2, TW, R>, grid, threads, smem, s, p);
 }
 
 template <int K, int S, int TW, int R>
@@ -254,7 +258,7 @@ int dw_prepare(const int8_t *w, const int32_t *q, const uint8_t *post_dev, const
         long long sum = 0;
         for (int t = 0; t < K * K; t++) sum += w[t * C + c];
         epi[c] = make_epilogue((long long)bias[c] + 128 * sum, mult[c], shift[c], yzp);
-        fast &= shift[c] <= -1 && shift[c] >= -15;
+        fast &= epi_fast(epi[c]);
         for (int ky = 0; ky < K; ky++) {
             uint32_t a = 0;
             for (int kx = 0; kx < 4 && kx < K; kx++) a |= (uint32_t)(uint8_t)w[(ky * K + kx) * C + c] << (8 * kx);

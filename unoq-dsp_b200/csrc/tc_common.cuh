@@ -9,6 +9,7 @@
 
 #include <cstdint>
 
+#include "common.cuh"
 #include "requant.cuh"
 
 namespace uq {
@@ -163,11 +164,12 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[16]) {
 
 
 // Epilogue requantisation modes, chosen per layer on the host (all exact, see make_epilogue):
-//   kRelu    every channel has -15 <= shift <= -1 and the clamp floor lo >= yzp, so the tie
+//   kRelu    every channel is in the short form (epi_fast: a negative shift with yzp folded into
+//            k, or a dead channel, m == 0) and the clamp floor lo >= yzp, so the tie
 //            correction for negative high products can never survive the clamp:
 //            y = clamp((hi32(acc*m + k)) >> (sh - 32));
 //   kTies    same shifts, lo < yzp: subtract 2^31 first when acc <= cut;
-//   kGeneral any channel with a pre-shift (shift >= 0) or shift < -15: full form.
+//   kGeneral any live channel with a pre-shift (shift >= 0), or whose k could not take yzp: full form.
 enum EpiMode { kRelu = 0, kTies = 1, kGeneral = 2 };
 
 // Per-channel constants in shared memory as structure-of-arrays so 16 columns load as
