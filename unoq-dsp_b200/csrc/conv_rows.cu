@@ -395,13 +395,21 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
     // resident. Inputs of 33-64 channels only with oc <= 32, where band-mode tiles are narrowest
     // (64 -> 16 channels: 2.2x faster than band mode; 64 -> 64 stride 2: 9% slower)
     const int ew = kRowsEW;
-    const int max_atoms = g.ic <= 32 ? 2 : (g.oc <= 32 ? 4 : 0);
+    const int max_atoms = g.ic <= 32 ? 3 : (g.oc <= 32 ? 4 : 0);
+    // Among the (G, atoms) whose window fits and whose layout fits shared memory with two stages,
+    // the fewest K blocks per output pixel (atoms / G: A bytes loaded and MMA work per output),
+    // then the fewest atoms. 32 -> 32 channels, 3x3 stride 2 thus takes G = 4 over 3 atoms rather
+    // than G = 2 over 2 (UNOQ_CONV_ROWS_ATOMS=2 restores the old two-atom limit).
+    const char *env_atoms = std::getenv("UNOQ_CONV_ROWS_ATOMS");
+    const int atom_cap = env_atoms ? std::atoi(env_atoms) : max_atoms;
     int G = 0, atoms = 0;
-    for (int na = 1; na <= max_atoms && !G; na++)
+    for (int na = 1; na <= max_atoms && na <= atom_cap; na++)
         for (int c = 256 / g.oc; c >= 1; c /= 2) {
+            if (G && na * G >= atoms * c) break;  // not fewer blocks per pixel than the choice so far
             const int b = c * g.oc / (ew / 4);
             if ((s * g.ic * c) % 16 != 0 || (b != 16 && b != 32 && b != 48 && b != 64)) continue;
             if (o + s * g.ic * (c - 1) + g.kw * g.ic > na * kBK) continue;
+            // the narrowest staging the epilogue split allows (nparts = ew / 4)
             const int ob = (int)(2 * ew * rows_warp_stage(b));
             if (RowsLayout(2, g.kh * na, c * g.oc, g.oc, ob).total > (size_t)kRowsMaxSmem) continue;
             G = c, atoms = na;
