@@ -348,6 +348,12 @@ def all_cases(scale=1):
         ("dw5_s1_post", lambda r: conv_post_case(r, (1, 9 * s, 11, 32), 32, (5, 5), (1, 1), depthwise=True)),
         ("dw3_s1_c48_none", lambda r: conv_case(r, (1, 5 * s, 21, 48), 48, (3, 3), (1, 1), depthwise=True,
                                                 act="none")),
+        # tensor-core depthwise shapes: odd 5x5 stride 2 (four phase planes), two whole images per
+        # tile (14x14 stride 2 -> 7x7), 128-channel slices over a 40-wide row (3 rows per tile)
+        ("dw5_s2_c64", lambda r: conv_case(r, (1, 15 * s, 13, 64), 64, (5, 5), (2, 2), depthwise=True)),
+        ("dw3_s2_c128_img2", lambda r: conv_case(r, (1, 14, 14, 128), 128, (3, 3), (2, 2), depthwise=True)),
+        ("dw3_s1_c256_wide", lambda r: conv_case(r, (1, 3 * s, 40, 256), 256, (3, 3), (1, 1), depthwise=True,
+                                                 act="none")),
         ("pool_max5", lambda r: pool_case(r, (1, 10 * s, 10, 16), (5, 5), (1, 1), True)),
         ("pool_avg3_s2", lambda r: pool_case(r, (1, 9 * s, 7, 8), (3, 3), (2, 2), False)),
         ("pool_avg2_valid", lambda r: pool_case(r, (1, 8 * s, 8, 4), (2, 2), (2, 2), False, padding="valid")),

@@ -15,7 +15,7 @@ CSRC = HERE / "csrc"
 LIB = HERE / "lib" / "libunoq_cuda.so"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-SOURCES = ["plan.cpp", "device_state.cpp", "k_simt.cu", "k_bytes.cu", "k_dw.cu", "k_conv_small.cu", "conv_tc.cu", "conv_rows.cu", "conv_taps.cu", "k_decode.cu", "gather.cu", "engine.cu", "abi.cu", "k_gemm.cu", "ops_abi.cu", "k_peak.cu"]
+SOURCES = ["plan.cpp", "device_state.cpp", "k_simt.cu", "k_bytes.cu", "k_dw.cu", "k_conv_small.cu", "conv_tc.cu", "conv_rows.cu", "conv_taps.cu", "dw_tc.cu", "k_decode.cu", "gather.cu", "engine.cu", "abi.cu", "k_gemm.cu", "ops_abi.cu", "k_peak.cu"]
 
 
 def build(debug=False, verbose=False):

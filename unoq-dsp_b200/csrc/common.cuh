@@ -16,17 +16,17 @@ namespace uq {
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-// Kernel families that take programmatic launches: the three tensor-core convolutions, whose
+// Kernel families that take programmatic launches: the tensor-core convolutions, whose
 // prologue (barriers, constants, weights, TMEM) then overlaps the previous kernel's tail (5% faster
 // steps at 512 images per GPU, 1% at 4,096). The depthwise kernel is launched in full stream order
 // (early depthwise blocks measured 1-3% slower), but it still lets the next convolution start once
 // all its blocks are running. UNOQ_PDL=<bits> overrides the set (a tuning and diagnosis switch;
 // results are the same either way).
-enum PdlKind { kPdlConvTc = 1, kPdlConvRows = 2, kPdlConvTaps = 4, kPdlDw = 8 };
+enum PdlKind { kPdlConvTc = 1, kPdlConvRows = 2, kPdlConvTaps = 4, kPdlDw = 8, kPdlDwTc = 16 };
 inline bool pdl_enabled(int kind) {
     static const int mask = [] {
         const char *e = std::getenv("UNOQ_PDL");
-        return e ? std::atoi(e) : (kPdlConvTc | kPdlConvRows | kPdlConvTaps);
+        return e ? std::atoi(e) : (kPdlConvTc | kPdlConvRows | kPdlConvTaps | kPdlDwTc);
     }();
     return (mask & kind) != 0;
 }

@@ -15,6 +15,6 @@ bool once_per_device(int family, const std::function<bool()> &set);
 // Streaming multiprocessors of the current device (148 on B200 when the query fails).
 int current_sm_count();
 
-enum KernelFamily { kFamilyConvTc = 1, kFamilyConvRows = 2, kFamilyConvTaps = 3, kFamilyDecode = 4 };
+enum KernelFamily { kFamilyConvTc = 1, kFamilyConvRows = 2, kFamilyConvTaps = 3, kFamilyDecode = 4, kFamilyDwTc = 5 };
 
 }  // namespace uq

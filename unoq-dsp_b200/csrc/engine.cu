@@ -14,6 +14,7 @@
 #include "conv_small.cuh"
 #include "conv_tc.cuh"
 #include "dw.cuh"
+#include "dw_tc.cuh"
 #include "kernels.cuh"
 
 namespace uq {
@@ -307,10 +308,21 @@ int Engine::prepare() {
                     Requant r{dq + kHead, dq + kHead + g.oc, dq + kHead + 2 * g.oc,
                               o.p[1] ? dconst(o.p[1] - 1) : nullptr, q[13], q[14], q[15]};
                     const int8_t *w = reinterpret_cast<const int8_t *>(dconst(o.b));
-                    DwFast *fast = nullptr;
-                    int rc = dw_prepare(P.s8(o.b), q, r.post, g, [this](size_t n) { return prep_alloc(n); }, &fast);
+                    DwTc *tcd = nullptr;
+                    int rc = dw_tc_prepare(P.s8(o.b), q, r.post, g, [this](size_t n) { return prep_alloc(n); }, &tcd);
                     if (rc) return rc;
-                    if (fast) {
+                    DwFast *fast = nullptr;
+                    if (!tcd) rc = dw_prepare(P.s8(o.b), q, r.post, g, [this](size_t n) { return prep_alloc(n); }, &fast);
+                    if (rc) return rc;
+                    if (tcd) {
+                        std::shared_ptr<DwTc> keep(tcd, dw_tc_free);
+                        st.run = [keep, g, ta, tz](const BatchCtx &B, cudaStream_t s) -> int {
+                            ConvGeom gb = g;
+                            gb.n = g.n * (int)B.images;
+                            return dw_tc_launch(*keep, reinterpret_cast<const int8_t *>(B.ptr[ta]),
+                                                reinterpret_cast<int8_t *>(B.ptr[tz]), gb, s);
+                        };
+                    } else if (fast) {
                         std::shared_ptr<DwFast> keep(fast, dw_free);
                         st.run = [keep, g, ta, tz](const BatchCtx &B, cudaStream_t s) -> int {
                             ConvGeom gb = g;
@@ -1113,6 +1125,7 @@ int Engine::device_status() {
     int code = conv_tc_error(true);
     if (!code) code = conv_rows_error(true);
     if (!code) code = conv_taps_error(true);
+    if (!code) code = dw_tc_error(true);
     if (code) {
         set_error("device wait timed out in the tensor-core conv (site " + std::to_string(code) + ")");
         return 2003;
