@@ -618,7 +618,8 @@ CONV_KERNELS = ("conv_tc_kernel", "conv_rows_kernel", "conv_taps_kernel", "conv_
 def traffic_from_ncu_csv(csv_path, images, step_launches=None):
     """DRAM bytes per image of the conv launches in an ncu launch list (--csv, with the metrics
     dram__bytes_read.sum and dram__bytes_write.sum) of one step at `images` images per launch:
-    the first `step_launches` launches of the list (all when None)."""
+    the first `step_launches` model launches of the list (all when None), after the INT8 peak
+    measurement's launches that bench.py makes first."""
     import csv
     total, launches = 0.0, set()
     with open(csv_path, newline="") as f:
@@ -626,8 +627,10 @@ def traffic_from_ncu_csv(csv_path, images, step_launches=None):
     head = rows[0]
     col = {k: head.index(k) for k in ("ID", "Kernel Name", "Metric Name", "Metric Unit", "Metric Value")}
     scale = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9, "KB": 1024, "MB": 1024 ** 2, "GB": 1024 ** 3}
+    model_ids = sorted({int(r[col["ID"]]) for r in rows[1:] if "int8_mma_peak" not in r[col["Kernel Name"]]})
+    keep = set(model_ids if step_launches is None else model_ids[:step_launches])
     for r in rows[1:]:
-        if step_launches is not None and int(r[col["ID"]]) >= step_launches:
+        if int(r[col["ID"]]) not in keep:
             continue
         if r[col["Metric Name"]] in ("dram__bytes_read.sum", "dram__bytes_write.sum") and \
                 any(k in r[col["Kernel Name"]] for k in CONV_KERNELS):
