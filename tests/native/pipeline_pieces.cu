@@ -18,7 +18,7 @@ static void check(bool ok, const char *what, unsigned images) {
 int main() {
     const unsigned sizes[] = {512, 513, 1000, 2048, 2101, 4096, 65536};
     for (unsigned images : sizes) {
-        for (double g : {1.15, 1.25, 2.7, 3.0}) {
+        for (double g : {uq::kRampedPieces, 1.15, 1.25, 2.7, 3.0}) {
             const std::vector<uint32_t> p = uq::pipeline_pieces(images, g);
             unsigned sum = 0;
             for (uint32_t n : p) sum += n;
@@ -34,7 +34,15 @@ int main() {
               images);
         check(uq::pipeline_growth(false, 2.7, 0.0) == 2.7, "a session alone uses what it learned", images);
         check(uq::pipeline_growth(true, 2.7, 1.5) == 1.5, "UNOQ_PIPE_GROWTH wins", images);
-        std::printf("images %u: %zu pieces, first %u, last %u\n", images, r0.size(), r0.front(), r0.back());
+        // copy-bound calls: the ramped schedule starts and ends on a quarter of its middle size
+        const auto rp = uq::pipeline_pieces(images, uq::kRampedPieces);
+        if (images >= 768) {
+            check(rp.size() >= 5 && rp.front() == rp.back() && rp[1] == rp[rp.size() - 2] && rp.front() < rp[1] &&
+                      rp[1] < rp[2],
+                  "ramped schedule: quarter and half pieces at both ends", images);
+        }
+        std::printf("images %u: %zu pieces, first %u, last %u; ramped %zu pieces, first %u, last %u\n", images,
+                    r0.size(), r0.front(), r0.back(), rp.size(), rp.front(), rp.back());
     }
     if (fails) return 1;
     std::printf("ok\n");

@@ -911,14 +911,16 @@ int Engine::run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint
     // that its upload still fits inside the previous piece's compute while the later, larger pieces
     // run at close to whole-batch efficiency (a 512-image MobileNetV4 graph runs about 17% slower
     // per image than a 4096-image one: tail waves and launch gaps). The growth is the ratio of
-    // compute to upload time per image measured on the previous call's last piece (1.25 at first;
-    // about 1.2 for MobileNetV4, 2.7 for YOLO26n; once the session has joined a multi-GPU output
-    // gather the factor stays at its initial value on every rank, see pipeline_growth). At most
-    // kMaxPieces; a small remainder joins the last piece. UNOQ_PIPE_GROWTH fixes the factor.
+    // compute to upload time per image measured on the previous call's largest piece (1.25 at
+    // first; 2.7 for YOLO26n). A call whose compute is faster than its upload (MobileNetV4: 0.8)
+    // takes the ramped schedule instead (pipeline_pieces). Once the session has joined a multi-GPU
+    // output gather the factor stays at its initial value on every rank (see pipeline_growth). At
+    // most kMaxPieces; a small remainder joins the last piece. UNOQ_PIPE_GROWTH fixes the factor
+    // (below 1: the ramped schedule).
     static const double fixed_growth = [] {
         const char *env = std::getenv("UNOQ_PIPE_GROWTH");
         const double g = env ? std::atof(env) : 0.0;
-        return g >= 1.0 && g <= 4.0 ? g : 0.0;
+        return g > 0.0 && g <= 4.0 ? g : 0.0;
     }();
     const bool joined = gather_ && gather_->active();
     const std::vector<uint32_t> sizes = pipeline_pieces(images, pipeline_growth(joined, pipe_growth_, fixed_growth));
@@ -940,11 +942,14 @@ int Engine::run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint
     UQ_CUDA(cudaStreamWaitEvent(h2d_, ev0_, 0));
     UQ_CUDA(cudaStreamWaitEvent(d2h_, ev0_, 0));
     size_t off = 0;
+    // the upload and compute of the largest piece are timed (a middle piece of a ramped schedule,
+    // the last of a growing one): their ratio picks the next call's schedule
+    const size_t timed_piece = (size_t)(std::max_element(sizes.begin(), sizes.end()) - sizes.begin());
     for (size_t piece = 0; piece < sizes.size(); piece++) {
         const int s = (int)(piece & 1);
         BatchCtx *B = ctx[piece];
         const size_t n = sizes[piece];
-        const bool timed = piece + 1 == sizes.size() && sizes.size() > 1;
+        const bool timed = piece == timed_piece && sizes.size() > 1;
         if (timed) UQ_CUDA(cudaEventRecord(pipe_t_[0], h2d_));
         UQ_CUDA(cudaMemcpyAsync(landing(*B), in + off * ni, n * ni, cudaMemcpyHostToDevice, h2d_));
         UQ_CUDA(cudaEventRecord(pipe_ev_[0][s], h2d_));
@@ -981,13 +986,18 @@ int Engine::run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint
     UQ_CUDA(cudaEventElapsedTime(&last_ms_, ev0_, ev1_));
     last_images_ = images;
     last_ctx_ = ctx.back();
-    // Learn the growth from this process's own timing only while the session has no output gather
-    // (pipeline_growth ignores it afterwards anyway): per-rank timings differ.
+    // Learn the schedule from this process's own timing only while the session has no output
+    // gather (pipeline_growth ignores it afterwards anyway): per-rank timings differ. Compute
+    // faster than upload takes the ramped schedule, else pieces grow by the ratio of compute to
+    // upload time. Entering the ramped schedule needs a 10% margin; staying needs none, because
+    // its middle pieces are smaller and so slower per image than the largest growing piece.
     if (sizes.size() > 1 && !joined) {
         float up = 0.f, comp = 0.f;
         if (cudaEventElapsedTime(&up, pipe_t_[0], pipe_t_[1]) == cudaSuccess &&
-            cudaEventElapsedTime(&comp, pipe_t_[2], pipe_t_[3]) == cudaSuccess && up > 0.f && comp > 0.f)
-            pipe_growth_ = std::min(3.0, std::max(1.15, 1.1 * comp / up));
+            cudaEventElapsedTime(&comp, pipe_t_[2], pipe_t_[3]) == cudaSuccess && up > 0.f && comp > 0.f) {
+            const float margin = pipe_growth_ < 1.0 ? 1.0f : 0.9f;
+            pipe_growth_ = comp < margin * up ? kRampedPieces : std::min(3.0, std::max(1.15, 1.1 * comp / up));
+        }
     }
     return device_status();
 }

@@ -24,13 +24,36 @@ constexpr size_t kStaticArenaBytes = (size_t)16 << 20;  // fixed arena of run_st
 constexpr size_t kNoOffset = ~(size_t)0;
 
 // Piece schedule of a pipelined host batch (Engine::run_pipelined), host-only and pure so that
-// every rank of a gathered run can be shown to cut the same pieces. The first piece is 1/16 of
-// the batch (64 to 256 images); each next one is `growth` times the previous; at most
-// kMaxPieces; a remainder under half a piece joins the last one.
+// every rank of a gathered run can be shown to cut the same pieces.
+//  * growth >= 1 (compute-bound calls): the first piece is 1/16 of the batch (64 to 256 images);
+//    each next one is `growth` times the previous; at most kMaxPieces; a remainder under half a
+//    piece joins the last one.
+//  * growth < 1 (kRampedPieces: copy-bound calls, compute per image below upload per image): middle
+//    pieces of about images / 8 (256 to 1024) between ramps of a quarter and a half of that size at
+//    both ends. The host-to-device copies run back to back either way; the ramps leave only a
+//    quarter piece's upload before the first compute and a quarter piece's compute after the
+//    last upload, where a growing schedule ends on its largest piece.
 constexpr double kInitialPieceGrowth = 1.25;
+constexpr double kRampedPieces = 0.5;
 constexpr size_t kMaxPieces = 16;
 inline std::vector<uint32_t> pipeline_pieces(uint32_t images, double growth) {
     std::vector<uint32_t> sizes;
+    if (growth < 1.0) {
+        uint32_t mid = images / 8 < 256 ? 256 : images / 8 > 1024 ? 1024 : images / 8;
+        const uint32_t q = mid / 4, h = mid / 2;
+        if (images >= 3 * mid) {
+            const uint32_t rest = images - 2 * (q + h);
+            uint32_t m = (rest + mid / 2) / mid;
+            if (m < 1) m = 1;
+            if (m > kMaxPieces - 4) m = (uint32_t)kMaxPieces - 4;
+            sizes = {q, h};
+            for (uint32_t i = 0; i < m; i++) sizes.push_back(rest / m + (i < rest % m ? 1 : 0));
+            sizes.push_back(h);
+            sizes.push_back(q);
+            return sizes;
+        }
+        growth = kInitialPieceGrowth;  // too few images to ramp
+    }
     uint32_t left = images;
     double cur = images / 16.0 < 64.0 ? 64.0 : images / 16.0 > 256.0 ? 256.0 : images / 16.0;
     while (left) {
@@ -42,7 +65,8 @@ inline std::vector<uint32_t> pipeline_pieces(uint32_t images, double growth) {
     }
     return sizes;
 }
-// The growth a call uses. `fixed` (UNOQ_PIPE_GROWTH, 0 when unset) wins. A session that has joined
+// The growth a call uses (below 1: the ramped schedule). `fixed` (UNOQ_PIPE_GROWTH, 0 when unset)
+// wins. A session that has joined
 // an output gather always uses the initial factor: each piece enqueues one gather step, so every
 // rank must cut identical pieces, whatever it measured on calls made before joining or on
 // calls that gather nothing (decoder calls). Otherwise the factor learned from the last call.
@@ -185,7 +209,7 @@ class Engine {
     cudaEvent_t pipe_ev_[3][2] = {};                         // per slot: input landed, computed, output read
     cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
     cudaEvent_t pipe_t_[4] = {};         // timing of the last piece: upload start / end, graph start / end
-    double pipe_growth_ = kInitialPieceGrowth;  // piece growth: compute / upload time per image, from the last call
+    double pipe_growth_ = kInitialPieceGrowth;  // piece schedule from the last call: growth, or kRampedPieces
     float last_ms_ = 0.f;
     uint32_t last_images_ = 0;
     const BatchCtx *last_ctx_ = nullptr; // context of the last run (a batch piece or the static arena)
