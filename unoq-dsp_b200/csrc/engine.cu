@@ -167,6 +167,7 @@ int Engine::prepare() {
     fuse_adds_ = !(fuse_env && fuse_env[0] == '0');
     skip_.assign(P.h.no, 0);
     concat_in_.assign(P.h.no, {});
+    concat_parts_.assign(P.h.no, {});
     lut_src_.assign(P.h.no, LutSrc{});
     const char *bytes_env = std::getenv("UNOQ_FUSE_BYTES");
     if (!(bytes_env && bytes_env[0] == '0')) fuse_byte_ops();
@@ -452,6 +453,10 @@ int Engine::prepare() {
                 break;
             }
             case 22: {
+                if (skip_[i]) {  // applied by the concat that alone reads its output
+                    st.run = nullptr;
+                    break;
+                }
                 const uint8_t *table = dconst(o.b);
                 const unsigned flip = a.type == 3 ? 128u : 0u;
                 if (lut_src_[i].tensor >= 0) {  // slice of the innermost axis + table in one pass
@@ -485,6 +490,32 @@ int Engine::prepare() {
             case 20: {
                 if (skip_[i]) {  // collapsed into the concat that consumes it
                     st.run = nullptr;
+                    break;
+                }
+                if (!concat_parts_[i].empty()) {
+                    const std::vector<ConcatPart> parts = concat_parts_[i];
+                    const std::vector<uint32_t> ins = concat_in_[i].empty() ? std::vector<uint32_t>{o.a, o.b} : concat_in_[i];
+                    size_t rows = 1;
+                    for (unsigned d = 0; d + 1 < z.rank; d++) rows *= z.d[d];
+                    ConcatParts cp{};
+                    cp.count = (int)parts.size();
+                    for (size_t k = 0; k < parts.size(); k++) {
+                        cp.in_w[k] = parts[k].in_w;
+                        cp.off[k] = parts[k].off;
+                        cp.out_w[k] = (uint32_t)(P.ts[ins[k]].bytes / rows);
+                        if (parts[k].lut_op >= 0) {
+                            const Op &l = P.ops[parts[k].lut_op];
+                            cp.table[k] = dconst(l.b);
+                            cp.flip[k] = P.ts[l.a].type == 3 ? 128u : 0u;
+                        }
+                    }
+                    const uint32_t tz = o.out;
+                    st.run = [=](const BatchCtx &B, cudaStream_t s) -> int {
+                        ConcatParts c = cp;
+                        for (size_t k = 0; k < parts.size(); k++) c.src[k] = B.ptr[parts[k].tensor];
+                        launch_concat_parts(c, B.ptr[tz], rows * B.images, s);
+                        return 0;
+                    };
                     break;
                 }
                 if (!concat_in_[i].empty()) {
@@ -656,6 +687,47 @@ void Engine::fuse_byte_ops() {
             skip_[j] = 1;
             death_[pj.a] = std::max(death_[pj.a], (int)i);
         }
+    }
+    // Tables folded into the concats that alone read them (YOLO's C2f blocks: the concat of the
+    // activated halves of a split): the concat reads each table's source and maps its bytes.
+    for (uint32_t i = 0; i < no; i++) {
+        const Op &o = P.ops[i];
+        if (o.code != 20 || skip_[i]) continue;
+        const Tensor &z = P.ts[o.out];
+        if (z.rank < 1 || o.p[0] + 1 != z.rank) continue;
+        const std::vector<uint32_t> list = concat_in_[i].empty() ? std::vector<uint32_t>{o.a, o.b} : concat_in_[i];
+        const size_t rows = rows_of(z);
+        if (rows == 0 || list.size() > 8) continue;
+        bool ok = true;
+        for (uint32_t t : list) ok = ok && rows_of(P.ts[t]) == rows && P.ts[t].bytes % rows == 0;
+        if (!ok) continue;
+        std::vector<ConcatPart> parts;
+        bool any = false;
+        for (uint32_t t : list) {
+            ConcatPart part;
+            part.tensor = t;
+            part.in_w = (uint32_t)(P.ts[t].bytes / rows);
+            const int j = prod[t];
+            if (j >= 0 && P.ops[j].code == 22 && !skip_[j] && uses[t] == 1 && t != P.h.output && !P.ts[t].flags) {
+                const Op &l = P.ops[j];
+                if (lut_src_[j].tensor >= 0 && lut_src_[j].rows == rows) {
+                    part.tensor = (uint32_t)lut_src_[j].tensor;
+                    part.in_w = lut_src_[j].in_w;
+                    part.off = lut_src_[j].off;
+                    part.lut_op = j;
+                } else if (lut_src_[j].tensor < 0 && P.ts[l.a].bytes == P.ts[t].bytes) {
+                    part.tensor = l.a;
+                    part.lut_op = j;
+                }
+                if (part.lut_op >= 0) {
+                    skip_[j] = 1;
+                    death_[part.tensor] = std::max(death_[part.tensor], (int)i);
+                    any = true;
+                }
+            }
+            parts.push_back(part);
+        }
+        if (any) concat_parts_[i] = parts;
     }
 }
 

@@ -198,8 +198,16 @@ class Engine {
         int tensor = -1;                 // the slice's source tensor (-1: not fused)
         uint32_t rows = 0, in_w = 0, off = 0, out_w = 0;
     };
+    // A concat input whose producer is a table op read by nothing else: the concat reads the
+    // table's source (a slice's source in place when the table read a slice) and applies it.
+    struct ConcatPart {
+        uint32_t tensor = 0;             // tensor read
+        uint32_t in_w = 0, off = 0;      // its row width and this part's offset in it (bytes)
+        int lut_op = -1;                 // table op folded into the part (-1: plain copy)
+    };
     std::vector<char> skip_;
     std::vector<std::vector<uint32_t>> concat_in_;
+    std::vector<std::vector<ConcatPart>> concat_parts_;
     std::vector<LutSrc> lut_src_;
     void fuse_byte_ops();
     std::vector<char> fused_;            // op computed inside the previous op's kernel

@@ -123,6 +123,45 @@ __global__ void concat_multi_kernel(const ConcatInputs in, uint8_t *__restrict__
     }
 }
 
+// Concat chain whose parts may read a slice of a wider row and map it through a byte table (the
+// concat absorbed the table ops that only it read).
+template <int V>
+__global__ void concat_parts_kernel(const ConcatParts in, uint8_t *__restrict__ z, uint64_t rows, uint32_t row_units) {
+    using T = typename Unit<V>::T;
+    __shared__ uint8_t tab[8][256];
+    __shared__ const uint8_t *src[8];
+    __shared__ uint32_t units[8], in_w[8], off[8], flip[8];
+    __shared__ int mapped[8];
+    if (threadIdx.x < 8) {
+        const int k = threadIdx.x;
+        const bool live = k < in.count;
+        src[k] = live ? in.src[k] : nullptr;
+        units[k] = live ? in.out_w[k] / V : 0u;
+        in_w[k] = live ? in.in_w[k] : 0u;
+        off[k] = live ? in.off[k] : 0u;
+        flip[k] = live ? in.flip[k] : 0u;
+        mapped[k] = live && in.table[k] != nullptr;
+    }
+    for (int k = 0; k < in.count; k++)
+        if (in.table[k])
+            for (int i = threadIdx.x; i < 256; i += blockDim.x) tab[k][i] = in.table[k][i];
+    __syncthreads();
+    const uint64_t total = rows * row_units;
+    for (uint64_t u = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; u < total; u += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t r = u / row_units;
+        uint32_t c = (uint32_t)(u - r * row_units);
+        int i = 0;
+        while (c >= units[i]) c -= units[i++];
+        T v = *reinterpret_cast<const T *>(src[i] + r * in_w[i] + off[i] + (size_t)c * V);
+        if (mapped[i]) {
+            uint8_t *b = reinterpret_cast<uint8_t *>(&v);
+#pragma unroll
+            for (int k = 0; k < V; k++) b[k] = tab[i][b[k] ^ flip[i]];
+        }
+        reinterpret_cast<T *>(z)[u] = v;
+    }
+}
+
 // Slice of the innermost axis followed by a byte table, in one pass.
 template <int V>
 __global__ void lut_rows_kernel(const uint8_t *__restrict__ x, uint8_t *__restrict__ y, uint64_t rows, uint32_t in_w,
@@ -610,6 +649,19 @@ void launch_concat_multi(const ConcatInputs &in, uint8_t *z, size_t rows, cudaSt
     if (v == 16) concat_multi_kernel<16><<<grid_for(units, kT), kT, 0, s>>>(in, z, rows, (uint32_t)(row / 16));
     else if (v == 4) concat_multi_kernel<4><<<grid_for(units, kT), kT, 0, s>>>(in, z, rows, (uint32_t)(row / 4));
     else concat_multi_kernel<1><<<grid_for(units, kT), kT, 0, s>>>(in, z, rows, (uint32_t)row);
+}
+
+void launch_concat_parts(const ConcatParts &in, uint8_t *z, size_t rows, cudaStream_t s) {
+    uint64_t m = reinterpret_cast<uintptr_t>(z), row = 0;
+    for (int i = 0; i < in.count; i++) {
+        m |= in.out_w[i] | in.in_w[i] | in.off[i] | reinterpret_cast<uintptr_t>(in.src[i]);
+        row += in.out_w[i];
+    }
+    const int v = unit_for(m);
+    const uint64_t units = rows * (row / v);
+    if (v == 16) concat_parts_kernel<16><<<grid_for(units, kT), kT, 0, s>>>(in, z, rows, (uint32_t)(row / 16));
+    else if (v == 4) concat_parts_kernel<4><<<grid_for(units, kT), kT, 0, s>>>(in, z, rows, (uint32_t)(row / 4));
+    else concat_parts_kernel<1><<<grid_for(units, kT), kT, 0, s>>>(in, z, rows, (uint32_t)row);
 }
 
 void launch_lut_rows(const uint8_t *x, uint8_t *y, size_t rows, uint32_t in_w, uint32_t off, uint32_t out_w,

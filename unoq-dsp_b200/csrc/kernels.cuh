@@ -84,6 +84,17 @@ struct ConcatInputs {
     uint32_t width[8];
 };
 void launch_concat_multi(const ConcatInputs &in, uint8_t *z, size_t rows, cudaStream_t s);
+// Code 20 chains whose inputs may be code-22 tables (of slices) read by nothing else: z row r = for
+// each part k in turn, bytes [off_k, off_k + out_w_k) of row r of src_k (rows of in_w_k bytes),
+// mapped through table_k (y = table[x ^ flip]) when it is set.
+struct ConcatParts {
+    int count;
+    const uint8_t *src[8];
+    uint32_t in_w[8], off[8], out_w[8];
+    const uint8_t *table[8];
+    unsigned flip[8];
+};
+void launch_concat_parts(const ConcatParts &in, uint8_t *z, size_t rows, cudaStream_t s);
 // Code 26 (innermost axis) followed by code 22, in one pass: y[r][c] = table[x[r][off + c] ^ flip]
 // for c < out_w, x rows of in_w bytes.
 void launch_lut_rows(const uint8_t *x, uint8_t *y, size_t rows, uint32_t in_w, uint32_t off, uint32_t out_w,
