@@ -282,9 +282,11 @@ int dw_prepare(const int8_t *w, const int32_t *q, const uint8_t *post_dev, const
     }
     // tile width: 7 or 8 output columns, whichever leaves fewer computed columns past the image
     const int tw = ((g.ow + 6) / 7 * 7 - g.ow) < ((g.ow + 7) / 8 * 8 - g.ow) ? 7 : 8;
-    // channels per block: 32 for stride 1 (smaller blocks, more of them resident: 7-10% faster on
-    // the 14x14 and 28x28 layers), 64 for stride 2 (wider halo reuse; 32 was up to 45% slower)
-    int cb = S == 1 ? 32 : 64;
+    // channels per block: 32 for stride 1 on images over 16 rows (smaller blocks, more of them
+    // resident: 16% faster than 64 on 28x28x64 5x5), 64 for stride 1 on smaller images (the whole
+    // image is one tile, and 32-channel blocks of 64 threads pay their set-up too often: 8-9%
+    // faster on 7x7x512 5x5) and for stride 2 (wider halo reuse; 32 was up to 45% slower)
+    int cb = S == 1 && g.oh > 16 ? 32 : 64;
     if (const char *ec = std::getenv(S == 1 ? "UNOQ_DW_CB1" : "UNOQ_DW_CB2")) {  // tuning switch
         const int v = std::atoi(ec);
         if (v == 16 || v == 32 || v == 64) cb = v;
