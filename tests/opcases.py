@@ -330,6 +330,12 @@ def all_cases(scale=1):
         ("conv_taps_ic128_oc320", lambda r: conv_case(r, (1, 5 * s, 6, 128), 320, (3, 3), (1, 1), act="none")),
         ("conv_taps_2x3_post", lambda r: conv_post_case(r, (1, 7 * s, 8, 32), 16, (2, 3), (1, 1))),
         ("conv_ic8_band", lambda r: conv_case(r, (1, 6 * s, 10, 8), 24, (3, 3), (1, 1))),
+        # row GEMM with fewer than 16 output channels: a 16-column epilogue chunk spans 2 or 4
+        # pixels, each with its own border correction
+        ("conv_rows_oc8", lambda r: conv_case(r, (1, 9 * s, 11, 16), 8, (3, 3), (1, 1))),
+        ("conv_rows_oc8_s2", lambda r: conv_case(r, (1, 10 * s, 13, 16), 8, (3, 3), (2, 2))),
+        ("conv_rows_oc4_3x3", lambda r: conv_case(r, (1, 7 * s, 9, 8), 4, (3, 3), (1, 1))),
+        ("conv_rows_oc4_1x1", lambda r: conv_case(r, (1, 6 * s, 10, 16), 4, (1, 1), (1, 1), act="none")),
         ("conv_rgb_odd_width", lambda r: conv_case(r, (1, 9 * s, 13, 3), 16, (3, 3), (2, 2), xq=(0.02, -5))),
         ("conv_ic8_small", lambda r: conv_case(r, (1, 9 * s, 11, 8), 16, (3, 3), (1, 1))),
         ("conv_ic16_small_post", lambda r: conv_post_case(r, (1, 8 * s, 10, 16), 8, (3, 3), (2, 2))),

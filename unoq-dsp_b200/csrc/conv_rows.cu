@@ -55,6 +55,8 @@ struct RowsParams {
     const uint8_t *post;   // 256 bytes or null
     const int32_t *corr;   // [(rowmask << kw) | colmask][oc]: xzp * weights of the taps outside
     int n, ih, iw, ic, oh, ow, oc;
+    int ec;                // epilogue constant entries: oc, or 16 (oc = 4 / 8: entry i is channel i % oc)
+    int loc;               // log2 of the columns of one pixel within a 16-column chunk (oc < 16), else 4
     int kh, kw, s, pt, pl;
     int G, bn;             // output pixels per column group; bn = G * oc
     int groups, row_tiles, tiles;
@@ -110,18 +112,20 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map
 // 16 epilogue warps (4 per TMEM lane quarter), each owning CHUNKS 16-column chunks of a tile.
 constexpr int kRowsEW = 16;
 
-template <int EPI, int CHUNKS>
+// SUB: fewer than 16 output channels, so a 16-column chunk holds several pixels, each with its
+// own border correction (a variant of its own, so that the common path compiles as before).
+template <int EPI, int CHUNKS, bool SUB>
 __global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const __grid_constant__ RowsParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int S = p.stages;
-    const RowsLayout L(S, p.kh * p.atoms, p.bn, p.oc, p.out_bytes);
+    const RowsLayout L(S, p.kh * p.atoms, p.bn, p.ec, p.out_bytes);
     uint8_t *sA = smem + L.a;
     uint8_t *sB = smem + L.b;
     uint8_t *sOut = smem + L.out;
     long long *sK = reinterpret_cast<long long *>(smem + L.epi);
-    int *sI = reinterpret_cast<int *>(sK + p.oc);
-    const EpiSoA E{sK, sI, sI + p.oc, sI + 2 * p.oc, sI + 3 * p.oc, sI + 4 * p.oc, sI + 5 * p.oc};
+    int *sI = reinterpret_cast<int *>(sK + p.ec);
+    const EpiSoA E{sK, sI, sI + p.ec, sI + 2 * p.ec, sI + 3 * p.ec, sI + 4 * p.ec, sI + 5 * p.ec};
     uint8_t *sLut = smem + L.lut;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
     uint64_t *full = bars, *empty = bars + S;
@@ -143,15 +147,15 @@ __global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const 
         *abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    for (int i = threadIdx.x; i < p.oc; i += blockDim.x) {
-        const EpiChan c = p.epi[i];
+    for (int i = threadIdx.x; i < p.ec; i += blockDim.x) {
+        const EpiChan c = p.epi[SUB ? i % p.oc : i];
         sK[i] = c.k;
         sI[i] = c.m;
-        sI[p.oc + i] = c.cut;
-        sI[2 * p.oc + i] = c.sh;
-        sI[3 * p.oc + i] = c.ls;
-        sI[4 * p.oc + i] = c.bs;
-        sI[5 * p.oc + i] = c.zadd;
+        sI[p.ec + i] = c.cut;
+        sI[2 * p.ec + i] = c.sh;
+        sI[3 * p.ec + i] = c.ls;
+        sI[4 * p.ec + i] = c.bs;
+        sI[5 * p.ec + i] = c.zadd;
     }
     if (p.post)
         for (int i = threadIdx.x; i < 256; i += blockDim.x) sLut[i] = p.post[i];
@@ -303,7 +307,27 @@ __global__ void __launch_bounds__((2 + kRowsEW) * 32, 1) conv_rows_kernel(const 
                     uint32_t a[16];
 #pragma unroll
                     for (int i = 0; i < 16; i++) a[i] = rr[i];
-                    if (rmask | (edge_cols ? 1 : 0)) {
+                    if (SUB && (rmask | (edge_cols ? 1 : 0))) {
+                        // the chunk's 16 / oc pixels: each one's correction row, or -1 when all
+                        // its taps lie inside the image
+                        auto crow = [&](int q) {
+                            if (q >= (16 >> p.loc)) return -1;
+                            const int ox = ox0 + jj[ci] + q;
+                            int cmask = 0;
+                            for (int kx = 0; kx < p.kw; kx++) {
+                                const int ix = p.s * ox - p.pl + kx;
+                                cmask |= (ix < 0 || ix >= p.iw) ? 1 << kx : 0;
+                            }
+                            return (rmask | cmask) && ox < p.ow ? ((rmask << p.kw) | cmask) * p.oc + oo[ci] : -1;
+                        };
+                        const int r0c = crow(0), r1c = crow(1), r2c = crow(2), r3c = crow(3);
+#pragma unroll
+                        for (int i = 0; i < 16; i++) {
+                            const int q = i >> p.loc;
+                            const int o = q == 0 ? r0c : q == 1 ? r1c : q == 2 ? r2c : r3c;
+                            if (o >= 0) a[i] = (uint32_t)((int32_t)a[i] + __ldg(p.corr + o + (i & ((1 << p.loc) - 1))));
+                        }
+                    } else if (!SUB && (rmask | (edge_cols ? 1 : 0))) {
                         const int ox = ox0 + jj[ci];
                         int cmask = 0;
                         for (int kx = 0; kx < p.kw; kx++) {
@@ -381,10 +405,11 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
     const int max_ic = env_ic ? std::atoi(env_ic) : 64;
     if (g.ic < 1 || g.ic > max_ic || g.kh < 1 || g.kh > 3 || g.kw < 1 || g.kw > 3 || g.dh != 1 || g.dw != 1) return 0;
     if (g.sw != s || (s != 1 && s != 2)) return 0;
-    if (g.oc % 16 != 0 || g.oc > 256) return 0;
+    if (!((g.oc % 16 == 0 && g.oc <= 256) || g.oc == 8 || g.oc == 4)) return 0;
+    const int ec = g.oc < 16 ? 16 : g.oc;  // epilogue constant entries (see RowsParams::ec)
     if (g.pt < 0 || g.pt >= g.kh || g.pl < 0 || g.pl >= g.kw) return 0;
     const long long row_bytes = (long long)g.iw * g.ic;
-    if (row_bytes % 16 != 0) return 0;  // tensor-map strides are whole 16-byte units
+    if (row_bytes % 16 != 0 || ((long long)g.ow * g.oc) % 16 != 0) return 0;  // tensor-map strides: 16-byte units
     if ((long long)g.ih * row_bytes >= (1ll << 31) || (long long)g.oh * g.ow * g.oc >= (1ll << 31)) return 0;
     // window offset of every group (constant because a group advances by whole 16-byte units)
     const int o = (((-g.pl * g.ic) % 16) + 16) % 16;
@@ -411,7 +436,7 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
             if (o + s * g.ic * (c - 1) + g.kw * g.ic > na * kBK) continue;
             // the narrowest staging the epilogue split allows (nparts = ew / 4)
             const int ob = (int)(2 * ew * rows_warp_stage(b));
-            if (RowsLayout(2, g.kh * na, c * g.oc, g.oc, ob).total > (size_t)kRowsMaxSmem) continue;
+            if (RowsLayout(2, g.kh * na, c * g.oc, ec, ob).total > (size_t)kRowsMaxSmem) continue;
             G = c, atoms = na;
             break;
         }
@@ -430,13 +455,13 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
         const int b = bn / np;
         if (bn % np || (b != 16 && b != 32 && b != 48 && b != 64)) continue;
         const int ob = (int)(2 * ew * rows_warp_stage(b));
-        if (RowsLayout(2, g.kh * atoms, bn, g.oc, ob).total > (size_t)kRowsMaxSmem) continue;
+        if (RowsLayout(2, g.kh * atoms, bn, ec, ob).total > (size_t)kRowsMaxSmem) continue;
         nparts = np, box = b;
         break;
     }
     out_bytes = (int)(2 * ew * rows_warp_stage(box));
-    while (stages > 2 && RowsLayout(stages, g.kh * atoms, bn, g.oc, out_bytes).total > (size_t)kRowsMaxSmem) stages--;
-    const RowsLayout L(stages, g.kh * atoms, bn, g.oc, out_bytes);
+    while (stages > 2 && RowsLayout(stages, g.kh * atoms, bn, ec, out_bytes).total > (size_t)kRowsMaxSmem) stages--;
+    const RowsLayout L(stages, g.kh * atoms, bn, ec, out_bytes);
     if (L.total > (size_t)kRowsMaxSmem) return 0;
     int n_acc = 2;
     while (n_acc * 2 <= kRowsMaxAcc && n_acc * 2 * bn <= 512) n_acc *= 2;
@@ -499,13 +524,16 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
         auto allow = [](auto fn) {
             return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsMaxSmem) == cudaSuccess;
         };
-        return allow(conv_rows_kernel<kRelu, 1>) && allow(conv_rows_kernel<kTies, 1>) &&
-            allow(conv_rows_kernel<kGeneral, 1>) && allow(conv_rows_kernel<kRelu, 2>) &&
-            allow(conv_rows_kernel<kTies, 2>) && allow(conv_rows_kernel<kGeneral, 2>) &&
-            allow(conv_rows_kernel<kRelu, 3>) && allow(conv_rows_kernel<kTies, 3>) &&
-            allow(conv_rows_kernel<kGeneral, 3>) &&
-            allow(conv_rows_kernel<kRelu, 4>) && allow(conv_rows_kernel<kTies, 4>) &&
-            allow(conv_rows_kernel<kGeneral, 4>);
+        auto allow_all = [&](auto sub) {
+            constexpr bool SB = decltype(sub)::value;
+            return allow(conv_rows_kernel<kRelu, 1, SB>) && allow(conv_rows_kernel<kTies, 1, SB>) &&
+                   allow(conv_rows_kernel<kGeneral, 1, SB>) && allow(conv_rows_kernel<kRelu, 2, SB>) &&
+                   allow(conv_rows_kernel<kTies, 2, SB>) && allow(conv_rows_kernel<kGeneral, 2, SB>) &&
+                   allow(conv_rows_kernel<kRelu, 3, SB>) && allow(conv_rows_kernel<kTies, 3, SB>) &&
+                   allow(conv_rows_kernel<kGeneral, 3, SB>) && allow(conv_rows_kernel<kRelu, 4, SB>) &&
+                   allow(conv_rows_kernel<kTies, 4, SB>) && allow(conv_rows_kernel<kGeneral, 4, SB>);
+        };
+        return allow_all(std::false_type{}) && allow_all(std::true_type{});
     });
     if (!attrs) return 2001;
     ConvRows *c = new ConvRows();
@@ -516,6 +544,8 @@ int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *p
     p.corr = static_cast<const int32_t *>(dc);
     p.post = post_dev;
     p.ih = g.ih, p.iw = g.iw, p.ic = g.ic, p.oh = g.oh, p.ow = g.ow, p.oc = g.oc;
+    p.ec = ec;
+    p.loc = g.oc == 4 ? 2 : g.oc == 8 ? 3 : 4;
     p.kh = g.kh, p.kw = g.kw, p.s = s, p.pt = g.pt, p.pl = g.pl;
     p.G = G;
     p.bn = bn;
@@ -598,9 +628,14 @@ int conv_rows_launch(const ConvRows &c, const int8_t *x, int8_t *y, const ConvGe
     constexpr int T = (2 + kRowsEW) * 32;
     auto go = [&](auto chunks) {
         constexpr int CH = decltype(chunks)::value;
-        if (c.epi_mode == kRelu) launch_pdl(kPdlConvRows, conv_rows_kernel<kRelu, CH>, grid, T, c.smem, s, p);
-        else if (c.epi_mode == kTies) launch_pdl(kPdlConvRows, conv_rows_kernel<kTies, CH>, grid, T, c.smem, s, p);
-        else launch_pdl(kPdlConvRows, conv_rows_kernel<kGeneral, CH>, grid, T, c.smem, s, p);
+        auto run = [&](auto sub) {
+            constexpr bool SB = decltype(sub)::value;
+            if (c.epi_mode == kRelu) launch_pdl(kPdlConvRows, conv_rows_kernel<kRelu, CH, SB>, grid, T, c.smem, s, p);
+            else if (c.epi_mode == kTies) launch_pdl(kPdlConvRows, conv_rows_kernel<kTies, CH, SB>, grid, T, c.smem, s, p);
+            else launch_pdl(kPdlConvRows, conv_rows_kernel<kGeneral, CH, SB>, grid, T, c.smem, s, p);
+        };
+        if (p.oc < 16) run(std::true_type{});
+        else run(std::false_type{});
     };
     if (c.chunks == 4) go(std::integral_constant<int, 4>{});
     else if (c.chunks == 3) go(std::integral_constant<int, 3>{});

@@ -14,7 +14,8 @@ struct ConvRows;  // prepared banded weights, epilogue constants and border corr
 
 // Take the conv if it has ic <= 32, or ic <= 64 with oc <= 32 (UNOQ_CONV_ROWS_IC lowers the input
 // bound), a kh x kw <= 3 x 3 kernel
-// with dilation 1, equal strides 1 or 2, oc a multiple of 16 (<= 256) and 16-byte input rows;
+// with dilation 1, equal strides 1 or 2, oc a multiple of 16 (<= 256) or 4 or 8, 16-byte input and
+// output rows;
 // prepare its device data with `alloc`. *out = nullptr when another path should run. Returns 0
 // or 2001.
 int conv_rows_prepare(const int8_t *w_packed, const int32_t *q, const uint8_t *post_dev, const ConvGeom &g,
