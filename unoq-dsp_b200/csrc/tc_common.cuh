@@ -198,8 +198,8 @@ struct AddEpi {
 // Requantise accumulators r[4g..4g+3] (columns c0+4g.. of one row) and pack them as int8: exact
 // scale, clamp to [lo, hi], then the post table (LUT 1: always, 2: when `lut` is set) and the
 // residual add (ADD). HI = false leaves the upper clamp to the saturating pack (hi == 127 without
-// a lookup after it).
-template <int EPI, int LUT, bool ADD, bool HI>
+// a lookup after it), and LO = false the lower one (lo == -128, the same condition).
+template <int EPI, int LUT, bool ADD, bool HI, bool LO>
 __device__ __forceinline__ uint32_t epilogue_group(const uint32_t (&r)[16], int g, const EpiSoA &E, const uint8_t *lut,
                                                    int c0, int lo, int hi, const AddEpi *fp, const int32_t *tabs,
                                                    uint32_t resw) {
@@ -231,7 +231,7 @@ __device__ __forceinline__ uint32_t epilogue_group(const uint32_t (&r)[16], int 
             if (EPI == kTies) p -= (long long)(acc <= cc[i]) << 31;
             v[i] = ((int32_t)(p >> 32)) >> ss[i];
         }
-        v[i] = max(v[i], lo);
+        if (LO || LUT || ADD) v[i] = max(v[i], lo);
         if (HI || LUT || ADD) v[i] = min(v[i], hi);
         if (LUT == 1 || (LUT == 2 && lut)) v[i] = (int8_t)lut[v[i] + 128];
         if (ADD) {  // fused residual add: the add's two tables, then its scale and clamp
@@ -254,17 +254,20 @@ __device__ __forceinline__ uint4 epilogue_chunk(const uint32_t (&r)[16], const E
                                                 uint4 res = make_uint4(0, 0, 0, 0)) {
     const uint32_t resw[4] = {res.x, res.y, res.z, res.w};
     uint32_t o[4];
-#define UQ_EPI_GROUPS(L, A, H)                                                                       \
+#define UQ_EPI_GROUPS(L, A, H, W)                                                                    \
     _Pragma("unroll") for (int g = 0; g < 4; g++) o[g] =                                             \
-        epilogue_group<EPI, L, A, H>(r, g, E, lut, c0, lo, hi, fp, tabs, resw[g])
+        epilogue_group<EPI, L, A, H, W>(r, g, E, lut, c0, lo, hi, fp, tabs, resw[g])
     if (fp) {
-        UQ_EPI_GROUPS(2, true, true);
+        UQ_EPI_GROUPS(2, true, true, true);
     } else if (lut) {
-        UQ_EPI_GROUPS(1, false, true);
+        UQ_EPI_GROUPS(1, false, true, true);
     } else if (hi < 127) {
-        UQ_EPI_GROUPS(0, false, true);
+        if (lo > -128) UQ_EPI_GROUPS(0, false, true, true);
+        else UQ_EPI_GROUPS(0, false, true, false);
+    } else if (lo > -128) {
+        UQ_EPI_GROUPS(0, false, false, true);
     } else {
-        UQ_EPI_GROUPS(0, false, false);
+        UQ_EPI_GROUPS(0, false, false, false);
     }
 #undef UQ_EPI_GROUPS
     return make_uint4(o[0], o[1], o[2], o[3]);
