@@ -984,18 +984,20 @@ int Engine::run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint
     // run at close to whole-batch efficiency (a 512-image MobileNetV4 graph runs about 17% slower
     // per image than a 4096-image one: tail waves and launch gaps). The growth is the ratio of
     // compute to upload time per image measured on the previous call's largest piece (1.25 at
-    // first; 2.7 for YOLO26n). A call whose compute is faster than its upload (MobileNetV4: 0.8)
-    // takes the ramped schedule instead (pipeline_pieces). Once the session has joined a multi-GPU
+    // first; 2.7 for YOLO26n). A call whose compute per image, beyond each piece's fixed cost, is
+    // below its upload per image (MobileNetV4) takes the copy-bound schedule instead (equal pieces
+    // near the break-even size: pipeline_pieces, learn_pieces). Once the session has joined a multi-GPU
     // output gather the factor stays at its initial value on every rank (see pipeline_growth). At
     // most kMaxPieces; a small remainder joins the last piece. UNOQ_PIPE_GROWTH fixes the factor
-    // (below 1: the ramped schedule).
+    // (below 1: the copy-bound schedule).
     static const double fixed_growth = [] {
         const char *env = std::getenv("UNOQ_PIPE_GROWTH");
         const double g = env ? std::atof(env) : 0.0;
         return g > 0.0 && g <= 4.0 ? g : 0.0;
     }();
     const bool joined = gather_ && gather_->active();
-    const std::vector<uint32_t> sizes = pipeline_pieces(images, pipeline_growth(joined, pipe_growth_, fixed_growth));
+    const std::vector<uint32_t> sizes =
+        pipeline_pieces(images, pipeline_growth(joined, pipe_growth_, fixed_growth), joined ? PieceModel() : pipe_model_);
     const size_t ni = input_bytes(), no = k ? sizeof(UgDetectionRecord) * k : output_bytes();
     // one batch context per piece (slot p + 1): no arena is refilled within a call
     std::vector<BatchCtx *> ctx(sizes.size(), nullptr);
@@ -1014,9 +1016,12 @@ int Engine::run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint
     UQ_CUDA(cudaStreamWaitEvent(h2d_, ev0_, 0));
     UQ_CUDA(cudaStreamWaitEvent(d2h_, ev0_, 0));
     size_t off = 0;
-    // the upload and compute of the largest piece are timed (a middle piece of a ramped schedule,
-    // the last of a growing one): their ratio picks the next call's schedule
+    // the upload and compute of the largest piece are timed (one of the equal pieces of a
+    // copy-bound schedule, the last of a growing one), and the compute of the smallest: they pick
+    // the next call's schedule (learn_pieces)
     const size_t timed_piece = (size_t)(std::max_element(sizes.begin(), sizes.end()) - sizes.begin());
+    const size_t small_piece = (size_t)(std::min_element(sizes.begin(), sizes.end()) - sizes.begin());
+    const bool two_sizes = sizes[small_piece] < sizes[timed_piece];
     for (size_t piece = 0; piece < sizes.size(); piece++) {
         const int s = (int)(piece & 1);
         BatchCtx *B = ctx[piece];
@@ -1027,13 +1032,16 @@ int Engine::run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint
         UQ_CUDA(cudaEventRecord(pipe_ev_[0][s], h2d_));
         if (timed) UQ_CUDA(cudaEventRecord(pipe_t_[1], h2d_));
         UQ_CUDA(cudaStreamWaitEvent(stream_, pipe_ev_[0][s], 0));
+        const bool small = two_sizes && piece == small_piece;
         if (timed) UQ_CUDA(cudaEventRecord(pipe_t_[2], stream_));
+        if (small) UQ_CUDA(cudaEventRecord(pipe_t_[4], stream_));
         if ((rc = stage_in(*B, stream_))) return rc;
         if (cudaGraphLaunch(B->exec, stream_) != cudaSuccess) {
             set_error("graph launch failed");
             return 2001;
         }
         if (timed) UQ_CUDA(cudaEventRecord(pipe_t_[3], stream_));
+        if (small) UQ_CUDA(cudaEventRecord(pipe_t_[5], stream_));
         if (k && (rc = stage_out(*B, k, stream_))) return rc;
         if (gathering && (rc = gather_->enqueue(B->ptr[P_.h.output], n * no, no * images, off * no, stream_)))
             return rc;
@@ -1058,17 +1066,17 @@ int Engine::run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint
     UQ_CUDA(cudaEventElapsedTime(&last_ms_, ev0_, ev1_));
     last_images_ = images;
     last_ctx_ = ctx.back();
-    // Learn the schedule from this process's own timing only while the session has no output
-    // gather (pipeline_growth ignores it afterwards anyway): per-rank timings differ. Compute
-    // faster than upload takes the ramped schedule, else pieces grow by the ratio of compute to
-    // upload time. Entering the ramped schedule needs a 10% margin; staying needs none, because
-    // its middle pieces are smaller and so slower per image than the largest growing piece.
+    // Learn the schedule (learn_pieces) from this process's own timing only while the session has
+    // no output gather (pipeline_growth ignores it afterwards anyway): per-rank timings differ.
     if (sizes.size() > 1 && !joined) {
-        float up = 0.f, comp = 0.f;
+        float up = 0.f, comp = 0.f, comp_s = 0.f;
         if (cudaEventElapsedTime(&up, pipe_t_[0], pipe_t_[1]) == cudaSuccess &&
             cudaEventElapsedTime(&comp, pipe_t_[2], pipe_t_[3]) == cudaSuccess && up > 0.f && comp > 0.f) {
-            const float margin = pipe_growth_ < 1.0 ? 1.0f : 0.9f;
-            pipe_growth_ = comp < margin * up ? kRampedPieces : std::min(3.0, std::max(1.15, 1.1 * comp / up));
+            if (!two_sizes || cudaEventElapsedTime(&comp_s, pipe_t_[4], pipe_t_[5]) != cudaSuccess) comp_s = 0.f;
+            const PieceChoice next = learn_pieces(pipe_growth_, sizes[timed_piece], up, comp,
+                                                  two_sizes ? sizes[small_piece] : 0, comp_s);
+            pipe_growth_ = next.growth;
+            pipe_model_ = next.model;
         }
     }
     return device_status();

@@ -28,31 +28,66 @@ constexpr size_t kNoOffset = ~(size_t)0;
 //  * growth >= 1 (compute-bound calls): the first piece is 1/16 of the batch (64 to 256 images);
 //    each next one is `growth` times the previous; at most kMaxPieces; a remainder under half a
 //    piece joins the last one.
-//  * growth < 1 (kRampedPieces: copy-bound calls, compute per image below upload per image): middle
-//    pieces of about images / 8 (256 to 1024) between ramps of a quarter and a half of that size at
-//    both ends. The host-to-device copies run back to back either way; the ramps leave only a
-//    quarter piece's upload before the first compute and a quarter piece's compute after the
-//    last upload, where a growing schedule ends on its largest piece.
+//  * growth < 1 (kCopyBoundPieces: copy-bound calls, compute per image below upload per image): a
+//    first piece, then equal pieces (at most kMaxPieces in all). The host-to-device copies run
+//    back to back; a piece's compute keeps pace with the next upload only if the upload time it
+//    frees (upload minus compute per image, times its images) covers the per-piece fixed cost of
+//    a graph launch. On MobileNetV4 (0.28 ms per piece beside 1.93 against 2.73 us per image) that
+//    break-even is about 350 images: smaller pieces, such as a ramp down at the end of the batch,
+//    leave a backlog of compute after the last upload. With a timing model of the last call
+//    (learn_pieces) the first piece (64-256 images) and the number of pieces are those whose
+//    simulated end time is least; without one, kCopyBoundFirst images (a quarter of a smaller
+//    batch) and pieces of about kCopyBoundPiece.
 constexpr double kInitialPieceGrowth = 1.25;
-constexpr double kRampedPieces = 0.5;
+constexpr double kCopyBoundPieces = 0.5;
+constexpr uint32_t kCopyBoundFirst = 192, kCopyBoundPiece = 352;  // without a model
 constexpr size_t kMaxPieces = 16;
-inline std::vector<uint32_t> pipeline_pieces(uint32_t images, double growth) {
+// Per-piece timing of a pipelined call (ms): a graph takes fixed + slope * images, an upload
+// up * images. Valid when up > 0.
+struct PieceModel {
+    double fixed = 0.0, slope = 0.0, up = 0.0;
+};
+// First piece `f`, then `m` equal pieces of the rest.
+inline std::vector<uint32_t> first_then_equal(uint32_t images, uint32_t f, uint32_t m) {
+    std::vector<uint32_t> sizes{f};
+    const uint32_t rest = images - f;
+    for (uint32_t i = 0; i < m; i++) sizes.push_back(rest / m + (i < rest % m ? 1 : 0));
+    return sizes;
+}
+// End time of a schedule under the model: uploads back to back, each graph after its upload and
+// the previous graph.
+inline double pipeline_end(const std::vector<uint32_t> &sizes, const PieceModel &pm) {
+    double t_up = 0.0, t_c = 0.0;
+    for (uint32_t n : sizes) {
+        t_up += pm.up * n;
+        t_c = (t_c > t_up ? t_c : t_up) + pm.fixed + pm.slope * n;
+    }
+    return t_c;
+}
+inline std::vector<uint32_t> pipeline_pieces(uint32_t images, double growth, const PieceModel &pm = PieceModel()) {
     std::vector<uint32_t> sizes;
     if (growth < 1.0) {
-        uint32_t mid = images / 8 < 256 ? 256 : images / 8 > 1024 ? 1024 : images / 8;
-        const uint32_t q = mid / 4, h = mid / 2;
-        if (images >= 3 * mid) {
-            const uint32_t rest = images - 2 * (q + h);
-            uint32_t m = (rest + mid / 2) / mid;
-            if (m < 1) m = 1;
-            if (m > kMaxPieces - 4) m = (uint32_t)kMaxPieces - 4;
-            sizes = {q, h};
-            for (uint32_t i = 0; i < m; i++) sizes.push_back(rest / m + (i < rest % m ? 1 : 0));
-            sizes.push_back(h);
-            sizes.push_back(q);
-            return sizes;
+        if (pm.up > 0.0 && images >= 128) {
+            double best = 0.0;
+            for (uint32_t f : {64u, 96u, 128u, 192u, 256u}) {
+                if (2 * f > images) break;
+                for (uint32_t m = 1; m < kMaxPieces && m <= (images - f) / 32; m++) {
+                    std::vector<uint32_t> s = first_then_equal(images, f, m);
+                    const double e = pipeline_end(s, pm);
+                    if (sizes.empty() || e < best - 1e-9) best = e, sizes = std::move(s);
+                }
+            }
+            if (!sizes.empty()) return sizes;
         }
-        growth = kInitialPieceGrowth;  // too few images to ramp
+        const uint32_t f = images / 4 < kCopyBoundFirst ? images / 4 : kCopyBoundFirst;
+        if (f >= 64) {
+            const uint32_t rest = images - f;
+            uint32_t m = (rest + kCopyBoundPiece / 2) / kCopyBoundPiece;
+            if (m < 1) m = 1;
+            if (m > kMaxPieces - 1) m = (uint32_t)kMaxPieces - 1;
+            return first_then_equal(images, f, m);
+        }
+        growth = kInitialPieceGrowth;  // too few images to split
     }
     uint32_t left = images;
     double cur = images / 16.0 < 64.0 ? 64.0 : images / 16.0 > 256.0 ? 256.0 : images / 16.0;
@@ -65,7 +100,7 @@ inline std::vector<uint32_t> pipeline_pieces(uint32_t images, double growth) {
     }
     return sizes;
 }
-// The growth a call uses (below 1: the ramped schedule). `fixed` (UNOQ_PIPE_GROWTH, 0 when unset)
+// The growth a call uses (below 1: the copy-bound schedule). `fixed` (UNOQ_PIPE_GROWTH, 0 when unset)
 // wins. A session that has joined
 // an output gather always uses the initial factor: each piece enqueues one gather step, so every
 // rank must cut identical pieces, whatever it measured on calls made before joining or on
@@ -73,6 +108,38 @@ inline std::vector<uint32_t> pipeline_pieces(uint32_t images, double growth) {
 inline double pipeline_growth(bool gather_joined, double learned, double fixed) {
     if (fixed > 0) return fixed;
     return gather_joined ? kInitialPieceGrowth : learned;
+}
+
+// The next call's schedule, learned from two pieces of the last one: the largest (`n_l` images,
+// upload `up` ms, graph `comp` ms) and the smallest (`n_s` images, graph `comp_s` ms; n_s = 0 when
+// the pieces were all alike). A graph's time is a fixed cost per piece plus a cost per image, the
+// slope between the two pieces. Compute per image below upload per image (10% below to enter,
+// not above to stay) takes the copy-bound schedule, planned on that model (no model without a
+// slope). Otherwise pieces grow by 1.1 x the ratio of compute to upload time of the largest
+// piece, within [1.15, 3]. Judging by the largest piece alone would take a small batch's small
+// pieces, whose fixed cost inflates their compute, for compute-bound (MobileNetV4 at 512 and
+// 1,024 images).
+struct PieceChoice {
+    double growth;
+    PieceModel model;
+};
+inline PieceChoice learn_pieces(double prev_growth, uint32_t n_l, float up, float comp, uint32_t n_s, float comp_s) {
+    const double up1 = (double)up / n_l;
+    double slope = (double)comp / n_l, fixed = 0.0;
+    if (n_s > 0 && n_s < n_l && comp_s > 0.f) {
+        const double sl = ((double)comp - comp_s) / (double)(n_l - n_s);
+        if (sl > 0.0) {
+            slope = sl;
+            fixed = (double)comp - sl * n_l;
+            if (fixed < 0.0) fixed = 0.0;
+        }
+    }
+    const double margin = prev_growth < 1.0 ? 1.0 : 0.9;
+    PieceModel pm;
+    if (fixed > 0.0) pm.fixed = fixed, pm.slope = slope, pm.up = up1;
+    if (slope < margin * up1) return {kCopyBoundPieces, pm};
+    const double g = 1.1 * comp / up;
+    return {g < 1.15 ? 1.15 : g > 3.0 ? 3.0 : g, pm};
 }
 
 struct BatchCtx;
@@ -216,8 +283,9 @@ class Engine {
     cudaStream_t h2d_ = nullptr, d2h_ = nullptr;             // copy streams of the pipeline
     cudaEvent_t pipe_ev_[3][2] = {};                         // per slot: input landed, computed, output read
     cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
-    cudaEvent_t pipe_t_[4] = {};         // timing of the last piece: upload start / end, graph start / end
-    double pipe_growth_ = kInitialPieceGrowth;  // piece schedule from the last call: growth, or kRampedPieces
+    cudaEvent_t pipe_t_[6] = {};         // largest piece: upload start / end, graph start / end; smallest: graph start / end
+    double pipe_growth_ = kInitialPieceGrowth;  // piece schedule from the last call: growth, or kCopyBoundPieces
+    PieceModel pipe_model_;                     // timing model of the last call (copy-bound schedule)
     float last_ms_ = 0.f;
     uint32_t last_images_ = 0;
     const BatchCtx *last_ctx_ = nullptr; // context of the last run (a batch piece or the static arena)
