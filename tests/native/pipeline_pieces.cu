@@ -90,6 +90,28 @@ int main() {
         std::printf("MobileNetV4 model, %u images: planned %zu pieces (first %u, then %u) %.2f ms, rule %.2f ms, ramped %.2f ms, upload %.2f ms\n",
                     images, planned.size(), planned[0], planned[1], e_plan, e_rule, e_ramp, a.model.up * images);
     }
+    // planning on a YOLO26n-like model (compute-bound, outputs of 171 KB per image read back):
+    // growing pieces, ending sooner than the growth-factor rule the session would use otherwise
+    uq::PieceModel ym;
+    ym.fixed = 0.95, ym.slope = 8.16e-3, ym.up = 5.59e-3, ym.down = 3.11e-3;
+    for (unsigned images : {512u, 1024u, 2048u}) {
+        const auto planned = uq::pipeline_pieces(images, 1.93, ym);
+        unsigned sum = 0;
+        for (uint32_t n : planned) sum += n;
+        check(sum == images && planned.size() <= uq::kMaxPieces, "planned pieces cover the batch", images);
+        const double e_plan = uq::pipeline_end(planned, ym), e_rule = uq::pipeline_end(uq::pipeline_pieces(images, 1.93), ym);
+        check(e_plan <= e_rule, "planned compute-bound schedule ends no later", images);
+        std::printf("YOLO26n model, %u images: planned %zu pieces (first %u, last %u) %.2f ms, growth rule %.2f ms\n",
+                    images, planned.size(), planned.front(), planned.back(), e_plan, e_rule);
+    }
+    for (unsigned images : {128u, 1000u, 4096u})
+        for (double g : {1.2, 2.0, 3.2})
+            for (uint32_t tail : {0u, 64u}) {
+                const auto gp = uq::growing_pieces(images, 64, g, tail);
+                unsigned sum = 0;
+                for (uint32_t n : gp) sum += n;
+                check(gp.empty() || (sum == images && gp.size() <= uq::kMaxPieces), "growing pieces cover the batch", images);
+            }
     if (fails) return 1;
     std::printf("ok\n");
     return 0;

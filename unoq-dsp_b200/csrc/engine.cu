@@ -996,9 +996,19 @@ int Engine::run_pipelined(const uint8_t *in, uint8_t *out, uint32_t images, uint
         return g > 0.0 && g <= 4.0 ? g : 0.0;
     }();
     const bool joined = gather_ && gather_->active();
-    const std::vector<uint32_t> sizes =
-        pipeline_pieces(images, pipeline_growth(joined, pipe_growth_, fixed_growth), joined ? PieceModel() : pipe_model_);
     const size_t ni = input_bytes(), no = k ? sizeof(UgDetectionRecord) * k : output_bytes();
+    PieceModel model = joined || fixed_growth > 0.0 ? PieceModel() : pipe_model_;
+    model.down = model.up * (double)no / (double)ni;  // this call's outputs, over the same link
+    std::vector<uint32_t> sizes = pipeline_pieces(images, pipeline_growth(joined, pipe_growth_, fixed_growth), model);
+    // A planned schedule replaces this batch size's previous one only when the model predicts it
+    // ends 2% sooner: timing noise then does not switch schedules call after call, each switch
+    // capturing graphs and planning arenas for piece sizes not seen before.
+    if (model.up > 0.0) {
+        const auto prev = pipe_plan_.find(images);
+        if (prev != pipe_plan_.end() && pipeline_end(prev->second, model) <= 1.02 * pipeline_end(sizes, model))
+            sizes = prev->second;
+        pipe_plan_[images] = sizes;
+    }
     // one batch context per piece (slot p + 1): no arena is refilled within a call
     std::vector<BatchCtx *> ctx(sizes.size(), nullptr);
     int rc = 0;

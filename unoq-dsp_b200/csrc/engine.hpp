@@ -24,28 +24,30 @@ constexpr size_t kStaticArenaBytes = (size_t)16 << 20;  // fixed arena of run_st
 constexpr size_t kNoOffset = ~(size_t)0;
 
 // Piece schedule of a pipelined host batch (Engine::run_pipelined), host-only and pure so that
-// every rank of a gathered run can be shown to cut the same pieces.
+// every rank of a gathered run can be shown to cut the same pieces. With a timing model of the
+// session's last call (learn_pieces; never for a gathered session) the schedule is the one of
+// least simulated end time (planned_pieces). Without one:
 //  * growth >= 1 (compute-bound calls): the first piece is 1/16 of the batch (64 to 256 images);
 //    each next one is `growth` times the previous; at most kMaxPieces; a remainder under half a
 //    piece joins the last one.
 //  * growth < 1 (kCopyBoundPieces: copy-bound calls, compute per image below upload per image): a
-//    first piece, then equal pieces (at most kMaxPieces in all). The host-to-device copies run
-//    back to back; a piece's compute keeps pace with the next upload only if the upload time it
-//    frees (upload minus compute per image, times its images) covers the per-piece fixed cost of
-//    a graph launch. On MobileNetV4 (0.28 ms per piece beside 1.93 against 2.73 us per image) that
-//    break-even is about 350 images: smaller pieces, such as a ramp down at the end of the batch,
-//    leave a backlog of compute after the last upload. With a timing model of the last call
-//    (learn_pieces) the first piece (64-256 images) and the number of pieces are those whose
-//    simulated end time is least; without one, kCopyBoundFirst images (a quarter of a smaller
-//    batch) and pieces of about kCopyBoundPiece.
+//    first piece of kCopyBoundFirst images (a quarter of a smaller batch), then equal pieces of
+//    about kCopyBoundPiece (at most kMaxPieces in all).
+// Why equal pieces when copy-bound: the host-to-device copies run back to back, and a piece's
+// compute keeps pace with the next upload only if the upload time it frees (upload minus compute
+// per image, times its images) covers the per-piece fixed cost of a graph launch. On MobileNetV4
+// (0.28 ms per piece beside 1.93 against 2.73 us per image) that break-even is about 350 images:
+// smaller pieces, such as a ramp down at the end of the batch, leave a backlog of compute after
+// the last upload. When compute-bound (YOLO26n), pieces grow so that each upload hides under the
+// previous compute, and a small closing piece shortens the last read-back of large outputs.
 constexpr double kInitialPieceGrowth = 1.25;
 constexpr double kCopyBoundPieces = 0.5;
 constexpr uint32_t kCopyBoundFirst = 192, kCopyBoundPiece = 352;  // without a model
 constexpr size_t kMaxPieces = 16;
 // Per-piece timing of a pipelined call (ms): a graph takes fixed + slope * images, an upload
-// up * images. Valid when up > 0.
+// up * images and the read-back of its outputs down * images. Valid when up > 0.
 struct PieceModel {
-    double fixed = 0.0, slope = 0.0, up = 0.0;
+    double fixed = 0.0, slope = 0.0, up = 0.0, down = 0.0;
 };
 // First piece `f`, then `m` equal pieces of the rest.
 inline std::vector<uint32_t> first_then_equal(uint32_t images, uint32_t f, uint32_t m) {
@@ -54,31 +56,63 @@ inline std::vector<uint32_t> first_then_equal(uint32_t images, uint32_t f, uint3
     for (uint32_t i = 0; i < m; i++) sizes.push_back(rest / m + (i < rest % m ? 1 : 0));
     return sizes;
 }
+// Pieces from `f` images up, each `g` times the previous (a remainder under half a piece joins
+// the last), then a closing piece of `tail` images (0: none); empty when that takes more than
+// kMaxPieces.
+inline std::vector<uint32_t> growing_pieces(uint32_t images, uint32_t f, double g, uint32_t tail) {
+    std::vector<uint32_t> sizes;
+    if (f < 1 || tail >= images) return sizes;
+    uint32_t left = images - tail;
+    double cur = f;
+    while (left) {
+        uint32_t n = left < (uint32_t)cur ? left : (uint32_t)cur;
+        if (n < 1) n = 1;
+        if (left - n < (uint32_t)(cur * 0.5)) n = left;
+        sizes.push_back(n);
+        left -= n;
+        cur *= g;
+        if (sizes.size() > kMaxPieces) return {};
+    }
+    if (tail) sizes.push_back(tail);
+    if (sizes.size() > kMaxPieces) return {};
+    return sizes;
+}
 // End time of a schedule under the model: uploads back to back, each graph after its upload and
-// the previous graph.
+// the previous graph, each read-back after its graph and the previous read-back.
 inline double pipeline_end(const std::vector<uint32_t> &sizes, const PieceModel &pm) {
-    double t_up = 0.0, t_c = 0.0;
+    double t_up = 0.0, t_c = 0.0, t_d = 0.0;
     for (uint32_t n : sizes) {
         t_up += pm.up * n;
         t_c = (t_c > t_up ? t_c : t_up) + pm.fixed + pm.slope * n;
+        t_d = (t_d > t_c ? t_d : t_c) + pm.down * n;
     }
-    return t_c;
+    return t_d;
+}
+// The schedule of least simulated end time among a first piece then equal pieces, and growing
+// pieces with an optional small closing piece (which shortens the last read-back); empty when
+// the model is not valid or the batch is under 128 images.
+inline std::vector<uint32_t> planned_pieces(uint32_t images, const PieceModel &pm) {
+    std::vector<uint32_t> best_s;
+    if (!(pm.up > 0.0) || images < 128) return best_s;
+    double best = 0.0;
+    auto consider = [&](std::vector<uint32_t> s) {
+        if (s.empty()) return;
+        const double e = pipeline_end(s, pm);
+        if (best_s.empty() || e < best - 1e-9) best = e, best_s = std::move(s);
+    };
+    for (uint32_t f : {32u, 64u, 96u, 128u, 192u, 256u}) {
+        if (2 * f > images) break;
+        for (uint32_t m = 1; m < kMaxPieces && m <= (images - f) / 32; m++) consider(first_then_equal(images, f, m));
+        for (double g : {1.2, 1.4, 1.6, 1.8, 2.0, 2.4, 2.8, 3.2})
+            for (uint32_t tail : {0u, 32u, 64u, 128u})
+                if (tail * 4 <= images) consider(growing_pieces(images, f, g, tail));
+    }
+    return best_s;
 }
 inline std::vector<uint32_t> pipeline_pieces(uint32_t images, double growth, const PieceModel &pm = PieceModel()) {
-    std::vector<uint32_t> sizes;
+    std::vector<uint32_t> sizes = planned_pieces(images, pm);
+    if (!sizes.empty()) return sizes;
     if (growth < 1.0) {
-        if (pm.up > 0.0 && images >= 128) {
-            double best = 0.0;
-            for (uint32_t f : {64u, 96u, 128u, 192u, 256u}) {
-                if (2 * f > images) break;
-                for (uint32_t m = 1; m < kMaxPieces && m <= (images - f) / 32; m++) {
-                    std::vector<uint32_t> s = first_then_equal(images, f, m);
-                    const double e = pipeline_end(s, pm);
-                    if (sizes.empty() || e < best - 1e-9) best = e, sizes = std::move(s);
-                }
-            }
-            if (!sizes.empty()) return sizes;
-        }
         const uint32_t f = images / 4 < kCopyBoundFirst ? images / 4 : kCopyBoundFirst;
         if (f >= 64) {
             const uint32_t rest = images - f;
@@ -285,7 +319,8 @@ class Engine {
     cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
     cudaEvent_t pipe_t_[6] = {};         // largest piece: upload start / end, graph start / end; smallest: graph start / end
     double pipe_growth_ = kInitialPieceGrowth;  // piece schedule from the last call: growth, or kCopyBoundPieces
-    PieceModel pipe_model_;                     // timing model of the last call (copy-bound schedule)
+    PieceModel pipe_model_;                     // timing model of the last call (planned schedules)
+    std::map<uint32_t, std::vector<uint32_t>> pipe_plan_;  // last planned schedule per batch size
     float last_ms_ = 0.f;
     uint32_t last_images_ = 0;
     const BatchCtx *last_ctx_ = nullptr; // context of the last run (a batch piece or the static arena)
