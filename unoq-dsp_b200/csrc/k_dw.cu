@@ -55,8 +55,9 @@ __device__ __forceinline__ void transpose4(uint32_t x0, uint32_t x1, uint32_t x2
     y[3] = __byte_perm(b, d, 0x7632);
 }
 
+// Exact requantisation before the clamp (the forms of requant.cuh's EpiChan).
 template <int EPI>
-__device__ __forceinline__ int32_t requant(int32_t acc, const EpiChan &e, int lo, int hi) {
+__device__ __forceinline__ int32_t requant_raw(int32_t acc, const EpiChan &e) {
     int32_t v;
     if (EPI == 2) {
         const int32_t a = (int32_t)(((uint32_t)acc << e.ls) + (uint32_t)e.bs);
@@ -68,7 +69,18 @@ __device__ __forceinline__ int32_t requant(int32_t acc, const EpiChan &e, int lo
         if (EPI == 1) p -= (long long)(acc <= e.cut) << 31;
         v = ((int32_t)(p >> 32)) >> e.sh;
     }
+    return v;
+}
+template <int EPI>
+__device__ __forceinline__ int32_t requant(int32_t acc, const EpiChan &e, int lo, int hi) {
+    const int32_t v = requant_raw<EPI>(acc, e);
     return v < lo ? lo : (v > hi ? hi : v);
+}
+// Clamp to [-128, 127] in one saturating conversion.
+__device__ __forceinline__ int32_t sat_s8(int32_t v) {
+    int32_t r;
+    asm("cvt.sat.s8.s32 %0, %1;" : "=r"(r) : "r"(v));
+    return r;
 }
 
 // Blocks per SM the compiler must fit in registers: with 2 output rows per thread, 4 for 3x3
@@ -173,14 +185,22 @@ __global__ void __launch_bounds__(512, kR == 4 ? 2 : ((K == 3 && S == 1) ? 4 : 3
         }
     }
     const uint8_t *lut = p.post ? sLut : nullptr;
+    if (!lut && p.lo == -128 && p.hi == 127) {  // the clamp is the int8 range: one saturating step
 #pragma unroll
-    for (int r = 0; r < kR; r++)
+        for (int r = 0; r < kR; r++)
 #pragma unroll
-        for (int j = 0; j < TW; j++) {
-            int32_t v = requant<EPI>(acc[r][j], e, p.lo, p.hi);
-            if (lut) v = (int8_t)lut[v + 128];
-            sOut[((size_t)(rg * kR + r) * TW + j) * cb + ch] = (uint8_t)v;
-        }
+            for (int j = 0; j < TW; j++)
+                sOut[((size_t)(rg * kR + r) * TW + j) * cb + ch] = (uint8_t)sat_s8(requant_raw<EPI>(acc[r][j], e));
+    } else {
+#pragma unroll
+        for (int r = 0; r < kR; r++)
+#pragma unroll
+            for (int j = 0; j < TW; j++) {
+                int32_t v = requant<EPI>(acc[r][j], e, p.lo, p.hi);
+                if (lut) v = (int8_t)lut[v + 128];
+                sOut[((size_t)(rg * kR + r) * TW + j) * cb + ch] = (uint8_t)v;
+            }
+    }
     __syncthreads();
     // ---- copy-out: 16 channels of one pixel per store
     const int units = th * TW * (cb / 16);
